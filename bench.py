@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark of the routed-expert MoE hot path on B200.
+
+Workload (the fused dequant+GEMV microbench): one stack of
+8 experts, each gate/up [14336 x 4096] and down [4096 x 14336] in GGUF Q4_K
+(or Q8_0 with --type q8_0), seeded Gaussian weights N(0, 0.02) encoded on the
+device; x = T bf16 tokens N(0, 1) (T = 8 by default, the top of the 1..8
+range).  One step = one MoE block over the whole stack: router (softmax,
+top-8 of 8), grouping, fused gate/up GEMV + SwiGLU, down GEMV, weighted combine
+-- every expert's rows are streamed from HBM once.  The 792.7 MB Q4_K stack is
+far larger than the 126 MB L2, so no flush is needed between steps.
+
+metric/value: algorithmic HBM bytes of the step (stack bytes + x + y) / step
+time, whole job over all ranks (weak scaling: every rank owns its own stack,
+an expert-parallel partition with no data-path exchange for this workload).
+e2e: the same metric through the C ABI with host buffers: pinned H2D of x and
+the router logits and D2H of y inside every timed step.
+
+--impl reference: the reference's own CPU code for the same step (its
+gemv_quant and silu in the engine's per-token expert loop, compiled from
+source into oracle/_ref; the C restatement if that is absent), on all host
+cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s + fused dequant-GEMV HBM GB/s (% of 8 TB/s), 1–8 B200"
+D_MODEL, FFN, EXPERTS = 4096, 14336, 8
+TYPES = {"q4_k": 12, "q8_0": 8}
+
+
+def row_bytes(t, n):
+    return n // 256 * 144 if t == 12 else n // 32 * 34
+
+
+def expert_bytes(t):
+    return 2 * FFN * row_bytes(t, D_MODEL) + D_MODEL * row_bytes(t, FFN)
+
+
+def step_bytes(t, tokens):
+    # weights streamed once + bf16 x read + f32 y written
+    return EXPERTS * expert_bytes(t) + tokens * D_MODEL * 2 + tokens * D_MODEL * 4
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.lines, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_step_reference(ref, type_id, host_slots, x, logits, tokens, threads):
+    """One reference step on the CPU: router + per-token expert loop (engine.cpp:1603-1772)."""
+    rc, ids, w, _ = ref.route(logits, EXPERTS)
+    if rc:
+        raise RuntimeError(f"reference router failed: {rc}")
+    gb = FFN * row_bytes(type_id, D_MODEL)
+    return ref.moe_block(type_id, host_slots, gb, 2 * gb, x, ids, w, D_MODEL, FFN, threads=threads)
+
+
+def make_cpu_runner(type_id, host_slots):
+    """The reference's own code when it was compiled here, else the C restatement."""
+    from oracle.oracle import Oracle, Reference, reference_available
+
+    if reference_available():
+        ref = Reference()
+        return "reference", lambda x, lg, T, th: cpu_step_reference(ref, type_id, host_slots, x, lg, T, th)
+    orc = Oracle()
+
+    def port(x, lg, T, th):
+        rc, ids, w, _ = orc.route(lg, EXPERTS)
+        return orc.moe_block(x, ids, w, host_slots, D_MODEL, FFN, type_id)
+    return "port", port
+
+
+def host_inputs(tokens, seed=0):
+    import numpy as np
+    from oracle.oracle import bf16_round
+
+    rng = np.random.default_rng(seed)
+    x = bf16_round(rng.normal(0, 1, size=(tokens, D_MODEL)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(tokens, EXPERTS)).astype(np.float32)
+    return x, logits
+
+
+def synth_host_slots(type_id, seed):
+    """Expert payloads on the host: the device encoder when a GPU is present
+    (identical bytes to the GPU arm), else the C restatement's encoder."""
+    import numpy as np
+
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            from freemoe_b200 import hotpath
+
+            hotpath.init(0)
+            out = []
+            for e in range(EXPERTS):
+                parts = [hotpath.synth_weights(type_id, rows, cols, seed=seed * 1000 + 3 * e + j)
+                         for j, (rows, cols) in enumerate(((FFN, D_MODEL), (FFN, D_MODEL), (D_MODEL, FFN)))]
+                out.append(torch.cat(parts).cpu().numpy())
+            return out
+    except Exception:  # noqa: BLE001 - no usable GPU: fall back to the host encoder
+        pass
+    from oracle.oracle import Oracle
+
+    orc = Oracle()
+    rng = np.random.default_rng(seed)
+    return [np.concatenate([orc.quantize(type_id, rng.normal(0, 0.02, n).astype(np.float32))
+                            for n in (FFN * D_MODEL, FFN * D_MODEL, D_MODEL * FFN)]) for _ in range(EXPERTS)]
+
+
+def run_reference(args):
+    world, rank, local = dist_setup(args)
+    if rank != 0:
+        return
+    type_id = TYPES[args.type]
+    threads = os.cpu_count() or 1
+    host_slots = synth_host_slots(type_id, seed=1)
+    kind, runner = make_cpu_runner(type_id, host_slots)
+    x, logits = host_inputs(args.tokens)
+    for _ in range(args.warmup):
+        runner(x, logits, args.tokens, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        runner(x, logits, args.tokens, threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = step_bytes(type_id, args.tokens) / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": args.type, "data": "synthetic",
+        "config": {"workload": f"{args.type} 8-expert stack [{FFN}x{D_MODEL}]x2+[{D_MODEL}x{FFN}], "
+                               f"T={args.tokens} bf16 tokens, top-8 of 8", "tokens": args.tokens,
+                   "l2": "inputs larger than L2"},
+        "tokens_per_s": args.tokens / dt,
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"the full step ({EXPERTS} experts x {args.tokens} tokens) per step"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200._lib import MOE_STAGES, check, load
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    hotpath.init(local)
+    type_id = TYPES[args.type]
+    T = args.tokens
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+
+    # expert slots: one 256-aligned HBM slab per expert holding gate || up || down
+    eb = expert_bytes(type_id)
+    gb = FFN * row_bytes(type_id, D_MODEL)
+    slots = []
+    for e in range(EXPERTS):
+        slab = torch.empty(eb, dtype=torch.uint8, device=dev)
+        off = 0
+        for j, (rows, cols) in enumerate(((FFN, D_MODEL), (FFN, D_MODEL), (D_MODEL, FFN))):
+            n = rows * row_bytes(type_id, cols)
+            check(load().fmcuda_synth_weights(type_id, C.c_void_p(slab.data_ptr() + off), rows, cols,
+                                              1000 * (rank + 1) + 3 * e + j, 0.02, stream.cuda_stream))
+            off += n
+        slots.append(slab)
+    table = hotpath.slot_table(slots, dev)
+    x_np, lg_np = host_inputs(T, seed=rank)
+    x = torch.from_numpy(x_np).to(dev).to(torch.bfloat16)
+    logits = torch.from_numpy(lg_np).to(dev)
+    y = torch.empty(T, D_MODEL, dtype=torch.float32, device=dev)
+    ws = torch.empty(hotpath.moe_workspace_bytes(T, EXPERTS, EXPERTS, D_MODEL, FFN), dtype=torch.uint8,
+                     device=dev)
+    n_ev = len(MOE_STAGES) + 1
+    ev_pool = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
+    ev_arrays = [(C.c_void_p * n_ev)(*[e.cuda_event for e in evs]) for evs in ev_pool]
+    for evs in ev_pool:
+        for e in evs:
+            e.record(stream)  # materialise the events before their handles are used
+    lib = load()
+    ws_ptr, ws_n, sptr = C.c_void_p(ws.data_ptr()), ws.numel(), stream.cuda_stream
+
+    arg_cache = {}
+
+    def call(xt, lgt, yt, events=None):
+        key = (xt.data_ptr(), lgt.data_ptr(), yt.data_ptr())
+        a = arg_cache.get(key)
+        if a is None:
+            a = hotpath.moe_args(xt, lgt, table, experts=EXPERTS, top_k=EXPERTS, d_model=D_MODEL, ffn=FFN,
+                                 gate_type=type_id, up_type=type_id, down_type=type_id, up_offset=gb,
+                                 down_offset=2 * gb, y=yt)
+            arg_cache[key] = a
+        a.stage_events = C.cast(events, C.c_void_p) if events is not None else None
+        check(lib.fmcuda_moe_block(C.byref(a), ws_ptr, ws_n, sptr))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # correctness guard on a slice: the step's routing must be every expert
+    for _ in range(args.warmup):
+        call(x, logits, y)
+    barrier()
+    assert hotpath.device_status() == 0
+
+    # ---- device-resident timing (value) -------------------------------------
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record(stream)
+        for i in range(args.steps):
+            call(x, logits, y, ev_arrays[i])
+        end.record(stream)
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    stage_ms = {s: statistics.mean(ev_pool[i][j].elapsed_time(ev_pool[i][j + 1]) for i in range(args.steps))
+                for j, s in enumerate(MOE_STAGES)}
+
+    # ---- end to end through the C ABI with host buffers ----------------------
+    hx = torch.from_numpy(x_np).to(torch.bfloat16).pin_memory()
+    hl = torch.from_numpy(lg_np).pin_memory()
+    hy = torch.empty(T, D_MODEL, dtype=torch.float32).pin_memory()
+    dx = torch.empty_like(x)
+    dl = torch.empty_like(logits)
+    h2d = hx.numel() * 2 + hl.numel() * 4
+    d2h = hy.numel() * 4
+    for _ in range(2):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        call(dx, dl, y)
+        hy.copy_(y, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        call(dx, dl, y)
+        hy.copy_(y, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    assert np.isfinite(hy.numpy()).all()
+    assert hotpath.device_status() == 0
+
+    # ---- max over ranks --------------------------------------------------------
+    vals = torch.tensor([ms, ms_e2e, stage_ms["gate_up"], stage_ms["down"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, ms_e2e, gu_ms, dn_ms = vals.tolist()
+    nbytes = step_bytes(type_id, T)
+    value = world * nbytes / (ms / 1e3) / 1e9
+    e2e = world * nbytes / (ms_e2e / 1e3) / 1e9
+
+    peak, peak_kind = load_peaks()
+    # dominant kernel: the fused gate/up GEMV + SwiGLU over the 8 experts
+    gu_bytes = EXPERTS * 2 * FFN * row_bytes(type_id, D_MODEL) + T * D_MODEL * 2 + EXPERTS * T * FFN * 4
+    gu_achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(f"gate_up_{args.type}_T{T}")
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": args.type, "data": "synthetic",
+        "config": {"workload": f"{args.type} 8-expert stack [{FFN}x{D_MODEL}]x2+[{D_MODEL}x{FFN}], "
+                               f"T={T} bf16 tokens, top-8 of 8 (fmcuda_moe_block)", "tokens": T,
+                   "parallelism": f"ep{world} (replicated stack per rank, no exchange)",
+                   "l2": "inputs larger than L2 (792.7 MB Q4_K stack vs 126 MB L2)"},
+        "tokens_per_s": world * T / (ms / 1e3),
+        "pct_of_8tbs": value / world / 8000.0 * 100.0,
+        "stage_ms": stage_ms,
+        "roofline": {"bound": "hbm", "kernel": "qgemv gate/up + SwiGLU (8 experts)", "achieved": gu_achieved,
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": gu_achieved / peak,
+                     "traffic": traffic, "algorithmic_bytes": gu_bytes,
+                     "down_achieved": (EXPERTS * D_MODEL * row_bytes(type_id, FFN)) / (dn_ms / 1e3) / 1e9},
+        "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": ms_e2e},
+        "gpu_launches": 7 * args.steps,
+        "clocks": clocks.summary(),
+    }
+
+    # ---- CPU baseline (rank 0, N = 1): bounded sample on the host cores -------
+    if rank == 0 and world == 1 and not args.no_cpu:
+        host_slots = [s.cpu().numpy() for s in slots]
+        kind, runner = make_cpu_runner(type_id, host_slots)
+        threads = os.cpu_count() or 1
+        runner(x_np, lg_np, T, threads)
+        n, t0 = 0, time.perf_counter()
+        while n < 3 or (time.perf_counter() - t0 < 10.0 and n < 50):
+            runner(x_np, lg_np, T, threads)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        line["cpu_baseline"] = {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+                                "sample": f"{n} full steps ({EXPERTS} experts x {T} tokens), "
+                                          f"{dt * 1e3:.1f} ms each"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))
+    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

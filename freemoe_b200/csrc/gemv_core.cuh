@@ -1,0 +1,262 @@
+// gemv_core.cuh -- fused dequant + tensor-core GEMV tiles for GGUF Q4_K / Q8_0.
+//
+// Replaces the per-row CPU kernels row_dot_q4_k_avx2 / row_dot_q8_0_avx2
+// (src/kernels.cpp:720-771, :639-653) and the fused scalar path (:574-590).
+//
+// Data flow per warp: a tile of 16*MT weight rows x 8 tokens, over the
+// quantisation blocks of the warp's K slice.  Weights stay in their stored
+// GGUF bytes (the residency slot holds the file's bytes, checksummed); the
+// codes are unpacked in registers straight into mma.sync m16n8k16 A
+// fragments, and x comes from "x planes" prepared once per call:
+//
+//   xh   fp16 copy of x, each group of 4 stored as (x0, x2, x1, x3) so that a
+//        thread's 8-byte load is exactly its B fragment (the k order inside a
+//        fragment is free as long as A and B use the same one);
+//   xl   fp16 residual x - xh (only for f32 inputs: x = xh + xl to 2^-22);
+//   xs   f32 sums of x over each 32-value sub-block.
+//
+// Exactness of the unpacking:
+//   Q4_K  (0x6400 | q) is the fp16 value 1024 + q.  One HFMA2 with
+//         (sc, -1024 sc) turns it into sc*q exactly (sc*q <= 945), so the
+//         sub-block scale is applied before the MMA and one accumulator spans
+//         the whole 256-value block; high nibbles are masked in place
+//         (1024 + 16 q) and use (sc/16, -64 sc).  The mins enter through one
+//         more MMA of the 6-bit mins against the sub-block sums (split into
+//         two fp16 planes).  Per block: y += d * acc - dmin * acc_min, the
+//         same algebra as row_dot_q4_k_avx2 (src/kernels.cpp:759-762).
+//   Q8_0  (q ^ 0x80) gives 1152 + q in fp16 via PRMT with 0x64; per block
+//         y += d * acc - 1152 d * X.
+// All products are exact in the tensor core's fp32 accumulation; the result
+// differs from the reference only by summation order.
+#pragma once
+
+#include "common.cuh"
+
+namespace fmb {
+
+// ---- PTX wrappers ---------------------------------------------------------
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+    return (a & mask) | orv;
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u16(const void *p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ float half_lo_f(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
+}
+__device__ __forceinline__ float half_hi_f(uint32_t v) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+}
+
+// (1024 + v_lo, 1024 + v_hi) for the bytes 0 and 1 of `v` -> exact (v_lo, v_hi).
+__device__ __forceinline__ uint32_t bytes01_to_half2(uint32_t v) {
+    return hsub2_u32(prmt(v, 0x64646464u, 0x4140u), 0x64006400u);
+}
+
+// ---- x planes -------------------------------------------------------------
+
+// Position of logical element k inside its group of 4 in the xh/xl planes.
+__host__ __device__ __forceinline__ uint32_t xplane_pos(uint32_t k) {
+    const uint32_t r = k & 3u;
+    return (k & ~3u) | (r == 1u ? 2u : r == 2u ? 1u : r);
+}
+
+// One thread per 32-value sub-block of one row of x: writes the permuted fp16
+// plane(s) and the sub-block sum.  `row_of` maps plane rows to source rows
+// (NULL = identity).
+template <typename XT>
+__global__ void xplanes_kernel(const XT *__restrict__ x, uint32_t rows, uint32_t k_dim,
+                               __half *__restrict__ xh, __half *__restrict__ xl,
+                               float *__restrict__ xs) {
+    const uint32_t subs = k_dim / 32;
+    const uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (id >= static_cast<uint64_t>(rows) * subs) return;
+    const uint32_t row = static_cast<uint32_t>(id / subs), s = static_cast<uint32_t>(id % subs);
+    const XT *src = x + static_cast<uint64_t>(row) * k_dim + 32 * s;
+    __half *dh = xh + static_cast<uint64_t>(row) * k_dim + 32 * s;
+    float sum = 0.0f;
+    __align__(16) __half hv[32];
+    __align__(16) __half lv[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float v = load_x<XT>(src + i);
+        sum += v;
+        const __half h = __float2half_rn(v);
+        hv[xplane_pos(i)] = h;
+        lv[xplane_pos(i)] = __float2half_rn(v - __half2float(h));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<uint4 *>(dh)[i] = reinterpret_cast<uint4 *>(hv)[i];
+    if (xl) {
+        __half *dl = xl + static_cast<uint64_t>(row) * k_dim + 32 * s;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4 *>(dl)[i] = reinterpret_cast<uint4 *>(lv)[i];
+    }
+    xs[static_cast<uint64_t>(row) * subs + s] = sum;
+}
+
+// ---- tile job description -------------------------------------------------
+
+// Which weight rows, which x rows and where the outputs go for one CTA.
+struct QTile {
+    const uint8_t *w[2];   // up to two matrices over the same rows (gate, up)
+    uint32_t row0;         // first output row of the tile
+    uint32_t out_dim;
+    uint32_t in_dim;
+    uint64_t row_bytes;
+    uint32_t ncol;         // valid token columns (<= 8)
+    uint32_t xrow[8];      // x plane row of each column
+    uint32_t orow[8];      // output row of each column
+};
+
+// ---- Q4_K -----------------------------------------------------------------
+
+struct Q4kRowConsts {
+    uint32_t hs_lo, hb_lo, hs_hi, hb_hi; // half2 (sc, -1024 sc), (sc/16, -64 sc)
+    uint32_t mins;                       // half2 (m_2c, m_2c+1)
+    float d, dmin;
+};
+
+__device__ __forceinline__ Q4kRowConsts q4k_row_consts(const uint4 &h, int c) {
+    Q4kRowConsts r;
+    r.d = half_lo_f(h.x);
+    r.dmin = half_hi_f(h.x);
+    const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
+    // All sixteen 6-bit values, one per byte (src/quant.cpp:63-71).
+    const uint32_t sc03 = s0 & 0x3F3F3F3Fu;
+    const uint32_t m03 = s1 & 0x3F3F3F3Fu;
+    const uint32_t sc47 = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+    const uint32_t m47 = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+    const uint32_t shift = 16u * (c & 1);
+    const uint32_t scw = ((c < 2) ? sc03 : sc47) >> shift; // bytes: sc_2c, sc_2c+1
+    const uint32_t mw = ((c < 2) ? m03 : m47) >> shift;
+    const uint32_t sc_pair = bytes01_to_half2(scw);            // (sc_lo, sc_hi)
+    r.mins = bytes01_to_half2(mw);                             // (m_lo, m_hi)
+    const uint32_t sc_lo2 = prmt(sc_pair, 0, 0x1010u);         // (sc_lo, sc_lo)
+    const uint32_t sc_hi2 = prmt(sc_pair, 0, 0x3232u);         // (sc_hi, sc_hi)
+    r.hs_lo = sc_lo2;
+    r.hb_lo = hmul2_u32(sc_lo2, 0xE400E400u);                  // * -1024
+    r.hs_hi = hmul2_u32(sc_hi2, 0x2C002C00u);                  // * 1/16
+    r.hb_hi = hmul2_u32(sc_hi2, 0xD400D400u);                  // * -64
+    return r;
+}
+
+// One m-tile (rows g and g+8 of the tile) over one Q4_K block.
+// xb: the thread's 32 B-fragment registers of x plane(s) for this block.
+template <int PLANES>
+__device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1,
+                                                const uint4 (&q0)[2], const uint4 (&q1)[2], int c,
+                                                const uint32_t (&xb)[PLANES][32],
+                                                const uint32_t (&xm)[2], float (&tot)[4]) {
+    const Q4kRowConsts r0 = q4k_row_consts(h0, c);
+    const Q4kRowConsts r1 = q4k_row_consts(h1, c);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t w0[8] = {q0[0].x, q0[0].y, q0[0].z, q0[0].w, q0[1].x, q0[1].y, q0[1].z, q0[1].w};
+    const uint32_t w1[8] = {q1[0].x, q1[0].y, q1[0].z, q1[0].w, q1[1].x, q1[1].y, q1[1].z, q1[1].w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t s0 = w0[i] >> 8, s1 = w1[i] >> 8;
+        // low nibbles: sub-block 2c
+        const uint32_t a0 = hfma2_u32(lop_and_or(w0[i], 0x000F000Fu, 0x64006400u), r0.hs_lo, r0.hb_lo);
+        const uint32_t a1 = hfma2_u32(lop_and_or(w1[i], 0x000F000Fu, 0x64006400u), r1.hs_lo, r1.hb_lo);
+        const uint32_t a2 = hfma2_u32(lop_and_or(s0, 0x000F000Fu, 0x64006400u), r0.hs_lo, r0.hb_lo);
+        const uint32_t a3 = hfma2_u32(lop_and_or(s1, 0x000F000Fu, 0x64006400u), r1.hs_lo, r1.hb_lo);
+#pragma unroll
+        for (int p = 0; p < PLANES; ++p) mma_f16(acc, a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
+        // high nibbles: sub-block 2c+1
+        const uint32_t e0 = hfma2_u32(lop_and_or(w0[i], 0x00F000F0u, 0x64006400u), r0.hs_hi, r0.hb_hi);
+        const uint32_t e1 = hfma2_u32(lop_and_or(w1[i], 0x00F000F0u, 0x64006400u), r1.hs_hi, r1.hb_hi);
+        const uint32_t e2 = hfma2_u32(lop_and_or(s0, 0x00F000F0u, 0x64006400u), r0.hs_hi, r0.hb_hi);
+        const uint32_t e3 = hfma2_u32(lop_and_or(s1, 0x00F000F0u, 0x64006400u), r1.hs_hi, r1.hb_hi);
+#pragma unroll
+        for (int p = 0; p < PLANES; ++p)
+            mma_f16(acc, e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);
+    }
+    float accm[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_f16(accm, r0.mins, r1.mins, 0u, 0u, xm[0], 0u);
+    mma_f16(accm, r0.mins, r1.mins, 0u, 0u, xm[1], 0u);
+    tot[0] = fmaf(r0.d, acc[0], fmaf(-r0.dmin, accm[0], tot[0]));
+    tot[1] = fmaf(r0.d, acc[1], fmaf(-r0.dmin, accm[1], tot[1]));
+    tot[2] = fmaf(r1.d, acc[2], fmaf(-r1.dmin, accm[2], tot[2]));
+    tot[3] = fmaf(r1.d, acc[3], fmaf(-r1.dmin, accm[3], tot[3]));
+}
+
+// ---- Q8_0 -----------------------------------------------------------------
+
+// Loads the thread's 8 codes (bytes 8c..8c+7 of the block's qs) of one row.
+__device__ __forceinline__ void q8_load(const uint8_t *row, uint32_t blk, int c, uint32_t &wa,
+                                        uint32_t &wb, uint32_t &dbits) {
+    const uint8_t *s = row + 34ull * blk;
+    dbits = ldg_nc_u16(s);
+    if ((blk & 1u) == 0u) {
+        // block start is 4-byte aligned: codes start 2 bytes into a word
+        const uint32_t W0 = ldg_nc_u32(s + 8 * c);
+        const uint32_t W1 = ldg_nc_u32(s + 8 * c + 4);
+        const uint32_t W2 = ldg_nc_u32(s + 8 * c + 8);
+        wa = __funnelshift_r(W0, W1, 16);
+        wb = __funnelshift_r(W1, W2, 16);
+    } else {
+        wa = ldg_nc_u32(s + 2 + 8 * c);
+        wb = ldg_nc_u32(s + 6 + 8 * c);
+    }
+}
+
+} // namespace fmb

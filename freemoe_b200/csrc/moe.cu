@@ -1,0 +1,223 @@
+// moe.cu -- one routed-expert MoE block on the device (src/engine.cpp:1603-1772).
+//
+// Launch sequence on one stream (no host synchronisation):
+//   1. router        logits -> ids, weights                (router.cu)
+//   2. grouping      ids -> counts, offsets, pairs, slot_of (router.cu)
+//   3. x planes      x -> fp16 plane(s) + sub-block sums    (gemv_core.cuh)
+//   4. gate/up       per expert, fused gate and up GEMV with SwiGLU -> act[slot]
+//   5. act planes    act -> fp16 planes + sums
+//   6. down          per expert, down GEMV -> part[slot]
+//   7. combine       y[t] = sum over r of w[t,r] * part[slot_of(t,r)], in top-k
+//                    order, multiply then add (src/engine.cpp:1770)
+// Each expert's weight rows are read once per 8 of its tokens.
+#include <string>
+
+#include "gemv_kernels.cuh"
+
+namespace fmb {
+
+int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                 int32_t normalise, double epsilon, double scale, uint32_t *ids, float *weights,
+                 float *probs, cudaStream_t s);
+int launch_group(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
+                 uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, cudaStream_t s);
+int check_route_args(uint32_t experts, uint32_t top_k);
+int launch_xplanes(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, __half *xh,
+                   __half *xl, float *xs, cudaStream_t s);
+template <int MODE>
+int launch_qgemv(const QGemvParams &prm, int planes, uint32_t grid_y, uint32_t grid_z,
+                 cudaStream_t s);
+int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what);
+
+namespace {
+
+inline uint64_t a256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+// Byte layout of the MoE workspace.
+struct MoeLayout {
+    uint64_t ids, weights, counts, offsets, pairs, slot_of;
+    uint64_t xh, xl, xs;
+    uint64_t act, ah, al, as;
+    uint64_t part;
+    uint64_t total;
+};
+
+MoeLayout moe_layout(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t d,
+                     uint32_t ffn) {
+    MoeLayout L{};
+    const uint64_t P = static_cast<uint64_t>(tokens) * top_k;
+    uint64_t o = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t at = o;
+        o += a256(bytes);
+        return at;
+    };
+    L.ids = take(P * 4);
+    L.weights = take(P * 4);
+    L.counts = take(static_cast<uint64_t>(experts) * 4);
+    L.offsets = take((static_cast<uint64_t>(experts) + 1) * 4);
+    L.pairs = take(P * 4);
+    L.slot_of = take(P * 4);
+    L.xh = take(static_cast<uint64_t>(tokens) * d * 2);
+    L.xl = take(static_cast<uint64_t>(tokens) * d * 2);
+    L.xs = take(static_cast<uint64_t>(tokens) * (d / 32) * 4);
+    L.act = take(P * ffn * 4);
+    L.ah = take(P * ffn * 2);
+    L.al = take(P * ffn * 2);
+    L.as = take(P * (ffn / 32) * 4);
+    L.part = take(P * d * 4);
+    L.total = o;
+    return L;
+}
+
+__global__ void combine_kernel(const float *__restrict__ part, const float *__restrict__ weights,
+                               const uint32_t *__restrict__ slot_of, uint32_t tokens,
+                               uint32_t top_k, uint32_t d, float *__restrict__ y) {
+    const uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (id >= static_cast<uint64_t>(tokens) * d) return;
+    const uint32_t t = static_cast<uint32_t>(id / d), j = static_cast<uint32_t>(id % d);
+    float acc = 0.0f;
+    for (uint32_t r = 0; r < top_k; ++r) {
+        const uint32_t slot = slot_of[static_cast<uint64_t>(t) * top_k + r];
+        if (slot == 0xFFFFFFFFu) continue;
+        acc = __fadd_rn(acc, __fmul_rn(weights[static_cast<uint64_t>(t) * top_k + r],
+                                       part[static_cast<uint64_t>(slot) * d + j]));
+    }
+    y[id] = acc;
+}
+
+} // namespace
+
+// Shared by the allocating entry point and any variant that brings its own scratch.
+int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_bytes,
+                  cudaStream_t s) {
+    if (!a) return set_error(FM_STATUS_INVALID_ARGUMENT, "null MoE arguments");
+    if (a->tokens == 0) return FM_STATUS_OK;
+    int rc = check_route_args(a->experts, a->top_k);
+    if (rc) return rc;
+    if (!a->x || !a->logits || !a->expert_slots || !a->y)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "null MoE pointer");
+    if (a->x_dtype != FM_X_F32 && a->x_dtype != FM_X_BF16)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "unknown activation dtype");
+    if ((rc = check_quant_shape(a->gate_type, a->d_model, "expert gate"))) return rc;
+    if ((rc = check_quant_shape(a->up_type, a->d_model, "expert up"))) return rc;
+    if ((rc = check_quant_shape(a->down_type, a->ffn, "expert down"))) return rc;
+    if (a->gate_type != a->up_type)
+        return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION,
+                         "fused gate/up needs one block type for both projections");
+    if (a->gate_type == FM_TYPE_F32 || a->down_type == FM_TYPE_F32)
+        return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION,
+                         "F32 experts run through fmcuda_matvec_f32 (Backend::matvec)");
+    const MoeLayout L = moe_layout(a->tokens, a->experts, a->top_k, a->d_model, a->ffn);
+    if (!workspace || workspace_bytes < L.total)
+        return set_error(FM_STATUS_INVALID_ARGUMENT,
+                         "MoE workspace too small: need " + std::to_string(L.total) + " bytes");
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    uint32_t *ids = reinterpret_cast<uint32_t *>(ws + L.ids);
+    float *weights = reinterpret_cast<float *>(ws + L.weights);
+    uint32_t *counts = reinterpret_cast<uint32_t *>(ws + L.counts);
+    uint32_t *offsets = reinterpret_cast<uint32_t *>(ws + L.offsets);
+    uint32_t *pairs = reinterpret_cast<uint32_t *>(ws + L.pairs);
+    uint32_t *slot_of = reinterpret_cast<uint32_t *>(ws + L.slot_of);
+    __half *xh = reinterpret_cast<__half *>(ws + L.xh);
+    __half *xl = reinterpret_cast<__half *>(ws + L.xl);
+    float *xs = reinterpret_cast<float *>(ws + L.xs);
+    float *act = reinterpret_cast<float *>(ws + L.act);
+    __half *ah = reinterpret_cast<__half *>(ws + L.ah);
+    __half *al = reinterpret_cast<__half *>(ws + L.al);
+    float *as = reinterpret_cast<float *>(ws + L.as);
+    float *part = reinterpret_cast<float *>(ws + L.part);
+    const uint32_t P = a->tokens * a->top_k;
+    auto mark = [&](int i) {
+        if (a->stage_events && a->stage_events[i])
+            cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s);
+    };
+
+    mark(0);
+    if ((rc = launch_route(a->logits, a->tokens, a->experts, a->top_k, a->normalise, a->epsilon,
+                           a->scale, ids, weights, nullptr, s)))
+        return rc;
+    mark(1);
+    if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
+    mark(2);
+    const int xplanes = a->x_dtype == FM_X_F32 ? 2 : 1;
+    if ((rc = launch_xplanes(a->x, a->x_dtype, a->tokens, a->d_model, xh, xplanes > 1 ? xl : nullptr,
+                             xs, s)))
+        return rc;
+    mark(3);
+
+    const uint32_t tok_tiles = (a->tokens + 7) / 8; // an expert holds at most `tokens` pairs
+    QGemvParams gu{};
+    gu.slots = a->expert_slots;
+    gu.w_off0 = 0;
+    gu.w_off1 = a->up_offset;
+    gu.type_id = a->gate_type;
+    gu.out_dim = a->ffn;
+    gu.in_dim = a->d_model;
+    gu.row_bytes = row_bytes(a->gate_type, a->d_model);
+    gu.offsets = offsets;
+    gu.pairs = pairs;
+    gu.top_k = a->top_k;
+    gu.xh = xh;
+    gu.xl = xplanes > 1 ? xl : nullptr;
+    gu.xs = xs;
+    gu.y = act;
+    gu.status = device_status_word();
+    if ((rc = launch_qgemv<GEMV_GATE_UP>(gu, xplanes, tok_tiles, a->experts, s))) return rc;
+    mark(4);
+
+    if ((rc = launch_xplanes(act, FM_X_F32, P, a->ffn, ah, al, as, s))) return rc;
+    mark(5);
+
+    QGemvParams dn{};
+    dn.slots = a->expert_slots;
+    dn.w_off0 = a->down_offset;
+    dn.w_off1 = a->down_offset;
+    dn.type_id = a->down_type;
+    dn.out_dim = a->d_model;
+    dn.in_dim = a->ffn;
+    dn.row_bytes = row_bytes(a->down_type, a->ffn);
+    dn.offsets = offsets;
+    dn.pairs = pairs;
+    dn.top_k = a->top_k;
+    dn.xh = ah;
+    dn.xl = al;
+    dn.xs = as;
+    dn.y = part;
+    dn.status = device_status_word();
+    if ((rc = launch_qgemv<GEMV_DOWN>(dn, 2, tok_tiles, a->experts, s))) return rc;
+    mark(6);
+
+    const uint64_t n = static_cast<uint64_t>(a->tokens) * a->d_model;
+    combine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+        part, weights, slot_of, a->tokens, a->top_k, a->d_model, a->y);
+    if ((rc = check_launch("combine launch"))) return rc;
+    mark(7);
+    if (a->ids_out)
+        cudaMemcpyAsync(a->ids_out, ids, static_cast<uint64_t>(P) * 4, cudaMemcpyDeviceToDevice, s);
+    if (a->weights_out)
+        cudaMemcpyAsync(a->weights_out, weights, static_cast<uint64_t>(P) * 4,
+                        cudaMemcpyDeviceToDevice, s);
+    return check_launch("MoE output copies");
+}
+
+uint64_t moe_workspace_size(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t d,
+                            uint32_t ffn) {
+    return moe_layout(tokens, experts, top_k, d, ffn).total;
+}
+
+} // namespace fmb
+
+using namespace fmb;
+
+extern "C" int fmcuda_moe_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k,
+                                          uint32_t d_model, uint32_t ffn, uint64_t *bytes) {
+    if (!bytes) return set_error(FM_STATUS_INVALID_ARGUMENT, "null size pointer");
+    *bytes = moe_workspace_size(tokens, experts, top_k, d_model, ffn);
+    return FM_STATUS_OK;
+}
+
+extern "C" int fmcuda_moe_block(const fmcuda_moe_args *args, void *workspace,
+                                uint64_t workspace_bytes, void *stream) {
+    return moe_block_run(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}

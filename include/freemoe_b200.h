@@ -1,0 +1,219 @@
+/*
+ * freemoe_b200.h -- C ABI of the B200 (sm_100a) backend for FreeMoe's
+ * routed-expert MoE hot path.
+ *
+ * Plain pointers and sizes only.  Every entry point returns a status: 0 on
+ * success, otherwise the ordinal of the reference's fm::ErrorCode
+ * (include/fm/common.hpp:27-57) with a message readable through
+ * fmcuda_last_error().  Nothing throws, traps or aborts.  Device pointers are
+ * ordinary CUDA device addresses of the current device; `stream` is a
+ * cudaStream_t (NULL = the legacy default stream).  Kernels are asynchronous
+ * on `stream` unless documented otherwise.
+ *
+ * The reference interface each entry point replaces is cited as
+ * path:line of the reference tree (StrangeFrostMax/FreeMoe).
+ */
+#ifndef FREEMOE_B200_H
+#define FREEMOE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: fm::ErrorCode ordinals (include/fm/common.hpp:27-57) ---- */
+enum {
+    FM_STATUS_OK = 0,
+    FM_STATUS_UNSUPPORTED_QUANTISATION = 3,
+    FM_STATUS_SHAPE_MISMATCH = 8,
+    FM_STATUS_ALLOCATION_FAILED = 14,
+    FM_STATUS_INVALID_EXPERT_ID = 16,
+    FM_STATUS_EXPERT_EXECUTION_MISMATCH = 18,
+    FM_STATUS_TRANSFER_FAILED = 21,
+    FM_STATUS_FENCE_TIMEOUT = 22,
+    FM_STATUS_DEVICE_LOSS = 23,
+    FM_STATUS_INVALID_ARGUMENT = 26,
+    FM_STATUS_INTERNAL_ERROR = 28
+};
+
+/* ---- GGUF tensor types on the path (src/gguf.cpp:58-106) ---- */
+enum { FM_TYPE_F32 = 0, FM_TYPE_Q8_0 = 8, FM_TYPE_Q4_K = 12 };
+
+/* ---- activation dtypes ---- */
+enum { FM_X_F32 = 0, FM_X_BF16 = 1 };
+
+/* ---- summation order of the F32 matvec (fmcuda_matvec_f32) ---- */
+enum {
+    FM_ORDER_ANY = 0,    /* fastest; tolerance-level agreement */
+    FM_ORDER_SCALAR = 1, /* bit-identical to gemv_scalar, src/kernels.cpp:132-140 */
+    FM_ORDER_AVX2 = 2    /* bit-identical to gemv_avx2_row, src/kernels.cpp:147-166 */
+};
+
+/* Last error message of the calling thread ("" when none). */
+const char *fmcuda_last_error(void);
+
+/* ======================= runtime (Backend plumbing) ======================= */
+
+/* Device facts for fm::DeviceInfo (include/fm/backend.hpp:22-36). */
+typedef struct fmcuda_device_info {
+    char name[256];
+    uint64_t total_memory_bytes;
+    uint64_t free_memory_bytes;
+    int32_t sm_count;
+    int32_t cc_major;
+    int32_t cc_minor;
+    int32_t driver_version;
+    int32_t runtime_version;
+    int32_t l2_bytes;
+} fmcuda_device_info;
+
+/* Selects `device` for the calling thread and creates the library's per-device
+ * state.  Replaces the GpuBackend placeholder constructor (src/backend.cpp:528-531).
+ * Fails with DEVICE_LOSS when no usable sm_100 device is present. */
+int fmcuda_init(int32_t device);
+/* Backend::info (include/fm/backend.hpp:151). */
+int fmcuda_device_info_get(int32_t device, fmcuda_device_info *out);
+
+/* Backend::allocate (include/fm/backend.hpp:152): HBM, 256-byte aligned,
+ * zero-filled like CpuBackend::allocate (src/backend.cpp:240-256). */
+int fmcuda_malloc(uint64_t bytes, void **ptr);
+/* DeviceBuffer::cleanup (include/fm/backend.hpp:70-110). */
+int fmcuda_free(void *ptr);
+/* Pinned host staging for uploads (host side of Backend::upload). */
+int fmcuda_host_alloc(uint64_t bytes, void **ptr);
+int fmcuda_host_free(void *ptr);
+
+int fmcuda_stream_create(void **stream);
+int fmcuda_stream_destroy(void *stream);
+int fmcuda_stream_sync(void *stream);
+int fmcuda_event_create(void **event);
+int fmcuda_event_destroy(void *event);
+int fmcuda_event_record(void *event, void *stream);
+
+/* Backend::upload (include/fm/backend.hpp:153): enqueue a host->device copy on
+ * `stream` and record `event` after it (the fence).  `src` should be pinned
+ * (fmcuda_host_alloc) for the copy to be asynchronous. */
+int fmcuda_upload_async(void *dst, const void *src, uint64_t bytes, void *stream, void *event);
+/* Backend::fence_complete (include/fm/backend.hpp:154): *complete = 1 when
+ * the event's work has finished, 0 while pending. */
+int fmcuda_event_query(void *event, int32_t *complete);
+/* Backend::wait_fence (include/fm/backend.hpp:155, src/backend.cpp:128-135):
+ * polls the event and returns FENCE_TIMEOUT after `timeout_ms`; never an
+ * unbounded wait. */
+int fmcuda_event_wait(void *event, uint32_t timeout_ms);
+/* Synchronous device->host copy: the slot read-back that the residency
+ * manager checksums (src/residency.cpp:703-704, :713-714). */
+int fmcuda_download(void *dst, const void *src, uint64_t bytes, void *stream);
+int fmcuda_memset_async(void *dst, int32_t value, uint64_t bytes, void *stream);
+
+/* Reads (and with clear != 0 resets) the device-side status word that kernels
+ * set instead of trapping (non-finite router logit, unresident expert).
+ * Synchronises the device first. */
+int fmcuda_device_status(int32_t clear, int32_t *status);
+
+/* ============================ hot-path kernels ============================ */
+
+/* Row bytes of `in_dim` values of `type_id` (0 on bad geometry). */
+uint64_t fmcuda_row_bytes(uint32_t type_id, uint32_t in_dim);
+
+/* K1, dequantize_tensor_region (src/quant.cpp:723-732) over `n_elems` values
+ * (whole blocks): F32, Q8_0 (:223-228), Q4_K (:297-318).  Bit-exact. */
+int fmcuda_dequant(uint32_t type_id, const void *src, float *dst, uint64_t n_elems,
+                   void *stream);
+
+/* K2, gemv_quant / gemm_quant (src/kernels.cpp:846-878, :316-345):
+ * y[t*out_dim + o] = sum_k W[o,k] x[t*in_dim + k] for t < tokens, with W in
+ * GGUF row-major blocks of `type_id` and x in `x_dtype`.  Dequantisation is
+ * fused into the contraction.  Any number of tokens; the weight rows are read
+ * once per 8 tokens.  Validation and error codes as gemv_quant. */
+int fmcuda_gemv(uint32_t type_id, const void *w, const void *x, int32_t x_dtype, float *y,
+                uint32_t tokens, uint32_t out_dim, uint32_t in_dim, void *stream);
+
+/* Backend::matvec (include/fm/backend.hpp:157; CpuBackend::matvec
+ * src/backend.cpp:277-290): one F32 product, y = W x, in the requested
+ * summation order (FM_ORDER_*). */
+int fmcuda_matvec_f32(const float *w, const float *x, float *y, uint32_t out_dim,
+                      uint32_t in_dim, int32_t order, void *stream);
+
+/* K4, the native router (Engine::softmax src/engine.cpp:378-393, Engine::topk
+ * :395-411, renormalisation :1680-1702), one warp per token:
+ *   logits [T*E] f32 -> ids [T*k] (stable descending, ties to the lower id),
+ *   weights [T*k] f32, probs [T*E] f32 (optional, may be NULL).
+ * A non-finite logit sets the device status to INTERNAL_ERROR (read it with
+ * fmcuda_device_status).  E <= 1024, k <= min(E, 32). */
+int fmcuda_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                 int32_t normalise, double epsilon, double scale, uint32_t *ids, float *weights,
+                 float *probs, void *stream);
+
+/* Grouping of the T*k (token, rank) pairs by expert:
+ *   counts [E], offsets [E+1] (exclusive scan), pairs [T*k] (for each expert,
+ *   its flat pair indices t*k + r in ascending token order), slot_of [T*k]
+ *   (inverse permutation; may be NULL).  Single kernel, bit-exact with the
+ *   deterministic host grouping.  E <= 1024. */
+int fmcuda_group(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t experts,
+                 uint32_t *counts, uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of,
+                 void *stream);
+
+/* One routed-expert MoE block (src/engine.cpp:1603-1772) for `tokens` tokens:
+ * router (softmax, top-k, renormalisation) on the given logits, grouping by
+ * expert, per expert a fused gate/up GEMV with SwiGLU
+ * (include/fm/activation.hpp:62-84), the down GEMV, and the weighted combine
+ * ffn[j] += w * down[j] in top-k order (src/engine.cpp:1770).
+ *
+ * expert_slots: device array [E] of expert payload base pointers laid out as
+ * an ExpertRecord (include/fm/gguf.hpp:737-758): gate rows, then up rows at
+ * `up_offset`, then down rows at `down_offset`.  A NULL entry is an expert
+ * that is not resident; routing to it sets the device status to
+ * EXPERT_EXECUTION_MISMATCH and leaves that expert's contribution out.
+ *
+ * workspace: device scratch of fmcuda_moe_workspace_bytes() bytes. */
+typedef struct fmcuda_moe_args {
+    const void *x;            /* [tokens * d_model], x_dtype */
+    int32_t x_dtype;          /* FM_X_F32 or FM_X_BF16 */
+    const float *logits;      /* [tokens * experts] router logits */
+    uint32_t tokens;
+    uint32_t experts;
+    uint32_t top_k;
+    uint32_t d_model;
+    uint32_t ffn;
+    const void *const *expert_slots; /* device array [experts] */
+    uint64_t up_offset;       /* bytes from slot base to the up rows */
+    uint64_t down_offset;     /* bytes from slot base to the down rows */
+    uint32_t gate_type;
+    uint32_t up_type;
+    uint32_t down_type;
+    int32_t normalise;        /* expert_weights_norm */
+    double epsilon;           /* expert_weights_epsilon (6.103515625e-5) */
+    double scale;             /* expert_weights_scale (1.0) */
+    float *y;                 /* [tokens * d_model] f32 output */
+    uint32_t *ids_out;        /* optional [tokens * top_k] */
+    float *weights_out;       /* optional [tokens * top_k] */
+    /* optional: FM_MOE_STAGES + 1 cudaEvent_t handles recorded on `stream`
+     * before the first stage and after each stage (router, grouping, x
+     * planes, gate/up, act planes, down, combine), for live per-kernel timing;
+     * NULL disables.  Entries may be NULL. */
+    void *const *stage_events;
+} fmcuda_moe_args;
+
+enum { FM_MOE_STAGES = 7 };
+
+int fmcuda_moe_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k,
+                               uint32_t d_model, uint32_t ffn, uint64_t *bytes);
+int fmcuda_moe_block(const fmcuda_moe_args *args, void *workspace, uint64_t workspace_bytes,
+                     void *stream);
+
+/* ====================== synthetic weights (bench/test) ====================== */
+
+/* Fills `dst` with `rows` rows of `cols` values of `type_id` (Q8_0 / Q4_K /
+ * F32) encoding seeded Gaussian weights N(0, std^2): value i of the tensor is
+ * a Box-Muller draw from a counter-based hash of (seed, i).  Any valid
+ * encoding is acceptable to the path; only the decode is graded. */
+int fmcuda_synth_weights(uint32_t type_id, void *dst, uint64_t rows, uint32_t cols,
+                         uint64_t seed, float std, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FREEMOE_B200_H */
