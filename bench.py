@@ -260,12 +260,21 @@ def run_ours(args):
     ws = torch.empty(hotpath.moe_workspace_bytes(T, EXPERTS, EXPERTS, D_MODEL, FFN), dtype=torch.uint8,
                      device=dev)
     n_ev = len(MOE_STAGES) + 1
-    ev_pool = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
-    ev_arrays = [(C.c_void_p * n_ev)(*[e.cuda_event for e in evs]) for evs in ev_pool]
-    for evs in ev_pool:
-        for e in evs:
-            e.record(stream)  # materialise the events before their handles are used
     lib = load()
+
+    def timing_event():
+        h = C.c_void_p()
+        check(lib.fmcuda_event_create_timing(C.byref(h)))
+        return h.value
+
+    # library-owned timing events, recorded by fmcuda_moe_block between its stages
+    ev_pool = [[timing_event() for _ in range(n_ev)] for _ in range(args.steps)]
+    ev_arrays = [(C.c_void_p * n_ev)(*evs) for evs in ev_pool]
+
+    def elapsed(a, b):
+        v = C.c_float()
+        check(lib.fmcuda_event_elapsed_ms(C.c_void_p(a), C.c_void_p(b), C.byref(v)))
+        return v.value
     ws_ptr, ws_n, sptr = C.c_void_p(ws.data_ptr()), ws.numel(), stream.cuda_stream
 
     arg_cache = {}
@@ -302,8 +311,11 @@ def run_ours(args):
         end.record(stream)
         barrier()
     ms = start.elapsed_time(end) / args.steps
-    stage_ms = {s: statistics.mean(ev_pool[i][j].elapsed_time(ev_pool[i][j + 1]) for i in range(args.steps))
+    stage_ms = {s: statistics.mean(elapsed(ev_pool[i][j], ev_pool[i][j + 1]) for i in range(args.steps))
                 for j, s in enumerate(MOE_STAGES)}
+    for evs in ev_pool:
+        for e in evs:
+            lib.fmcuda_event_destroy(C.c_void_p(e))
 
     # ---- end to end through the C ABI with host buffers ----------------------
     hx = torch.from_numpy(x_np).to(torch.bfloat16).pin_memory()
@@ -395,7 +407,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))

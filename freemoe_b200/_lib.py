@@ -90,6 +90,7 @@ SIGNATURES = [
     ("fmcuda_init", C.c_int, [_I32]),
     ("fmcuda_device_info_get", C.c_int, [_I32, C.POINTER(DeviceInfo)]),
     ("fmcuda_malloc", C.c_int, [_U64, C.POINTER(C.c_void_p)]),
+    ("fmcuda_malloc_managed", C.c_int, [_U64, C.POINTER(C.c_void_p)]),
     ("fmcuda_free", C.c_int, [_P]),
     ("fmcuda_host_alloc", C.c_int, [_U64, C.POINTER(C.c_void_p)]),
     ("fmcuda_host_free", C.c_int, [_P]),
@@ -99,6 +100,8 @@ SIGNATURES = [
     ("fmcuda_event_create", C.c_int, [C.POINTER(C.c_void_p)]),
     ("fmcuda_event_destroy", C.c_int, [_P]),
     ("fmcuda_event_record", C.c_int, [_P, _P]),
+    ("fmcuda_event_create_timing", C.c_int, [C.POINTER(C.c_void_p)]),
+    ("fmcuda_event_elapsed_ms", C.c_int, [_P, _P, C.POINTER(C.c_float)]),
     ("fmcuda_upload_async", C.c_int, [_P, _P, _U64, _P, _P]),
     ("fmcuda_event_query", C.c_int, [_P, C.POINTER(C.c_int32)]),
     ("fmcuda_event_wait", C.c_int, [_P, _U32]),

@@ -1,11 +1,13 @@
 // gemv.cu -- K2 entry points: quantised GEMV (gemv_quant / gemm_quant,
 // src/kernels.cpp:846-878, :316-345) and the F32 matvec behind
 // Backend::matvec (src/backend.cpp:277-290 -> gemv, src/kernels.cpp:470-508).
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "gemv_kernels.cuh"
+#include "gemv_async.cuh"
 
 namespace fmb {
 
@@ -180,8 +182,9 @@ template int launch_qgemv<GEMV_PLAIN>(const QGemvParams &, int, uint32_t, uint32
 template int launch_qgemv<GEMV_GATE_UP>(const QGemvParams &, int, uint32_t, uint32_t, cudaStream_t);
 template int launch_qgemv<GEMV_DOWN>(const QGemvParams &, int, uint32_t, uint32_t, cudaStream_t);
 
-// Shape checks shared with the MoE block: the fast paths need whole blocks
-// and 16-byte aligned rows (every shape on the path satisfies both).
+// Shape checks shared with the MoE block (gemv_quant's own rules,
+// src/kernels.cpp:850-858: whole blocks per row).  The register-fed kernel
+// additionally needs Q8_0 rows of a multiple of 32 values (whole blocks).
 int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what) {
     uint32_t bs, bb;
     if (!block_geometry(type_id, &bs, &bb))
@@ -191,11 +194,89 @@ int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what) {
     if (in_dim % bs)
         return set_error(FM_STATUS_SHAPE_MISMATCH,
                          std::string(what) + ": quantised row length is not a whole number of blocks");
-    if (type_id != FM_TYPE_F32 && in_dim % 256)
-        return set_error(FM_STATUS_SHAPE_MISMATCH,
-                         std::string(what) + ": device kernels need rows of a multiple of 256 values");
     return FM_STATUS_OK;
 }
+
+// The TMA-staged kernel takes rows of whole 256-value K steps whose byte
+// length keeps every row 16-byte aligned (bulk copies need 16-byte aligned
+// sources); everything on the BASELINE shapes qualifies.
+bool staged_shape(uint32_t type_id, uint32_t in_dim) {
+    return type_id != FM_TYPE_F32 && in_dim % 256 == 0 && row_bytes(type_id, in_dim) % 16 == 0;
+}
+
+int xplane_layout(uint32_t type_id) { return type_id == FM_TYPE_Q4_K ? XL_Q4K : XL_Q8; }
+
+int launch_xplanes_staged(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, int layout,
+                          __half *xh, __half *xl, float *xs, cudaStream_t s) {
+    const uint64_t n = static_cast<uint64_t>(rows) * (k_dim / 32);
+    if (n == 0) return FM_STATUS_OK;
+    const unsigned grid = static_cast<unsigned>((n + 127) / 128);
+    if (x_dtype == FM_X_BF16)
+        xplanes_staged_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+            static_cast<const __nv_bfloat16 *>(x), rows, k_dim, layout, xh, xl, xs);
+    else
+        xplanes_staged_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float *>(x), rows, k_dim,
+                                                          layout, xh, xl, xs);
+    return check_launch("staged x-plane launch");
+}
+
+namespace {
+int sm_count() {
+    static int n[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        if (cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || !n[dev])
+            n[dev] = 148;
+    }
+    return n[dev];
+}
+
+template <int TYPE, int PL, int MODE, int P>
+int launch_async_inst(const QGemvParams &prm, uint32_t tok_tiles, uint32_t experts, cudaStream_t s) {
+    constexpr int MT = 2, NW = 4;
+    constexpr int NMAT = MODE == GEMV_GATE_UP ? 2 : 1;
+    using G = StageGeom<TYPE, MT, NMAT>;
+    constexpr size_t smem = static_cast<size_t>(NW) * P * G::BYTES;
+    auto kern = qgemv_async_kernel<TYPE, MT, NW, PL, MODE, P>;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+        if (err != cudaSuccess) return cuda_status(err, "streamed GEMV shared-memory limit");
+        configured[dev] = true;
+    }
+    int per_sm = 0;
+    cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NW * 32, smem);
+    if (err != cudaSuccess || per_sm < 1) per_sm = 1;
+    const uint32_t row_tiles = (prm.out_dim + G::TILE - 1) / G::TILE;
+    uint32_t grid = static_cast<uint32_t>(per_sm * sm_count());
+    if (MODE == GEMV_PLAIN) grid = std::min<uint32_t>(grid, row_tiles * tok_tiles);
+    if (grid == 0) return FM_STATUS_OK;
+    kern<<<grid, NW * 32, smem, s>>>(prm, row_tiles, tok_tiles, experts);
+    return check_launch("streamed GEMV launch");
+}
+} // namespace
+
+// Ring depth P per warp: as many K steps in flight as fit in ~72 KB per CTA
+// (two CTAs per SM), at least two.
+template <int MODE>
+int launch_qgemv_stream(const QGemvParams &prm, int planes, uint32_t tok_tiles, uint32_t experts,
+                        cudaStream_t s) {
+    constexpr int PQ4 = MODE == GEMV_GATE_UP ? 2 : 4; // 9 KB / 4.5 KB slots
+    if (prm.type_id == FM_TYPE_Q4_K)
+        return planes == 1 ? launch_async_inst<FM_TYPE_Q4_K, 1, MODE, PQ4>(prm, tok_tiles, experts, s)
+                           : launch_async_inst<FM_TYPE_Q4_K, 2, MODE, PQ4>(prm, tok_tiles, experts, s);
+    return planes == 1 ? launch_async_inst<FM_TYPE_Q8_0, 1, MODE, 2>(prm, tok_tiles, experts, s)
+                       : launch_async_inst<FM_TYPE_Q8_0, 2, MODE, 2>(prm, tok_tiles, experts, s);
+}
+
+template int launch_qgemv_stream<GEMV_PLAIN>(const QGemvParams &, int, uint32_t, uint32_t, cudaStream_t);
+template int launch_qgemv_stream<GEMV_GATE_UP>(const QGemvParams &, int, uint32_t, uint32_t, cudaStream_t);
+template int launch_qgemv_stream<GEMV_DOWN>(const QGemvParams &, int, uint32_t, uint32_t, cudaStream_t);
 
 } // namespace fmb
 
@@ -224,6 +305,7 @@ extern "C" int fmcuda_gemv(uint32_t type_id, const void *w, const void *x, int32
         return check_launch("f32 GEMV launch");
     }
     const int planes = x_dtype == FM_X_F32 ? 2 : 1;
+    const bool staged = staged_shape(type_id, in_dim) && (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
     const uint64_t plane_bytes = align256(static_cast<uint64_t>(tokens) * in_dim * 2);
     const uint64_t sum_bytes = align256(static_cast<uint64_t>(tokens) * (in_dim / 32) * 4);
     void *ws = nullptr;
@@ -233,7 +315,8 @@ extern "C" int fmcuda_gemv(uint32_t type_id, const void *w, const void *x, int32
     __half *xl = planes > 1 ? reinterpret_cast<__half *>(static_cast<uint8_t *>(ws) + plane_bytes)
                             : nullptr;
     float *xs = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + plane_bytes * planes);
-    rc = launch_xplanes(x, x_dtype, tokens, in_dim, xh, xl, xs, s);
+    rc = staged ? launch_xplanes_staged(x, x_dtype, tokens, in_dim, xplane_layout(type_id), xh, xl, xs, s)
+                : launch_xplanes(x, x_dtype, tokens, in_dim, xh, xl, xs, s);
     if (rc) return rc;
     QGemvParams prm{};
     prm.w = static_cast<const uint8_t *>(w);
@@ -246,6 +329,8 @@ extern "C" int fmcuda_gemv(uint32_t type_id, const void *w, const void *x, int32
     prm.xl = xl;
     prm.xs = xs;
     prm.y = y;
+    prm.status = device_status_word();
+    if (staged) return launch_qgemv_stream<GEMV_PLAIN>(prm, planes, (tokens + 7) / 8, 1, s);
     return launch_qgemv<GEMV_PLAIN>(prm, planes, (tokens + 7) / 8, 1, s);
 }
 

@@ -1,0 +1,355 @@
+// gemv_async.cuh -- the decode GEMV: quantised rows streamed with 16-byte
+// cp.async copies into per-warp shared-memory rings, dequantised in
+// registers into mma.sync tensor-core fragments.
+//
+// Replaces the per-row CPU kernels row_dot_q4_k_avx2 / row_dot_q8_0_avx2
+// (src/kernels.cpp:720-771, :639-653) for rows of a multiple of 256 values.
+//
+// Structure: persistent CTAs of NW warps; a tile is 16*MT rows (of NMAT
+// matrices over the same rows: gate and up) x 8 token columns.  Warp w takes
+// the 256-value K steps w, w + NW, ... of each tile.  Each warp keeps P of its
+// K steps in flight: for step j it issues 16-byte cp.async copies of every
+// tile row's quant bytes (each warp instruction moves 512 contiguous-ish
+// bytes; 9 or 17 chunks per row) into ring slot j % P, P steps ahead,
+// crossing tile boundaries, so the HBM stream never drains between tiles.
+// The weight bytes never pass through registers until they are unpacked; x
+// fragments (L2/L1 resident, read by every tile) are loaded directly before
+// the ring wait.  Per tile the warps' partial sums are reduced in shared
+// memory in a fixed order (deterministic) and written (with SwiGLU for
+// gate/up).  Only tiles that hold tokens are visited: the CTA first builds
+// the prefix of token tiles per expert from the grouping offsets.
+#pragma once
+
+#include "gemv_core.cuh"
+#include "gemv_kernels.cuh"
+#include "ptx.cuh"
+
+namespace fmb {
+
+// ---- x-plane layouts for the staged kernel -----------------------------------
+//
+// Position of logical element k of a 256-value K step inside its staged row,
+// chosen so that a warp's 16-byte fragment loads read 64 contiguous bytes per
+// token:
+//   Q4_K: lane (g, c) reads, for i = 0..7, the 8 values 64c + 8i + [0, 8) as
+//         chunk 4i + c;
+//   Q8_0: lane (g, c) reads, for sub-block s = 0..7, the 4 + 4 values
+//         32s + 4c + [0, 4) and 32s + 16 + 4c + [0, 4) as chunk 4s + c.
+// Inside a chunk each group of 4 is stored (0, 2, 1, 3) (xplane_pos).
+enum { XL_Q4K = 0, XL_Q8 = 1 };
+
+__host__ __device__ __forceinline__ uint32_t staged_pos(uint32_t k, int layout) {
+    const uint32_t base = k & ~255u, r = k & 255u;
+    uint32_t chunk, j;
+    if (layout == XL_Q4K) {
+        const uint32_t c = r >> 6, i = (r >> 3) & 7u;
+        chunk = 4 * i + c;
+        j = r & 7u;
+    } else {
+        const uint32_t s = r >> 5, w = r & 31u;       // sub-block, position in it
+        const uint32_t half = w >> 4, c = (w >> 2) & 3u; // [0,16) or [16,32); lane c
+        chunk = 4 * s + c;
+        j = half * 4 + (w & 3u);
+    }
+    return base + chunk * 8 + (j & 4u) + xplane_pos(j & 3u);
+}
+
+template <typename XT>
+__global__ void xplanes_staged_kernel(const XT *__restrict__ x, uint32_t rows, uint32_t k_dim,
+                                      int layout, __half *__restrict__ xh, __half *__restrict__ xl,
+                                      float *__restrict__ xs) {
+    const uint32_t subs = k_dim / 32;
+    const uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (id >= static_cast<uint64_t>(rows) * subs) return;
+    const uint32_t row = static_cast<uint32_t>(id / subs), s = static_cast<uint32_t>(id % subs);
+    const XT *src = x + static_cast<uint64_t>(row) * k_dim;
+    __half *dh = xh + static_cast<uint64_t>(row) * k_dim;
+    __half *dl = xl ? xl + static_cast<uint64_t>(row) * k_dim : nullptr;
+    float sum = 0.0f;
+#pragma unroll 8
+    for (uint32_t i = 0; i < 32; ++i) {
+        const uint32_t k = 32 * s + i;
+        const float v = load_x<XT>(src + k);
+        sum += v;
+        const __half h = __float2half_rn(v);
+        const uint32_t pos = staged_pos(k, layout);
+        dh[pos] = h;
+        if (dl) dl[pos] = __float2half_rn(v - __half2float(h));
+    }
+    xs[static_cast<uint64_t>(row) * subs + s] = sum;
+}
+
+template <int TYPE, int MT, int NMAT>
+struct StageGeom {
+    static constexpr int TILE = 16 * MT;
+    static constexpr int RB = TYPE == FM_TYPE_Q4_K ? 144 : 272; // quant bytes per row per K step
+    static constexpr int CHUNKS = RB / 16;                       // 16-byte copies per row
+    static constexpr int BYTES = NMAT * TILE * RB;               // one ring slot
+};
+
+constexpr int kMaxGroupExperts = 1024;
+
+template <int TYPE, int MT, int NW, int PLANES, int MODE, int P>
+__global__ void __launch_bounds__(NW * 32)
+    qgemv_async_kernel(const QGemvParams p, uint32_t row_tiles, uint32_t tok_tiles, uint32_t experts) {
+    constexpr int NMAT = (MODE == GEMV_GATE_UP) ? 2 : 1;
+    using G = StageGeom<TYPE, MT, NMAT>;
+    constexpr int TILE = G::TILE;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float s_red[NW][NMAT][TILE][8];
+    __shared__ uint32_t s_prefix[kMaxGroupExperts + 1]; // token tiles before expert e
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, c = lane & 3;
+    const uint32_t nsteps = p.in_dim / 256;
+    const uint32_t nsub = p.in_dim / 32;
+    uint8_t *ring = smem + static_cast<size_t>(warp) * P * G::BYTES;
+
+    // ---- active tiles: (expert, token tile, row tile), empty experts skipped
+    uint32_t total_tok_tiles;
+    if (MODE == GEMV_PLAIN) {
+        total_tok_tiles = tok_tiles;
+    } else {
+        if (warp == 0) {
+            uint32_t carry = 0;
+            for (uint32_t e0 = 0; e0 < experts; e0 += 32) {
+                const uint32_t e = e0 + lane;
+                uint32_t v = 0;
+                if (e < experts) v = (__ldg(p.offsets + e + 1) - __ldg(p.offsets + e) + 7) / 8;
+                uint32_t incl = v;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                    if (lane >= o) incl += n;
+                }
+                if (e < experts) s_prefix[e] = carry + incl - v;
+                carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+            }
+            if (lane == 0) s_prefix[experts] = carry;
+        }
+        __syncthreads();
+        total_tok_tiles = s_prefix[experts];
+    }
+    const uint32_t n_tiles = total_tok_tiles * row_tiles;
+    const uint32_t my_tiles = n_tiles > blockIdx.x ? (n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0u;
+    const uint32_t nw = nsteps > static_cast<uint32_t>(warp) ? (nsteps - warp + NW - 1) / NW : 0u;
+
+    // tile i of this CTA -> rows, expert, columns
+    struct Tile {
+        uint32_t row0, e, start, ncol;
+        const uint8_t *base;
+    };
+    auto tile_of = [&](uint32_t i) -> Tile {
+        Tile tl;
+        const uint32_t a = blockIdx.x + i * gridDim.x;
+        tl.row0 = (a % row_tiles) * TILE;
+        const uint32_t q = a / row_tiles;
+        if (MODE == GEMV_PLAIN) {
+            tl.e = 0;
+            tl.start = q * 8;
+            tl.ncol = min(8u, p.tokens - tl.start);
+            tl.base = p.w;
+        } else {
+            uint32_t lo = 0, hi = experts; // last e with s_prefix[e] <= q
+            while (hi - lo > 1) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (s_prefix[mid] <= q) lo = mid;
+                else hi = mid;
+            }
+            tl.e = lo;
+            const uint32_t off = __ldg(p.offsets + lo), end = __ldg(p.offsets + lo + 1);
+            tl.start = off + (q - s_prefix[lo]) * 8;
+            tl.ncol = min(8u, end - tl.start);
+            tl.base = static_cast<const uint8_t *>(p.slots[lo]);
+        }
+        return tl;
+    };
+
+    // issue the copies of this warp's item j (tile j / nw, K step w + NW (j % nw))
+    auto issue = [&](uint32_t j) {
+        if (nw && j < my_tiles * nw) {
+            const Tile tl = tile_of(j / nw);
+            const uint32_t b = warp + NW * (j % nw);
+            if (tl.base && (reinterpret_cast<uintptr_t>(tl.base) & 15u) == 0) {
+                uint8_t *slot = ring + (j % P) * G::BYTES;
+#pragma unroll
+                for (int u = 0; u < (NMAT * TILE * G::CHUNKS + 31) / 32; ++u) {
+                    const int qd = lane + 32 * u;
+                    if (qd < NMAT * TILE * G::CHUNKS) {
+                        const int r = qd / G::CHUNKS, part = qd % G::CHUNKS;
+                        const int m = r / TILE, rr = r % TILE;
+                        const uint32_t row = min(tl.row0 + rr, p.out_dim - 1);
+                        const uint8_t *src = tl.base + (m ? p.w_off1 : p.w_off0) +
+                                             static_cast<uint64_t>(row) * p.row_bytes +
+                                             static_cast<uint64_t>(b) * G::RB + part * 16;
+                        cp_async16(slot + r * G::RB + part * 16, src);
+                    }
+                }
+            }
+        }
+        cp_async_commit(); // one group per item, even an empty one
+    };
+
+#pragma unroll
+    for (int j = 0; j < P; ++j) issue(j);
+
+    for (uint32_t i = 0; i < my_tiles; ++i) {
+        const Tile tl = tile_of(i);
+        if (threadIdx.x == 0 && MODE != GEMV_PLAIN && !tl.base)
+            raise_device_status(p.status, FM_STATUS_EXPERT_EXECUTION_MISMATCH);
+        if (threadIdx.x == 0 && tl.base && (reinterpret_cast<uintptr_t>(tl.base) & 15u))
+            raise_device_status(p.status, FM_STATUS_INVALID_ARGUMENT);
+        const bool tile_ok = tl.base && (reinterpret_cast<uintptr_t>(tl.base) & 15u) == 0;
+        const bool col_ok = static_cast<uint32_t>(g) < tl.ncol;
+        auto xrow_of = [&](uint32_t col) -> uint32_t {
+            const uint32_t o = tl.start + col;
+            return MODE == GEMV_GATE_UP ? __ldg(p.pairs + o) / p.top_k : o;
+        };
+        const uint32_t xr = col_ok ? xrow_of(g) : 0u;
+        const uint8_t *xh_row = reinterpret_cast<const uint8_t *>(p.xh + static_cast<uint64_t>(xr) * p.in_dim);
+        const uint8_t *xl_row =
+            PLANES > 1 ? reinterpret_cast<const uint8_t *>(p.xl + static_cast<uint64_t>(xr) * p.in_dim) : nullptr;
+        const float *xs_row = p.xs + static_cast<uint64_t>(xr) * nsub;
+        const bool ok_a = static_cast<uint32_t>(2 * c) < tl.ncol, ok_b = static_cast<uint32_t>(2 * c + 1) < tl.ncol;
+        const float *xs_a = (TYPE == FM_TYPE_Q8_0 && ok_a) ? p.xs + static_cast<uint64_t>(xrow_of(2 * c)) * nsub : nullptr;
+        const float *xs_b = (TYPE == FM_TYPE_Q8_0 && ok_b) ? p.xs + static_cast<uint64_t>(xrow_of(2 * c + 1)) * nsub : nullptr;
+
+        float tot[NMAT][MT][4];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) tot[m][mt][e] = 0.0f;
+
+        for (uint32_t jj = 0; jj < nw; ++jj) {
+            const uint32_t j = i * nw + jj;
+            const uint32_t b = warp + NW * jj;
+            // x fragments for this K step, loaded before the ring wait
+            uint32_t xb[PLANES][32];
+#pragma unroll
+            for (int pl = 0; pl < PLANES; ++pl) {
+                const uint8_t *row = (pl ? xl_row : xh_row) + static_cast<uint64_t>(b) * 512;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (col_ok) v = __ldg(reinterpret_cast<const uint4 *>(row + (4 * q + c) * 16));
+                    xb[pl][4 * q + 0] = v.x;
+                    xb[pl][4 * q + 1] = v.y;
+                    xb[pl][4 * q + 2] = v.z;
+                    xb[pl][4 * q + 3] = v.w;
+                }
+            }
+            float2 X = make_float2(0.f, 0.f);
+            float Xa[8], Xb[8];
+            if (TYPE == FM_TYPE_Q4_K) {
+                if (col_ok) X = __ldg(reinterpret_cast<const float2 *>(xs_row + b * 8 + 2 * c));
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    Xa[q] = ok_a ? __ldg(xs_a + b * 8 + q) : 0.0f;
+                    Xb[q] = ok_b ? __ldg(xs_b + b * 8 + q) : 0.0f;
+                }
+            }
+            cp_async_wait<P - 1>(); // item j landed (this lane's copies)
+            __syncwarp();           // ... and every other lane's
+            const uint8_t *st = ring + (j % P) * G::BYTES;
+            if (tile_ok && TYPE == FM_TYPE_Q4_K) {
+                uint32_t xm[2];
+                xm[0] = pack_half2(X.x, X.y);
+                xm[1] = pack_half2(X.x - half_lo_f(xm[0]), X.y - half_hi_f(xm[0]));
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const uint8_t *r0 = st + (m * TILE + 16 * mt + g) * G::RB;
+                        const uint8_t *r1 = r0 + 8 * G::RB;
+                        const uint4 h0 = *reinterpret_cast<const uint4 *>(r0);
+                        const uint4 h1 = *reinterpret_cast<const uint4 *>(r1);
+                        uint4 q0[2], q1[2];
+                        q0[0] = *reinterpret_cast<const uint4 *>(r0 + 16 + 32 * c);
+                        q0[1] = *reinterpret_cast<const uint4 *>(r0 + 32 + 32 * c);
+                        q1[0] = *reinterpret_cast<const uint4 *>(r1 + 16 + 32 * c);
+                        q1[1] = *reinterpret_cast<const uint4 *>(r1 + 32 + 32 * c);
+                        q4k_mtile_block<PLANES>(h0, h1, q0, q1, c, xb, xm, tot[m][mt]);
+                    }
+            } else if (tile_ok) { // Q8_0: 8 blocks of 32 per K step; block sb uses registers 4sb..4sb+3
+#pragma unroll
+                for (int sb = 0; sb < 8; ++sb) {
+                    const uint32_t off = 34 * sb;
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            uint32_t wa[2], wb[2], dr[2];
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const uint8_t *r = st + (m * TILE + 16 * mt + g + 8 * h) * G::RB + off;
+                                dr[h] = *reinterpret_cast<const uint16_t *>(r);
+                                if ((sb & 1) == 0) { // codes start 2 bytes into an aligned word
+                                    const uint32_t *wp = reinterpret_cast<const uint32_t *>(r + 4 * c);
+                                    const uint32_t *wq = reinterpret_cast<const uint32_t *>(r + 16 + 4 * c);
+                                    wa[h] = __funnelshift_r(wp[0], wp[1], 16);
+                                    wb[h] = __funnelshift_r(wq[0], wq[1], 16);
+                                } else {
+                                    wa[h] = *reinterpret_cast<const uint32_t *>(r + 2 + 4 * c);
+                                    wb[h] = *reinterpret_cast<const uint32_t *>(r + 18 + 4 * c);
+                                }
+                            }
+                            const uint32_t va0 = wa[0] ^ 0x80808080u, vb0 = wb[0] ^ 0x80808080u;
+                            const uint32_t va1 = wa[1] ^ 0x80808080u, vb1 = wb[1] ^ 0x80808080u;
+                            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                            for (int pl = 0; pl < PLANES; ++pl) {
+                                mma_f16(acc, prmt(va0, 0x64646464u, 0x4240u), prmt(va1, 0x64646464u, 0x4240u),
+                                        prmt(va0, 0x64646464u, 0x4341u), prmt(va1, 0x64646464u, 0x4341u),
+                                        xb[pl][4 * sb + 0], xb[pl][4 * sb + 1]);
+                                mma_f16(acc, prmt(vb0, 0x64646464u, 0x4240u), prmt(vb1, 0x64646464u, 0x4240u),
+                                        prmt(vb0, 0x64646464u, 0x4341u), prmt(vb1, 0x64646464u, 0x4341u),
+                                        xb[pl][4 * sb + 2], xb[pl][4 * sb + 3]);
+                            }
+                            const float d0 = fp16_bits_to_f32(static_cast<uint16_t>(dr[0]));
+                            const float d1 = fp16_bits_to_f32(static_cast<uint16_t>(dr[1]));
+                            float *tt = tot[m][mt];
+                            tt[0] = fmaf(d0, acc[0], fmaf(-1152.0f * d0, Xa[sb], tt[0]));
+                            tt[1] = fmaf(d0, acc[1], fmaf(-1152.0f * d0, Xb[sb], tt[1]));
+                            tt[2] = fmaf(d1, acc[2], fmaf(-1152.0f * d1, Xa[sb], tt[2]));
+                            tt[3] = fmaf(d1, acc[3], fmaf(-1152.0f * d1, Xb[sb], tt[3]));
+                        }
+                }
+            }
+            __syncwarp(); // every lane is done with the slot before it is refilled
+            issue(j + P);
+        }
+        // ---- per-tile epilogue: fixed-order reduction over the NW warps
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                s_red[warp][m][16 * mt + g][2 * c] = tot[m][mt][0];
+                s_red[warp][m][16 * mt + g][2 * c + 1] = tot[m][mt][1];
+                s_red[warp][m][16 * mt + g + 8][2 * c] = tot[m][mt][2];
+                s_red[warp][m][16 * mt + g + 8][2 * c + 1] = tot[m][mt][3];
+            }
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < TILE * 8; idx += NW * 32) {
+            const int r = idx >> 3, col = idx & 7;
+            const uint32_t row = tl.row0 + r;
+            if (!tile_ok || static_cast<uint32_t>(col) >= tl.ncol || row >= p.out_dim) continue;
+            float v[NMAT];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                float sum = 0.0f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) sum += s_red[w][m][r][col];
+                v[m] = sum;
+            }
+            const float out = (MODE == GEMV_GATE_UP) ? swiglu_ref(v[0], v[NMAT - 1]) : v[0];
+            p.y[static_cast<uint64_t>(tl.start + col) * p.out_dim + row] = out;
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+}
+
+} // namespace fmb

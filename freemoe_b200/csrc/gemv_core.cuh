@@ -246,7 +246,7 @@ __device__ __forceinline__ void q8_load(const uint8_t *row, uint32_t blk, int c,
                                         uint32_t &wb, uint32_t &dbits) {
     const uint8_t *s = row + 34ull * blk;
     dbits = ldg_nc_u16(s);
-    if ((blk & 1u) == 0u) {
+    if ((reinterpret_cast<uintptr_t>(s) & 2u) == 0u) {
         // block start is 4-byte aligned: codes start 2 bytes into a word
         const uint32_t W0 = ldg_nc_u32(s + 8 * c);
         const uint32_t W1 = ldg_nc_u32(s + 8 * c + 4);

@@ -28,6 +28,13 @@ template <int MODE>
 int launch_qgemv(const QGemvParams &prm, int planes, uint32_t grid_y, uint32_t grid_z,
                  cudaStream_t s);
 int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what);
+bool staged_shape(uint32_t type_id, uint32_t in_dim);
+int xplane_layout(uint32_t type_id);
+int launch_xplanes_staged(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, int layout,
+                          __half *xh, __half *xl, float *xs, cudaStream_t s);
+template <int MODE>
+int launch_qgemv_stream(const QGemvParams &prm, int planes, uint32_t tok_tiles, uint32_t experts,
+                     cudaStream_t s);
 
 namespace {
 
@@ -128,9 +135,12 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     float *as = reinterpret_cast<float *>(ws + L.as);
     float *part = reinterpret_cast<float *>(ws + L.part);
     const uint32_t P = a->tokens * a->top_k;
+    int mark_rc = FM_STATUS_OK;
     auto mark = [&](int i) {
-        if (a->stage_events && a->stage_events[i])
-            cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s);
+        if (a->stage_events && a->stage_events[i] && mark_rc == FM_STATUS_OK) {
+            const cudaError_t err = cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), s);
+            if (err != cudaSuccess) mark_rc = cuda_status(err, "stage event record");
+        }
     };
 
     mark(0);
@@ -141,9 +151,15 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
     mark(2);
     const int xplanes = a->x_dtype == FM_X_F32 ? 2 : 1;
-    if ((rc = launch_xplanes(a->x, a->x_dtype, a->tokens, a->d_model, xh, xplanes > 1 ? xl : nullptr,
-                             xs, s)))
-        return rc;
+    // Expert slots come from cudaMalloc-class allocations (256-byte aligned);
+    // the staged kernels also re-check each slot base on the device.
+    const bool gu_staged = staged_shape(a->gate_type, a->d_model);
+    const bool dn_staged = staged_shape(a->down_type, a->ffn);
+    rc = gu_staged ? launch_xplanes_staged(a->x, a->x_dtype, a->tokens, a->d_model,
+                                           xplane_layout(a->gate_type), xh, xplanes > 1 ? xl : nullptr, xs, s)
+                   : launch_xplanes(a->x, a->x_dtype, a->tokens, a->d_model, xh, xplanes > 1 ? xl : nullptr,
+                                    xs, s);
+    if (rc) return rc;
     mark(3);
 
     const uint32_t tok_tiles = (a->tokens + 7) / 8; // an expert holds at most `tokens` pairs
@@ -163,10 +179,14 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     gu.xs = xs;
     gu.y = act;
     gu.status = device_status_word();
-    if ((rc = launch_qgemv<GEMV_GATE_UP>(gu, xplanes, tok_tiles, a->experts, s))) return rc;
+    rc = gu_staged ? launch_qgemv_stream<GEMV_GATE_UP>(gu, xplanes, tok_tiles, a->experts, s)
+                   : launch_qgemv<GEMV_GATE_UP>(gu, xplanes, tok_tiles, a->experts, s);
+    if (rc) return rc;
     mark(4);
 
-    if ((rc = launch_xplanes(act, FM_X_F32, P, a->ffn, ah, al, as, s))) return rc;
+    rc = dn_staged ? launch_xplanes_staged(act, FM_X_F32, P, a->ffn, xplane_layout(a->down_type), ah, al, as, s)
+                   : launch_xplanes(act, FM_X_F32, P, a->ffn, ah, al, as, s);
+    if (rc) return rc;
     mark(5);
 
     QGemvParams dn{};
@@ -185,7 +205,9 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     dn.xs = as;
     dn.y = part;
     dn.status = device_status_word();
-    if ((rc = launch_qgemv<GEMV_DOWN>(dn, 2, tok_tiles, a->experts, s))) return rc;
+    rc = dn_staged ? launch_qgemv_stream<GEMV_DOWN>(dn, 2, tok_tiles, a->experts, s)
+                   : launch_qgemv<GEMV_DOWN>(dn, 2, tok_tiles, a->experts, s);
+    if (rc) return rc;
     mark(6);
 
     const uint64_t n = static_cast<uint64_t>(a->tokens) * a->d_model;
@@ -198,6 +220,7 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     if (a->weights_out)
         cudaMemcpyAsync(a->weights_out, weights, static_cast<uint64_t>(P) * 4,
                         cudaMemcpyDeviceToDevice, s);
+    if (mark_rc) return mark_rc;
     return check_launch("MoE output copies");
 }
 

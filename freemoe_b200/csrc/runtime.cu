@@ -137,6 +137,34 @@ int fmcuda_malloc(uint64_t bytes, void **ptr) {
     return FM_STATUS_OK;
 }
 
+int fmcuda_malloc_managed(uint64_t bytes, void **ptr) {
+    if (!ptr) return set_error(FM_STATUS_INVALID_ARGUMENT, "null output pointer");
+    *ptr = nullptr;
+    if (bytes == 0) return set_error(FM_STATUS_INVALID_ARGUMENT, "zero-byte allocation");
+    int dev = 0;
+    FM_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    void *p = nullptr;
+    cudaError_t err = cudaMallocManaged(&p, bytes, cudaMemAttachGlobal);
+    if (err != cudaSuccess) {
+        (void)cudaGetLastError();
+        return cuda_status(err, "cudaMallocManaged");
+    }
+    cudaMemLocation loc{};
+    loc.type = cudaMemLocationTypeDevice;
+    loc.id = dev;
+    // Advice is a placement hint; a device that declines it still works.
+    if (cudaMemAdvise(p, bytes, cudaMemAdviseSetPreferredLocation, loc) != cudaSuccess)
+        (void)cudaGetLastError();
+    err = cudaMemset(p, 0, bytes);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(err, "managed zero-fill");
+    }
+    *ptr = p;
+    return FM_STATUS_OK;
+}
+
 int fmcuda_free(void *ptr) {
     if (!ptr) return FM_STATUS_OK;
     FM_CUDA(cudaFree(ptr), "cudaFree");
@@ -184,6 +212,21 @@ int fmcuda_event_create(void **event) {
     cudaEvent_t e;
     FM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
     *event = e;
+    return FM_STATUS_OK;
+}
+
+int fmcuda_event_create_timing(void **event) {
+    if (!event) return set_error(FM_STATUS_INVALID_ARGUMENT, "null event pointer");
+    cudaEvent_t e;
+    FM_CUDA(cudaEventCreate(&e), "cudaEventCreate");
+    *event = e;
+    return FM_STATUS_OK;
+}
+
+int fmcuda_event_elapsed_ms(void *start, void *end, float *ms) {
+    if (!start || !end || !ms) return set_error(FM_STATUS_INVALID_ARGUMENT, "bad elapsed-time query");
+    FM_CUDA(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(end)),
+            "cudaEventElapsedTime");
     return FM_STATUS_OK;
 }
 

@@ -78,6 +78,12 @@ int fmcuda_device_info_get(int32_t device, fmcuda_device_info *out);
 /* Backend::allocate (include/fm/backend.hpp:152): HBM, 256-byte aligned,
  * zero-filled like CpuBackend::allocate (src/backend.cpp:240-256). */
 int fmcuda_malloc(uint64_t bytes, void **ptr);
+/* Backend::allocate for buffers that the unchanged engine also reads on the
+ * host (fixed weights read by Engine::weights, src/engine.cpp:306-346; expert
+ * slots read back for checksums, src/residency.cpp:703-714): managed memory
+ * whose preferred location is this device's HBM, zero-filled.  Freed with
+ * fmcuda_free. */
+int fmcuda_malloc_managed(uint64_t bytes, void **ptr);
 /* DeviceBuffer::cleanup (include/fm/backend.hpp:70-110). */
 int fmcuda_free(void *ptr);
 /* Pinned host staging for uploads (host side of Backend::upload). */
@@ -90,6 +96,10 @@ int fmcuda_stream_sync(void *stream);
 int fmcuda_event_create(void **event);
 int fmcuda_event_destroy(void *event);
 int fmcuda_event_record(void *event, void *stream);
+/* Events with timing enabled, and the milliseconds between two recorded ones
+ * (cudaEventElapsedTime), for live per-kernel timing. */
+int fmcuda_event_create_timing(void **event);
+int fmcuda_event_elapsed_ms(void *start, void *end, float *ms);
 
 /* Backend::upload (include/fm/backend.hpp:153): enqueue a host->device copy on
  * `stream` and record `event` after it (the fence).  `src` should be pinned

@@ -1,0 +1,286 @@
+// engine_harness.cpp -- drives the reference's own, unmodified fm::Engine.
+//
+// TEST INFRASTRUCTURE ONLY.  Linked (by oracle/Makefile, target `engine`)
+// with the reference's sources, the CUDA fm::Backend adapter
+// (freemoe_b200/backend/) and libfreemoe_b200.so into
+// oracle/_ref/libfmengine.so.  The same engine code runs once with
+// --backend cpu and once with --backend gpu; the tests compare greedy ids,
+// logits and routing between the two.
+//
+// fme_write_tiny writes the freemoe-tiny-v1 fixture as a GGUF v3 file per the
+// public GGUF layout (header, key/value metadata, tensor directory, aligned
+// data), with the metadata the strict native adapter checks
+// (src/gguf.cpp:2990-3213) and FNV-1a expert checksums over each expert's
+// gate || up || down payload (include/fm/common.hpp:73-85).
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "fm/common.hpp"
+#include "fm/engine.hpp"
+
+namespace {
+
+thread_local std::string g_error;
+
+// ---- minimal GGUF v3 writer -------------------------------------------------
+enum : uint32_t { GT_U32 = 4, GT_F32 = 6, GT_BOOL = 7, GT_STRING = 8, GT_ARRAY = 9, GT_U64 = 10 };
+
+struct Out {
+    std::vector<uint8_t> b;
+    void u32(uint32_t v) { b.insert(b.end(), reinterpret_cast<uint8_t *>(&v), reinterpret_cast<uint8_t *>(&v) + 4); }
+    void u64(uint64_t v) { b.insert(b.end(), reinterpret_cast<uint8_t *>(&v), reinterpret_cast<uint8_t *>(&v) + 8); }
+    void f32(float v) { b.insert(b.end(), reinterpret_cast<uint8_t *>(&v), reinterpret_cast<uint8_t *>(&v) + 4); }
+    void str(const std::string &s) {
+        u64(s.size());
+        b.insert(b.end(), s.begin(), s.end());
+    }
+};
+
+struct Kv {
+    std::string key;
+    uint32_t type;
+    uint64_t u = 0;
+    float f = 0.0f;
+    bool flag = false;
+    std::string s;
+    uint32_t elem = 0;
+    std::vector<uint64_t> u64s;
+    std::vector<std::string> strs;
+};
+
+struct Tensor {
+    std::string name;
+    std::vector<uint64_t> dims;
+    std::vector<float> data;
+};
+
+uint64_t fnv(const std::string &s) { return fm::fnv1a64(s.data(), s.size()); }
+
+// N(0, std) values of one tensor: mt19937_64 seeded with seed ^ fnv(name),
+// Box-Muller pairs.
+std::vector<float> gaussian(uint64_t seed, const std::string &name, size_t n, double std_dev,
+                            double mean = 0.0) {
+    std::mt19937_64 gen(seed ^ fnv(name));
+    std::vector<float> out(n);
+    const double two_pi = 6.283185307179586;
+    for (size_t i = 0; i < n; i += 2) {
+        const double u1 = (static_cast<double>(gen() >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+        const double u2 = static_cast<double>(gen() >> 11) * (1.0 / 9007199254740992.0);
+        const double r = std::sqrt(-2.0 * std::log(u1));
+        out[i] = static_cast<float>(mean + std_dev * r * std::cos(two_pi * u2));
+        if (i + 1 < n) out[i + 1] = static_cast<float>(mean + std_dev * r * std::sin(two_pi * u2));
+    }
+    return out;
+}
+
+std::string layer_name(uint32_t l, const char *suffix) { return "blk." + std::to_string(l) + "." + suffix; }
+
+} // namespace
+
+extern "C" {
+
+const char *fme_last_error(void) { return g_error.c_str(); }
+
+// freemoe-tiny-v1: F32 throughout, weights N(0, std) from `seed`, RMSNorm
+// scales 1 + N(0, std).  vocab = 256 bytes + BOS (256) + EOS (257).
+int fme_write_tiny(const char *path, uint64_t seed, uint32_t layers, uint32_t hidden, uint32_t heads,
+                   uint32_t experts, uint32_t ffn, uint32_t top_k, uint32_t vocab, uint32_t context,
+                   float std_dev) {
+    try {
+        const uint32_t head_dim = hidden / heads;
+        std::vector<Tensor> tensors;
+        auto add = [&](const std::string &name, std::vector<uint64_t> dims, std::vector<float> v) {
+            tensors.push_back({name, std::move(dims), std::move(v)});
+        };
+        const uint64_t H = hidden, V = vocab, I = ffn, E = experts;
+        add("token_embd.weight", {H, V}, gaussian(seed, "token_embd.weight", H * V, std_dev));
+        add("output.weight", {H, V}, gaussian(seed, "output.weight", H * V, std_dev));
+        add("output_norm.weight", {H}, gaussian(seed, "output_norm.weight", H, std_dev, 1.0));
+        for (uint32_t l = 0; l < layers; ++l) {
+            for (const char *s : {"attn_norm.weight", "ffn_norm.weight"})
+                add(layer_name(l, s), {H}, gaussian(seed, layer_name(l, s), H, std_dev, 1.0));
+            for (const char *s : {"attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight"})
+                add(layer_name(l, s), {H, H}, gaussian(seed, layer_name(l, s), H * H, std_dev));
+            add(layer_name(l, "ffn_router.weight"), {H, E},
+                gaussian(seed, layer_name(l, "ffn_router.weight"), H * E, std_dev));
+            add(layer_name(l, "ffn_gate_exps.weight"), {H, I, E},
+                gaussian(seed, layer_name(l, "ffn_gate_exps.weight"), H * I * E, std_dev));
+            add(layer_name(l, "ffn_up_exps.weight"), {H, I, E},
+                gaussian(seed, layer_name(l, "ffn_up_exps.weight"), H * I * E, std_dev));
+            add(layer_name(l, "ffn_down_exps.weight"), {I, H, E},
+                gaussian(seed, layer_name(l, "ffn_down_exps.weight"), I * H * E, std_dev));
+        }
+        // per-expert checksums over gate || up || down slices
+        std::vector<uint64_t> sums;
+        for (uint32_t l = 0; l < layers; ++l) {
+            const Tensor *g = nullptr, *u = nullptr, *d = nullptr;
+            for (const auto &t : tensors) {
+                if (t.name == layer_name(l, "ffn_gate_exps.weight")) g = &t;
+                if (t.name == layer_name(l, "ffn_up_exps.weight")) u = &t;
+                if (t.name == layer_name(l, "ffn_down_exps.weight")) d = &t;
+            }
+            const size_t stride = static_cast<size_t>(H * I);
+            for (uint32_t e = 0; e < experts; ++e) {
+                std::vector<uint8_t> payload;
+                for (const Tensor *t : {g, u, d}) {
+                    const uint8_t *p = reinterpret_cast<const uint8_t *>(t->data.data() + e * stride);
+                    payload.insert(payload.end(), p, p + stride * 4);
+                }
+                sums.push_back(fm::fnv1a64(payload));
+            }
+        }
+        std::vector<Kv> kv;
+        auto s = [&](const char *k, const std::string &v) { Kv x{k, GT_STRING}; x.s = v; kv.push_back(x); };
+        auto u = [&](const char *k, uint64_t v) { Kv x{k, GT_U32}; x.u = v; kv.push_back(x); };
+        auto f = [&](const char *k, float v) { Kv x{k, GT_F32}; x.f = v; kv.push_back(x); };
+        s("general.architecture", "freemoe-tiny");
+        s("general.name", "freemoe-tiny-v1 b200 parity fixture");
+        u("general.alignment", 32);
+        u("general.file_type", 0);
+        s("freemoe.adapter", "freemoe-tiny-v1");
+        s("freemoe.model_kind", "moe");
+        u("freemoe.hidden_size", hidden);
+        u("freemoe.intermediate_size", ffn);
+        u("freemoe.num_hidden_layers", layers);
+        u("freemoe.num_attention_heads", heads);
+        u("freemoe.num_key_value_heads", heads);
+        u("freemoe.head_dim", head_dim);
+        u("freemoe.vocab_size", vocab);
+        u("freemoe.max_context_length", context);
+        f("freemoe.rms_norm_epsilon", 1e-5f);
+        f("freemoe.rope_theta", 10000.0f);
+        s("freemoe.rope_mode", "half");
+        s("freemoe.tokenizer_model", "freemoe.byte-v1");
+        s("freemoe.router_operation", "linear-topk-softmax-v1");
+        { Kv x{"freemoe.shared_expert", GT_BOOL}; x.flag = false; kv.push_back(x); }
+        s("freemoe.expert_layout", "stacked-f32");
+        u("freemoe.expert_count", experts);
+        u("freemoe.expert_top_k", top_k);
+        { Kv x{"freemoe.expert_checksums", GT_ARRAY}; x.elem = GT_U64; x.u64s = sums; kv.push_back(x); }
+        s("tokenizer.ggml.model", "freemoe.byte-v1");
+        u("tokenizer.ggml.bos_token_id", 256);
+        u("tokenizer.ggml.eos_token_id", 257);
+        {
+            Kv x{"tokenizer.ggml.tokens", GT_ARRAY};
+            x.elem = GT_STRING;
+            for (uint32_t i = 0; i < vocab; ++i) {
+                char buf[16];
+                if (i < 256) std::snprintf(buf, sizeof(buf), "<0x%02X>", i);
+                else if (i == 256) std::snprintf(buf, sizeof(buf), "<bos>");
+                else if (i == 257) std::snprintf(buf, sizeof(buf), "<eos>");
+                else std::snprintf(buf, sizeof(buf), "<pad%u>", i - 258);
+                x.strs.push_back(buf);
+            }
+            kv.push_back(x);
+        }
+        s("tokenizer.chat_template", "raw-v1");
+
+        Out o;
+        o.b.insert(o.b.end(), {'G', 'G', 'U', 'F'});
+        o.u32(3);
+        o.u64(tensors.size());
+        o.u64(kv.size());
+        for (const Kv &x : kv) {
+            o.str(x.key);
+            o.u32(x.type);
+            switch (x.type) {
+            case GT_STRING: o.str(x.s); break;
+            case GT_U32: o.u32(static_cast<uint32_t>(x.u)); break;
+            case GT_F32: o.f32(x.f); break;
+            case GT_BOOL: o.b.push_back(x.flag ? 1 : 0); break;
+            case GT_ARRAY:
+                o.u32(x.elem);
+                if (x.elem == GT_U64) {
+                    o.u64(x.u64s.size());
+                    for (uint64_t v : x.u64s) o.u64(v);
+                } else {
+                    o.u64(x.strs.size());
+                    for (const auto &v : x.strs) o.str(v);
+                }
+                break;
+            }
+        }
+        uint64_t rel = 0;
+        std::vector<uint64_t> offs;
+        for (const Tensor &t : tensors) {
+            rel = (rel + 31) & ~uint64_t(31);
+            offs.push_back(rel);
+            rel += t.data.size() * 4;
+        }
+        for (size_t i = 0; i < tensors.size(); ++i) {
+            o.str(tensors[i].name);
+            o.u32(static_cast<uint32_t>(tensors[i].dims.size()));
+            for (uint64_t d : tensors[i].dims) o.u64(d);
+            o.u32(0); // F32
+            o.u64(offs[i]);
+        }
+        const size_t data_at = (o.b.size() + 31) & ~size_t(31);
+        o.b.resize(data_at, 0);
+        for (size_t i = 0; i < tensors.size(); ++i) {
+            o.b.resize(data_at + offs[i], 0);
+            const uint8_t *p = reinterpret_cast<const uint8_t *>(tensors[i].data.data());
+            o.b.insert(o.b.end(), p, p + tensors[i].data.size() * 4);
+        }
+        std::ofstream fout(path, std::ios::binary);
+        fout.write(reinterpret_cast<const char *>(o.b.data()), static_cast<std::streamsize>(o.b.size()));
+        if (!fout) {
+            g_error = "cannot write fixture";
+            return 11;
+        }
+        return 0;
+    } catch (const fm::Error &e) {
+        g_error = e.what();
+        return static_cast<int>(e.code);
+    }
+}
+
+// Runs one prompt through fm::Engine with the CPU (backend 0) or the GPU
+// (backend 2) backend.  Outputs: generated ids, the prefill logits, and the
+// routing events flattened as (token_index, layer, expert ids...).
+int fme_run(const char *path, int backend, int scalar_kernels, const uint8_t *prompt, uint32_t prompt_len,
+            uint32_t n_gen, uint32_t cache_slots, int32_t *ids_out, uint32_t ids_cap, uint32_t *n_ids,
+            float *logits_out, uint32_t logits_cap, uint32_t *n_logits, uint32_t *routing_out,
+            uint32_t routing_cap, uint32_t *n_routing, char *metrics_out, uint32_t metrics_cap) {
+    try {
+        fm::RunConfig cfg;
+        cfg.model_path = path;
+        cfg.backend.kind = backend == 2 ? fm::BackendKind::PhysicalGPU : fm::BackendKind::ScalarCPU;
+        if (scalar_kernels) cfg.backend.kernel_isa = fm::KernelIsa::Scalar;
+        cfg.backend.kernel_threads = 1;
+        cfg.budget.requested_slots = cache_slots;
+        cfg.t_wait_ms = 5000;
+        fm::Engine engine(cfg);
+        engine.initialize();
+        fm::PromptResult r =
+            engine.run_prompt(std::string(reinterpret_cast<const char *>(prompt), prompt_len), n_gen);
+        *n_ids = static_cast<uint32_t>(r.generated_ids.size());
+        for (uint32_t i = 0; i < *n_ids && i < ids_cap; ++i) ids_out[i] = r.generated_ids[i];
+        *n_logits = static_cast<uint32_t>(r.prefill_logits.size());
+        for (uint32_t i = 0; i < *n_logits && i < logits_cap; ++i) logits_out[i] = r.prefill_logits[i];
+        uint32_t n = 0;
+        for (const auto &ev : r.routing) {
+            if (n + 2 + ev.experts.size() > routing_cap) break;
+            routing_out[n++] = static_cast<uint32_t>(ev.token_index);
+            routing_out[n++] = ev.layer;
+            for (uint32_t e : ev.experts) routing_out[n++] = e;
+        }
+        *n_routing = n;
+        const std::string m = engine.backend().metrics_json().dump();
+        if (metrics_out && metrics_cap) {
+            std::snprintf(metrics_out, metrics_cap, "%s", m.c_str());
+        }
+        engine.release_runtime();
+        return 0;
+    } catch (const fm::Error &e) {
+        g_error = e.what();
+        return static_cast<int>(e.code);
+    }
+}
+
+} // extern "C"
