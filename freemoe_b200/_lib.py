@@ -8,7 +8,10 @@ from __future__ import annotations
 import ctypes as C
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libfreemoe_b200.so"
+import os
+
+# FREEMOE_B200_LIB selects another build of the same library (same ABI).
+LIB_PATH = Path(os.environ.get("FREEMOE_B200_LIB") or Path(__file__).resolve().parent / "libfreemoe_b200.so")
 
 # fm::ErrorCode ordinals (include/fm/common.hpp:27-57 of the reference)
 ERROR_NAMES = {

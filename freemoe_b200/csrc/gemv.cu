@@ -9,6 +9,21 @@
 #include "gemv_kernels.cuh"
 #include "gemv_async.cuh"
 
+// Tile shape of the streamed GEMV: MT m-tiles of 16 rows per tile, NW warps
+// per CTA splitting K, ring depth P (two matrices: gate/up) or P1 (one).
+#ifndef FMB_GEMV_MT
+#define FMB_GEMV_MT 2
+#endif
+#ifndef FMB_GEMV_NW
+#define FMB_GEMV_NW 4
+#endif
+#ifndef FMB_GEMV_P2
+#define FMB_GEMV_P2 2
+#endif
+#ifndef FMB_GEMV_P1
+#define FMB_GEMV_P1 4
+#endif
+
 namespace fmb {
 
 // ---------------------------------------------------------------------------
@@ -235,7 +250,7 @@ int sm_count() {
 
 template <int TYPE, int PL, int MODE, int P>
 int launch_async_inst(const QGemvParams &prm, uint32_t tok_tiles, uint32_t experts, cudaStream_t s) {
-    constexpr int MT = 2, NW = 4;
+    constexpr int MT = FMB_GEMV_MT, NW = FMB_GEMV_NW;
     constexpr int NMAT = MODE == GEMV_GATE_UP ? 2 : 1;
     using G = StageGeom<TYPE, MT, NMAT>;
     constexpr size_t smem = static_cast<size_t>(NW) * P * G::BYTES;
@@ -252,6 +267,8 @@ int launch_async_inst(const QGemvParams &prm, uint32_t tok_tiles, uint32_t exper
     int per_sm = 0;
     cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NW * 32, smem);
     if (err != cudaSuccess || per_sm < 1) per_sm = 1;
+    if (prm.out_dim < static_cast<uint32_t>(G::TILE)) // too few rows for one staged tile
+        return launch_qgemv<MODE>(prm, PL, tok_tiles, experts, s);
     const uint32_t row_tiles = (prm.out_dim + G::TILE - 1) / G::TILE;
     uint32_t grid = static_cast<uint32_t>(per_sm * sm_count());
     if (MODE == GEMV_PLAIN) grid = std::min<uint32_t>(grid, row_tiles * tok_tiles);
@@ -261,12 +278,11 @@ int launch_async_inst(const QGemvParams &prm, uint32_t tok_tiles, uint32_t exper
 }
 } // namespace
 
-// Ring depth P per warp: as many K steps in flight as fit in ~72 KB per CTA
-// (two CTAs per SM), at least two.
+// Ring depth P per warp (K steps in flight per warp).
 template <int MODE>
 int launch_qgemv_stream(const QGemvParams &prm, int planes, uint32_t tok_tiles, uint32_t experts,
                         cudaStream_t s) {
-    constexpr int PQ4 = MODE == GEMV_GATE_UP ? 2 : 4; // 9 KB / 4.5 KB slots
+    constexpr int PQ4 = MODE == GEMV_GATE_UP ? FMB_GEMV_P2 : FMB_GEMV_P1;
     if (prm.type_id == FM_TYPE_Q4_K)
         return planes == 1 ? launch_async_inst<FM_TYPE_Q4_K, 1, MODE, PQ4>(prm, tok_tiles, experts, s)
                            : launch_async_inst<FM_TYPE_Q4_K, 2, MODE, PQ4>(prm, tok_tiles, experts, s);

@@ -89,8 +89,12 @@ struct StageGeom {
 
 constexpr int kMaxGroupExperts = 1024;
 
+#ifndef FMB_GEMV_MINB
+#define FMB_GEMV_MINB 1
+#endif
+
 template <int TYPE, int MT, int NW, int PLANES, int MODE, int P>
-__global__ void __launch_bounds__(NW * 32)
+__global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
     qgemv_async_kernel(const QGemvParams p, uint32_t row_tiles, uint32_t tok_tiles, uint32_t experts) {
     constexpr int NMAT = (MODE == GEMV_GATE_UP) ? 2 : 1;
     using G = StageGeom<TYPE, MT, NMAT>;
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(NW * 32)
     auto tile_of = [&](uint32_t i) -> Tile {
         Tile tl;
         const uint32_t a = blockIdx.x + i * gridDim.x;
-        tl.row0 = (a % row_tiles) * TILE;
+        tl.row0 = min((a % row_tiles) * TILE, p.out_dim - TILE); // last tile overlaps the previous one
         const uint32_t q = a / row_tiles;
         if (MODE == GEMV_PLAIN) {
             tl.e = 0;
@@ -165,33 +169,49 @@ __global__ void __launch_bounds__(NW * 32)
         return tl;
     };
 
-    // issue the copies of this warp's item j (tile j / nw, K step w + NW (j % nw))
-    auto issue = [&](uint32_t j) {
-        if (nw && j < my_tiles * nw) {
-            const Tile tl = tile_of(j / nw);
-            const uint32_t b = warp + NW * (j % nw);
-            if (tl.base && (reinterpret_cast<uintptr_t>(tl.base) & 15u) == 0) {
-                uint8_t *slot = ring + (j % P) * G::BYTES;
+    // ---- copy issue.  A ring slot holds the tile rows back to back (RB bytes
+    // each), so chunk q of a slot is 16 bytes at q * 16 and lane l copies
+    // chunks l, l + 32, ...: every cp.async warp instruction moves 512
+    // contiguous slot bytes, drawn from 3-4 consecutive row pieces.  The
+    // global offset of each of the lane's chunks relative to the tile's first
+    // row is fixed for the whole kernel (row_bytes and the matrix offsets do
+    // not change), so it is computed once; a cursor walks this warp's items
+    // (tile, K step) without divisions.
+    constexpr int ROWS = NMAT * TILE, NCH = ROWS * G::CHUNKS, NU = (NCH + 31) / 32;
+    uint32_t gofs[NU];
 #pragma unroll
-                for (int u = 0; u < (NMAT * TILE * G::CHUNKS + 31) / 32; ++u) {
-                    const int qd = lane + 32 * u;
-                    if (qd < NMAT * TILE * G::CHUNKS) {
-                        const int r = qd / G::CHUNKS, part = qd % G::CHUNKS;
-                        const int m = r / TILE, rr = r % TILE;
-                        const uint32_t row = min(tl.row0 + rr, p.out_dim - 1);
-                        const uint8_t *src = tl.base + (m ? p.w_off1 : p.w_off0) +
-                                             static_cast<uint64_t>(row) * p.row_bytes +
-                                             static_cast<uint64_t>(b) * G::RB + part * 16;
-                        cp_async16(slot + r * G::RB + part * 16, src);
-                    }
-                }
+    for (int u = 0; u < NU; ++u) {
+        const int q = lane + 32 * u;
+        const int r = q / G::CHUNKS, part = q % G::CHUNKS;
+        const int m = r / TILE, rr = r % TILE;
+        gofs[u] = static_cast<uint32_t>((m ? p.w_off1 : p.w_off0) + static_cast<uint64_t>(rr) * p.row_bytes) +
+                  part * 16;
+    }
+    const uint8_t *cur_base = nullptr; // first row of the current tile (matrix 0)
+    uint32_t cur_tile = 0xFFFFFFFFu, cur_jj = 0, issued = 0;
+    const uint32_t my_items = my_tiles * nw;
+    auto issue = [&]() {
+        if (issued < my_items) {
+            if (cur_jj == 0) {
+                cur_tile = cur_tile == 0xFFFFFFFFu ? 0u : cur_tile + 1;
+                const Tile tl = tile_of(cur_tile);
+                const bool ok = tl.base && (reinterpret_cast<uintptr_t>(tl.base) & 15u) == 0;
+                cur_base = ok ? tl.base + static_cast<uint64_t>(tl.row0) * p.row_bytes : nullptr;
             }
+            if (cur_base) {
+                const uint8_t *src = cur_base + static_cast<uint64_t>(warp + NW * cur_jj) * G::RB;
+                uint8_t *dst = ring + (issued % P) * G::BYTES + lane * 16;
+#pragma unroll
+                for (int u = 0; u < NU; ++u)
+                    if (lane + 32 * u < NCH) cp_async16(dst + 512 * u, src + gofs[u]);
+            }
+            if (++cur_jj == nw) cur_jj = 0;
+            ++issued;
         }
         cp_async_commit(); // one group per item, even an empty one
     };
 
-#pragma unroll
-    for (int j = 0; j < P; ++j) issue(j);
+    for (int j = 0; j < P; ++j) issue();
 
     for (uint32_t i = 0; i < my_tiles; ++i) {
         const Tile tl = tile_of(i);
@@ -319,7 +339,7 @@ __global__ void __launch_bounds__(NW * 32)
                 }
             }
             __syncwarp(); // every lane is done with the slot before it is refilled
-            issue(j + P);
+            issue();
         }
         // ---- per-tile epilogue: fixed-order reduction over the NW warps
 #pragma unroll

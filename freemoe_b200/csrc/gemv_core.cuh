@@ -36,9 +36,11 @@ namespace fmb {
 
 // ---- PTX wrappers ---------------------------------------------------------
 
+// Not volatile: the MMA has no side effects, and leaving the compiler free to
+// interleave independent accumulator chains hides the MMA latency.
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -208,7 +210,8 @@ __device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1
                                                 const uint32_t (&xm)[2], float (&tot)[4]) {
     const Q4kRowConsts r0 = q4k_row_consts(h0, c);
     const Q4kRowConsts r1 = q4k_row_consts(h1, c);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // four independent accumulator chains (low / high nibbles x even / odd words)
+    float acc[4][4] = {};
     const uint32_t w0[8] = {q0[0].x, q0[0].y, q0[0].z, q0[0].w, q0[1].x, q0[1].y, q0[1].z, q0[1].w};
     const uint32_t w1[8] = {q1[0].x, q1[0].y, q1[0].z, q1[0].w, q1[1].x, q1[1].y, q1[1].z, q1[1].w};
 #pragma unroll
@@ -220,7 +223,7 @@ __device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1
         const uint32_t a2 = hfma2_u32(lop_and_or(s0, 0x000F000Fu, 0x64006400u), r0.hs_lo, r0.hb_lo);
         const uint32_t a3 = hfma2_u32(lop_and_or(s1, 0x000F000Fu, 0x64006400u), r1.hs_lo, r1.hb_lo);
 #pragma unroll
-        for (int p = 0; p < PLANES; ++p) mma_f16(acc, a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
+        for (int p = 0; p < PLANES; ++p) mma_f16(acc[i & 1], a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
         // high nibbles: sub-block 2c+1
         const uint32_t e0 = hfma2_u32(lop_and_or(w0[i], 0x00F000F0u, 0x64006400u), r0.hs_hi, r0.hb_hi);
         const uint32_t e1 = hfma2_u32(lop_and_or(w1[i], 0x00F000F0u, 0x64006400u), r1.hs_hi, r1.hb_hi);
@@ -228,15 +231,17 @@ __device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1
         const uint32_t e3 = hfma2_u32(lop_and_or(s1, 0x00F000F0u, 0x64006400u), r1.hs_hi, r1.hb_hi);
 #pragma unroll
         for (int p = 0; p < PLANES; ++p)
-            mma_f16(acc, e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);
+            mma_f16(acc[2 + (i & 1)], e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);
     }
     float accm[4] = {0.f, 0.f, 0.f, 0.f};
     mma_f16(accm, r0.mins, r1.mins, 0u, 0u, xm[0], 0u);
     mma_f16(accm, r0.mins, r1.mins, 0u, 0u, xm[1], 0u);
-    tot[0] = fmaf(r0.d, acc[0], fmaf(-r0.dmin, accm[0], tot[0]));
-    tot[1] = fmaf(r0.d, acc[1], fmaf(-r0.dmin, accm[1], tot[1]));
-    tot[2] = fmaf(r1.d, acc[2], fmaf(-r1.dmin, accm[2], tot[2]));
-    tot[3] = fmaf(r1.d, acc[3], fmaf(-r1.dmin, accm[3], tot[3]));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float a = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+        const float d = e < 2 ? r0.d : r1.d, dm = e < 2 ? r0.dmin : r1.dmin;
+        tot[e] = fmaf(d, a, fmaf(-dm, accm[e], tot[e]));
+    }
 }
 
 // ---- Q8_0 -----------------------------------------------------------------
