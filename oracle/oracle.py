@@ -35,7 +35,7 @@ def build(ref: bool | None = None) -> None:
     if ref is None:
         ref = REF_TREE.exists()
     if ref:
-        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref", f"REF={REF_TREE}"], check=True)
+        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref", "engine", f"REF={REF_TREE}"], check=True)
 
 
 def _ptr(a: np.ndarray | None):
