@@ -27,6 +27,7 @@ ERROR_NAMES = {
 }
 
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K = 0, 8, 12
+MOE_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024  # FM_MOE_NOALLOC_SCRATCH_BYTES
 X_F32, X_BF16 = 0, 1
 ORDER_ANY, ORDER_SCALAR, ORDER_AVX2 = 0, 1, 2
 
@@ -119,6 +120,7 @@ SIGNATURES = [
     ("fmcuda_group", C.c_int, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _P]),
     ("fmcuda_moe_workspace_bytes", C.c_int, [_U32, _U32, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
     ("fmcuda_moe_block", C.c_int, [C.POINTER(MoeArgs), _P, _U64, _P]),
+    ("fmcuda_moe_block_noalloc", C.c_int, [C.POINTER(MoeArgs), _P]),
     ("fmcuda_synth_weights", C.c_int, [_U32, _P, _U64, _U32, _U64, _F, _P]),
 ]
 

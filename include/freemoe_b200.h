@@ -213,6 +213,25 @@ int fmcuda_moe_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k
 int fmcuda_moe_block(const fmcuda_moe_args *args, void *workspace, uint64_t workspace_bytes,
                      void *stream);
 
+/* Size of the scratch built into the library for fmcuda_moe_block_noalloc. */
+#define FM_MOE_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* The same MoE block as fmcuda_moe_block, for callers that cannot allocate
+ * device memory -- for example a host whose HBM is fully committed to expert
+ * slots before decoding starts, or a plug-in whose host framework owns the
+ * device allocator.  No counterpart in the reference: FreeMoe has no GPU path.
+ *
+ * It allocates and frees nothing: its scratch is a fixed array of
+ * FM_MOE_NOALLOC_SCRATCH_BYTES inside the library's device image, held by
+ * every GPU that loads the library until the process exits.  A block whose
+ * fmcuda_moe_workspace_bytes() exceeds that size is refused with
+ * INVALID_ARGUMENT.  The first call on each device looks up the scratch's
+ * device address with that device current; make that first call before
+ * capturing the stream.  All calls share the one array and the next call
+ * overwrites it, so calls that overlap on the GPU (other streams, other host
+ * threads on the same device) race: keep them ordered on one stream. */
+int fmcuda_moe_block_noalloc(const fmcuda_moe_args *args, void *stream);
+
 /* ====================== synthetic weights (bench/test) ====================== */
 
 /* Fills `dst` with `rows` rows of `cols` values of `type_id` (Q8_0 / Q4_K /
