@@ -84,7 +84,22 @@ class MoeArgs(C.Structure):
     ]
 
 
+class SharedExpert(C.Structure):
+    _fields_ = [
+        ("slot", C.c_void_p),
+        ("ffn", C.c_uint32),
+        ("up_offset", C.c_uint64),
+        ("down_offset", C.c_uint64),
+        ("gate_type", C.c_uint32),
+        ("up_type", C.c_uint32),
+        ("down_type", C.c_uint32),
+        ("gate_scalar", C.c_void_p),
+    ]
+
+
 MOE_STAGES = ("router", "grouping", "x_planes", "gate_up", "act_planes", "down", "combine")
+# the prefill path's stages under the same eight events (stage 5 is empty there)
+PREFILL_STAGES = ("router", "grouping", "gather", "gate_up", "none", "down", "combine")
 
 
 # (name, restype, argtypes): every symbol declared in include/freemoe_b200.h
@@ -121,6 +136,8 @@ SIGNATURES = [
     ("fmcuda_moe_workspace_bytes", C.c_int, [_U32, _U32, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
     ("fmcuda_moe_block", C.c_int, [C.POINTER(MoeArgs), _P, _U64, _P]),
     ("fmcuda_moe_block_noalloc", C.c_int, [C.POINTER(MoeArgs), _P]),
+    ("fmcuda_moe_prefill_workspace_bytes", C.c_int, [_U32, _U32, _U32, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
+    ("fmcuda_moe_prefill", C.c_int, [C.POINTER(MoeArgs), C.POINTER(SharedExpert), _P, _U64, _P]),
     ("fmcuda_synth_weights", C.c_int, [_U32, _P, _U64, _U32, _U64, _F, _P]),
 ]
 

@@ -95,6 +95,15 @@ __global__ void combine_kernel(const float *__restrict__ part, const float *__re
 
 } // namespace
 
+// y[t] = sum over r of w[t,r] * part[slot_of(t,r)]; also used by the prefill path.
+int launch_combine(const float *part, const float *weights, const uint32_t *slot_of, uint32_t tokens,
+                   uint32_t top_k, uint32_t d, float *y, cudaStream_t s) {
+    const uint64_t n = static_cast<uint64_t>(tokens) * d;
+    combine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(part, weights, slot_of, tokens, top_k,
+                                                                          d, y);
+    return check_launch("combine launch");
+}
+
 // Shared by the allocating entry point and any variant that brings its own scratch.
 int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_bytes,
                   cudaStream_t s) {

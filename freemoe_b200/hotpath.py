@@ -10,7 +10,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import (GEOMETRY, ORDER_ANY, TYPE_F32, X_BF16, X_F32, DeviceInfo, FmError, MoeArgs,
+from ._lib import (GEOMETRY, ORDER_ANY, TYPE_F32, X_BF16, X_F32, DeviceInfo, FmError, MoeArgs, SharedExpert,
                    check, load)
 
 
@@ -166,6 +166,59 @@ def moe_block(x: torch.Tensor, logits: torch.Tensor, slots, *, top_k: int, ffn: 
                  gate_type=gate_type, up_type=up_type, down_type=down_type, up_offset=gate_bytes,
                  down_offset=gate_bytes + up_bytes, y=y, ids_out=ids, weights_out=wts)
     check(load().fmcuda_moe_block(C.byref(a), _ptr(workspace), workspace.numel(), _stream(stream)))
+    if return_routing:
+        return y, ids, wts
+    return y
+
+
+def moe_prefill_workspace_bytes(tokens: int, experts: int, top_k: int, d_model: int, ffn: int,
+                                shared_ffn: int = 0) -> int:
+    v = C.c_uint64(0)
+    check(load().fmcuda_moe_prefill_workspace_bytes(tokens, experts, top_k, d_model, ffn, shared_ffn,
+                                                     C.byref(v)))
+    return v.value
+
+
+def shared_expert_args(slot: torch.Tensor, *, d_model: int, ffn: int, gate_type: int, up_type=None,
+                       down_type=None, gate_scalar: torch.Tensor | None = None) -> SharedExpert:
+    """The C struct for a shared expert whose payload is gate || up || down."""
+    up_type = gate_type if up_type is None else up_type
+    down_type = gate_type if down_type is None else down_type
+    gate_bytes = row_bytes(gate_type, d_model) * ffn
+    up_bytes = row_bytes(up_type, d_model) * ffn
+    s = SharedExpert()
+    s.slot = slot.data_ptr()
+    s.ffn = ffn
+    s.up_offset = gate_bytes
+    s.down_offset = gate_bytes + up_bytes
+    s.gate_type, s.up_type, s.down_type = gate_type, up_type, down_type
+    s.gate_scalar = gate_scalar.data_ptr() if gate_scalar is not None else None
+    return s
+
+
+def moe_prefill(x: torch.Tensor, logits: torch.Tensor, slots, *, top_k: int, ffn: int, gate_type: int,
+                up_type: int | None = None, down_type: int | None = None, shared=None, workspace=None,
+                return_routing: bool = False, stream=None):
+    """The routed MoE block for a batch of tokens on the tcgen05 grouped GEMM
+    (fmcuda_moe_prefill).  ``shared`` is an optional :func:`shared_expert_args`."""
+    up_type = gate_type if up_type is None else up_type
+    down_type = gate_type if down_type is None else down_type
+    tokens, d_model = x.shape
+    experts = logits.shape[1]
+    gate_bytes = row_bytes(gate_type, d_model) * ffn
+    up_bytes = row_bytes(up_type, d_model) * ffn
+    table = slot_table(slots, x.device)
+    need = moe_prefill_workspace_bytes(tokens, experts, top_k, d_model, ffn, shared.ffn if shared else 0)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    y = torch.empty(tokens, d_model, dtype=torch.float32, device=x.device)
+    ids = torch.empty(tokens, top_k, dtype=torch.int32, device=x.device) if return_routing else None
+    wts = torch.empty(tokens, top_k, dtype=torch.float32, device=x.device) if return_routing else None
+    a = moe_args(x, logits, table, experts=experts, top_k=top_k, d_model=d_model, ffn=ffn,
+                 gate_type=gate_type, up_type=up_type, down_type=down_type, up_offset=gate_bytes,
+                 down_offset=gate_bytes + up_bytes, y=y, ids_out=ids, weights_out=wts)
+    check(load().fmcuda_moe_prefill(C.byref(a), C.byref(shared) if shared is not None else None,
+                                    _ptr(workspace), workspace.numel(), _stream(stream)))
     if return_routing:
         return y, ids, wts
     return y

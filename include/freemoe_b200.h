@@ -213,6 +213,45 @@ int fmcuda_moe_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k
 int fmcuda_moe_block(const fmcuda_moe_args *args, void *workspace, uint64_t workspace_bytes,
                      void *stream);
 
+/* ========================= MoE prefill (grouped GEMM) ========================= */
+
+/* A dense SwiGLU FFN run beside the routed experts for every token
+ * (src/engine.cpp:1778-1811): y[t] += gate_scalar[t] * down(silu(gate x) * up x),
+ * added after the routed combine.  `slot` holds gate rows, up rows at
+ * `up_offset`, down rows at `down_offset` (the ffn_*_shexp tensors, one record). */
+typedef struct fmcuda_shared_expert {
+    const void *slot;          /* device pointer */
+    uint32_t ffn;              /* shared_expert_intermediate (multiple of 128) */
+    uint64_t up_offset;
+    uint64_t down_offset;
+    uint32_t gate_type;
+    uint32_t up_type;
+    uint32_t down_type;
+    const float *gate_scalar;  /* optional device [tokens]: the per-token branch scalar
+                                  (sigmoid of ffn_gate_inp_shexp); NULL = 1.0 (ungated) */
+} fmcuda_shared_expert;
+
+/* The routed MoE block of fmcuda_moe_block for a batch of tokens (prompt
+ * prefill), on the sm_100a tensor cores: router and grouping as in
+ * fmcuda_moe_block, the token rows gathered per expert, then per expert one
+ * grouped GEMM for gate/up with SwiGLU and one for down (tcgen05.mma, fp16
+ * operands dequantised from the stored Q8_0 / Q4_K bytes in the kernel, f32
+ * accumulation), then the weighted combine in top-k order and the optional
+ * shared expert.  Reference: the per-token expert loop of src/engine.cpp:1711-1811
+ * applied to every prompt token.  Outputs match fmcuda_moe_block / the
+ * reference within a relative tolerance (fp16 operands), not bit for bit.
+ *
+ * Shapes: Q8_0 or Q4_K experts (gate and up of one type), d_model and ffn
+ * multiples of 128 (and of 256 for Q4_K rows), at most 1024 experts; other
+ * shapes return SHAPE_MISMATCH / UNSUPPORTED_QUANTISATION.  `shared` may be
+ * NULL.  stage_events: 0 start, 1 router, 2 grouping, 3 gather, 4 gate/up,
+ * 5 (same as 4), 6 down, 7 combine and shared expert. */
+int fmcuda_moe_prefill_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k,
+                                       uint32_t d_model, uint32_t ffn, uint32_t shared_ffn,
+                                       uint64_t *bytes);
+int fmcuda_moe_prefill(const fmcuda_moe_args *args, const fmcuda_shared_expert *shared,
+                       void *workspace, uint64_t workspace_bytes, void *stream);
+
 /* Size of the scratch built into the library for fmcuda_moe_block_noalloc. */
 #define FM_MOE_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
