@@ -404,6 +404,232 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Layer configurations beside the headline stack (BASELINE configs[2..4]):
+# prefill of a DeepSeek-shaped layer and a Qwen3-shaped layer on the tcgen05
+# grouped GEMM (fmcuda_moe_prefill), and the Mixtral-shaped decode layer on the
+# GEMV path (fmcuda_moe_block).  One step = one MoE block over the config's
+# tokens; value = tokens/s; roofline of the dominant kernel against the
+# measured dense bf16 peak (tensor-bound prefill) or HBM (decode).
+# ---------------------------------------------------------------------------
+
+LAYERS = {
+    # name: experts, top_k, d_model, ffn, type, tokens, logits, shared_ffn
+    "deepseek": dict(E=64, k=6, d=2048, ffn=1408, t=8, T=4096, logits="zipf", shared=2816),
+    "qwen3": dict(E=128, k=8, d=4096, ffn=1536, t=12, T=8192, logits="uniform", shared=0),
+    "mixtral": dict(E=8, k=2, d=4096, ffn=14336, t=12, T=16, logits="normal", shared=0),
+}
+
+
+def layer_inputs(cfg, tokens, seed):
+    import numpy as np
+    from oracle.oracle import bf16_round
+
+    rng = np.random.default_rng(seed)
+    x = bf16_round(rng.normal(0, 1, size=(tokens, cfg["d"])).astype(np.float32))
+    E = cfg["E"]
+    if cfg["logits"] == "zipf":
+        # Zipf(1.1) expert popularity, ranks permuted, Gumbel-top-k sampling
+        p = 1.0 / np.arange(1, E + 1) ** 1.1
+        logp = np.log(p / p.sum())[rng.permutation(E)]
+        lg = logp[None, :] + rng.gumbel(size=(tokens, E))
+    elif cfg["logits"] == "uniform":
+        lg = rng.uniform(-1, 1, size=(tokens, E))
+    else:
+        lg = rng.normal(0, 1, size=(tokens, E))
+    return x, lg.astype(np.float32)
+
+
+def layer_flops(cfg, pairs, tokens):
+    routed = 2 * pairs * 3 * cfg["d"] * cfg["ffn"]
+    shared = 2 * tokens * 3 * cfg["d"] * cfg["shared"]
+    return routed, shared
+
+
+def run_layer(args):
+    import numpy as np
+    import torch
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200._lib import PREFILL_STAGES, MOE_STAGES, check, load
+
+    cfg = dict(LAYERS[args.config])
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    hotpath.init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    lib = load()
+    E, k, d, ffn, t = cfg["E"], cfg["k"], cfg["d"], cfg["ffn"], cfg["t"]
+    T = args.tokens if args.tokens_set else cfg["T"]
+    prefill = args.config != "mixtral"
+    rb_in, rb_ffn = row_bytes(t, d), row_bytes(t, ffn)
+    gb = ffn * rb_in
+    slots = []
+    for e in range(E):
+        slab = torch.empty(2 * gb + d * rb_ffn, dtype=torch.uint8, device=dev)
+        off = 0
+        for j, (rows, cols) in enumerate(((ffn, d), (ffn, d), (d, ffn))):
+            check(lib.fmcuda_synth_weights(t, C.c_void_p(slab.data_ptr() + off), rows, cols,
+                                           1000 * (rank + 1) + 3 * e + j, 0.02, stream.cuda_stream))
+            off += rows * row_bytes(t, cols)
+        slots.append(slab)
+    table = hotpath.slot_table(slots, dev)
+    shared = None
+    if cfg["shared"]:
+        sf = cfg["shared"]
+        sh_slab = torch.cat([hotpath.synth_weights(t, sf, d, 77001), hotpath.synth_weights(t, sf, d, 77002),
+                             hotpath.synth_weights(t, d, sf, 77003)])
+        shared = hotpath.shared_expert_args(sh_slab, d_model=d, ffn=sf, gate_type=t)
+    x_np, lg_np = layer_inputs(cfg, T, seed=rank + 1)
+    x = torch.from_numpy(x_np).to(dev).to(torch.bfloat16)
+    logits = torch.from_numpy(lg_np).to(dev)
+    y = torch.empty(T, d, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+    if prefill:
+        need = hotpath.moe_prefill_workspace_bytes(T, E, k, d, ffn, cfg["shared"])
+    else:
+        need = hotpath.moe_workspace_bytes(T, E, k, d, ffn)
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    n_ev = len(MOE_STAGES) + 1
+
+    def timing_event():
+        h = C.c_void_p()
+        check(lib.fmcuda_event_create_timing(C.byref(h)))
+        return h.value
+
+    ev_pool = [[timing_event() for _ in range(n_ev)] for _ in range(args.steps)]
+    ev_arrays = [(C.c_void_p * n_ev)(*evs) for evs in ev_pool]
+
+    def elapsed(a, b):
+        v = C.c_float()
+        check(lib.fmcuda_event_elapsed_ms(C.c_void_p(a), C.c_void_p(b), C.byref(v)))
+        return v.value
+
+    arg_cache = {}
+    sh_ref = C.byref(shared) if shared is not None else None
+
+    def call(xt, lgt, yt, events=None):
+        key = (xt.data_ptr(), lgt.data_ptr(), yt.data_ptr())
+        a = arg_cache.get(key)
+        if a is None:
+            a = hotpath.moe_args(xt, lgt, table, experts=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t,
+                                 down_type=t, up_offset=gb, down_offset=2 * gb, y=yt, ids_out=ids)
+            arg_cache[key] = a
+        a.stage_events = C.cast(events, C.c_void_p) if events is not None else None
+        if prefill:
+            check(lib.fmcuda_moe_prefill(C.byref(a), sh_ref, C.c_void_p(ws.data_ptr()), ws.numel(),
+                                         stream.cuda_stream))
+        else:
+            check(lib.fmcuda_moe_block(C.byref(a), C.c_void_p(ws.data_ptr()), ws.numel(), stream.cuda_stream))
+
+    for _ in range(args.warmup):
+        call(x, logits, y)
+    torch.cuda.synchronize()
+    assert hotpath.device_status() == 0
+    ids_np = ids.cpu().numpy()
+    counts = np.bincount(ids_np.ravel(), minlength=E)
+    pairs = int(counts.sum())
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            call(x, logits, y, ev_arrays[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    names = PREFILL_STAGES if prefill else MOE_STAGES
+    stage_ms = {s: statistics.mean(elapsed(ev_pool[i][j], ev_pool[i][j + 1]) for i in range(args.steps))
+                for j, s in enumerate(names) if s != "none"}
+    for evs in ev_pool:
+        for e in evs:
+            lib.fmcuda_event_destroy(C.c_void_p(e))
+
+    # end to end with host buffers
+    hx = torch.from_numpy(x_np).to(torch.bfloat16).pin_memory()
+    hl = torch.from_numpy(lg_np).pin_memory()
+    hy = torch.empty(T, d, dtype=torch.float32).pin_memory()
+    dx, dl = torch.empty_like(x), torch.empty_like(logits)
+    for _ in range(2):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        call(dx, dl, y)
+        hy.copy_(y, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        call(dx, dl, y)
+        hy.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    assert np.isfinite(hy.numpy()).all()
+    assert hotpath.device_status() == 0
+
+    line = {"metric": METRIC, "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": {8: "q8_0", 12: "q4_k"}[t] + (" -> fp16 tensor cores" if prefill else ""),
+            "data": "synthetic",
+            "config": {"workload": f"{args.config}: {E} experts d {d} ffn {ffn} top-{k}"
+                                   + (f" + shared ffn {cfg['shared']}" if cfg["shared"] else "")
+                                   + f", T={T} bf16 tokens, {cfg['logits']} router logits",
+                       "tokens": T, "pairs": pairs, "experts_hit": int((counts > 0).sum()),
+                       "max_group": int(counts.max()), "min_group": int(counts.min()),
+                       "l2": "expert weights larger than L2"},
+            "stage_ms": stage_ms,
+            "e2e": {"value": T / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4,
+                    "d2h_bytes_per_step": hy.numel() * 4, "ms_per_step": ms_e2e},
+            "gpu_launches": None, "clocks": clocks.summary()}
+    if prefill:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak = float(peaks.get("bf16_tflops", 1590.0))
+        routed, sh = layer_flops(cfg, pairs, T)
+        gu_flops = 2 * pairs * 2 * d * ffn
+        gu_ms = stage_ms["gate_up"]
+        line["roofline"] = {"bound": "tensor", "kernel": "grouped GEMM gate/up + SwiGLU (tcgen05)",
+                            "achieved": gu_flops / (gu_ms / 1e3) / 1e12, "peak": peak,
+                            "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
+                            "frac": gu_flops / (gu_ms / 1e3) / 1e12 / peak, "traffic": None,
+                            "algorithmic_flops": gu_flops,
+                            "down_achieved": 2 * pairs * d * ffn / (stage_ms["down"] / 1e3) / 1e12,
+                            "step_achieved": (routed + sh) / (ms / 1e3) / 1e12,
+                            "step_frac": (routed + sh) / (ms / 1e3) / 1e12 / peak}
+        # 3 launches before the GEMMs (route, group, gather), 2 GEMMs, combine,
+        # and for the shared expert: group, 2 GEMMs, add
+        line["gpu_launches"] = (6 + (4 if cfg["shared"] else 0)) * args.steps
+    else:
+        hit = int((counts > 0).sum())
+        wbytes = hit * (2 * gb + d * rb_ffn)
+        peak, kind = load_peaks()
+        line["hbm_gbs"] = wbytes / (ms / 1e3) / 1e9
+        line["roofline"] = {"bound": "hbm", "kernel": "MoE block (distinct experts' bytes)",
+                            "achieved": line["hbm_gbs"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                            "frac": line["hbm_gbs"] / peak, "traffic": None, "algorithmic_bytes": wbytes}
+        line["gpu_launches"] = 7 * args.steps
+
+    if not args.no_cpu:
+        # the reference's CPU code on a bounded sample of the same tokens
+        from oracle.oracle import Reference, reference_available
+
+        if reference_available():
+            ref = Reference()
+            host_slots = [s.cpu().numpy() for s in slots]
+            threads = os.cpu_count() or 1
+            n_s = min(T, 64 if prefill else T)
+            rc, ids_r, w_r, _ = ref.route(lg_np[:n_s], k)
+            t0 = time.perf_counter()
+            ref.moe_block(t, host_slots, gb, 2 * gb, x_np[:n_s], ids_r, w_r, d, ffn, threads=threads)
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": n_s / dt, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                    "sample": f"{n_s} of the {T} tokens (routed experts only), {dt:.2f} s"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -413,8 +639,14 @@ def main():
     ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--config", default="stack", choices=["stack", *LAYERS],
+                    help="stack (default, the headline) or a layer configuration")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
+    args.tokens_set = any(a.startswith("--tokens") for a in sys.argv[1:])
+    if args.config != "stack" and args.impl == "ours":
+        run_layer(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -133,6 +133,8 @@ SIGNATURES = [
     ("fmcuda_matvec_f32", C.c_int, [_P, _P, _P, _U32, _U32, _I32, _P]),
     ("fmcuda_route", C.c_int, [_P, _U32, _U32, _U32, _I32, _D, _D, _P, _P, _P, _P]),
     ("fmcuda_group", C.c_int, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _P]),
+    ("fmcuda_group_scratch_bytes", C.c_uint64, [_U32, _U32]),
+    ("fmcuda_group_batched", C.c_int, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _P, _P]),
     ("fmcuda_moe_workspace_bytes", C.c_int, [_U32, _U32, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
     ("fmcuda_moe_block", C.c_int, [C.POINTER(MoeArgs), _P, _U64, _P]),
     ("fmcuda_moe_block_noalloc", C.c_int, [C.POINTER(MoeArgs), _P]),

@@ -377,16 +377,38 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
         const uint32_t njobs = my_units * J;
         const uint32_t lane_addr = (wq * 32u) << 16;
 
+        // The prefetch cursor runs up to RS chunks ahead, possibly into the next
+        // unit; the unit's row address is worked out once per unit.  The warp
+        // copies its 32 rows' chunk as one block: lane l moves pieces l, l+32, ...
+        // in row-major order, so each copy instruction covers ~512 contiguous
+        // bytes of two or three rows instead of 32 scattered rows.
+        uint32_t iss_nord = 0xFFFFFFFFu;
+        const uint8_t *iss_row0 = nullptr;
         auto issue = [&](uint32_t j) {
             if (j < njobs) {
-                const uint32_t n_ord = j / J, ch = c0 + (j % J) * cstep;
-                const GUnit g = gg_unit(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
-                const uint8_t *src = p.slots[g.e] + w_off +
-                                     static_cast<uint64_t>(g.rt * GG_BM + row_in_tile) * p.row_bytes +
-                                     static_cast<uint64_t>(ch) * CB;
+                const uint32_t n_ord = j / J, ch = c0 + (j - n_ord * J) * cstep;
+                if (n_ord != iss_nord) {
+                    const GUnit g = gg_unit(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
+                    iss_row0 = p.slots[g.e] + w_off + static_cast<uint64_t>(g.rt * GG_BM + wq * 32u) * p.row_bytes;
+                    iss_nord = n_ord;
+                }
+                const uint8_t *src = iss_row0 + static_cast<uint64_t>(ch) * CB;
+                uint8_t *dst = ring + (j % RS) * L::RAW_SLOT;
                 const uint32_t bytes = min(CB, p.row_bytes - ch * CB);
-                uint8_t *dst = ring + (j % RS) * L::RAW_SLOT + lane * L::PITCH;
-                for (uint32_t o = 0; o < bytes; o += G) cp_async_g<G>(dst + o, src + o);
+                if (bytes == CB) {
+                    constexpr uint32_t PPR = CB / G; // pieces per row
+#pragma unroll
+                    for (uint32_t u = 0; u < PPR; ++u) {
+                        const uint32_t q = lane + 32u * u, r = q / PPR, c = q - r * PPR;
+                        cp_async_g<G>(dst + r * L::PITCH + c * G, src + static_cast<uint64_t>(r) * p.row_bytes + c * G);
+                    }
+                } else {
+                    const uint32_t ppr = bytes / G;
+                    for (uint32_t q = lane; q < 32u * ppr; q += 32u) {
+                        const uint32_t r = q / ppr, c = q - r * ppr;
+                        cp_async_g<G>(dst + r * L::PITCH + c * G, src + static_cast<uint64_t>(r) * p.row_bytes + c * G);
+                    }
+                }
             }
             cp_async_commit();
         };

@@ -28,6 +28,10 @@ int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_
 int launch_group(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
                  uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, cudaStream_t s);
 int check_route_args(uint32_t experts, uint32_t top_k);
+uint64_t group_scratch_bytes(uint32_t n_pairs, uint32_t experts);
+int launch_group_large(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
+                       uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, uint32_t *scratch,
+                       cudaStream_t s);
 int launch_combine(const float *part, const float *weights, const uint32_t *slot_of, uint32_t tokens,
                    uint32_t top_k, uint32_t d, float *y, cudaStream_t s);
 
@@ -36,7 +40,7 @@ namespace {
 inline uint64_t a256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
 struct PrefillLayout {
-    uint64_t ids, weights, counts, offsets, pairs, slot_of;
+    uint64_t ids, weights, counts, offsets, pairs, slot_of, gscratch;
     uint64_t xg, act, part;
     uint64_t sh_counts, sh_offsets, sh_slot, sh_act, sh_part;
     uint64_t total;
@@ -58,6 +62,7 @@ PrefillLayout prefill_layout(uint32_t tokens, uint32_t experts, uint32_t top_k, 
     L.offsets = take((static_cast<uint64_t>(experts) + 1) * 4);
     L.pairs = take(P * 4);
     L.slot_of = take(P * 4);
+    L.gscratch = take(group_scratch_bytes(static_cast<uint32_t>(P), experts));
     // rows [0, P) grouped pairs; rows [P, P + tokens) the tokens in order (shared expert)
     L.xg = take((P + (shared_ffn ? tokens : 0)) * d * 2);
     L.act = take(P * ffn * 2);
@@ -306,7 +311,9 @@ int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, vo
                            weights, nullptr, s)))
         return rc;
     mark(1);
-    if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
+    if ((rc = launch_group_large(ids, P, a->experts, counts, offsets, pairs, slot_of,
+                                 reinterpret_cast<uint32_t *>(ws + L.gscratch), s)))
+        return rc;
     mark(2);
     const uint32_t n_rows = P + (sh ? a->tokens : 0);
     if (a->x_dtype == FM_X_F32)

@@ -200,6 +200,139 @@ int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_
     return check_launch("router launch");
 }
 
+// ---- grouping for large batches (prefill): the same outputs as group_kernel,
+// computed by many warps.  Each warp owns 256 consecutive pairs; a pair's
+// place is offsets[e] + (pairs of expert e in earlier warps) + (earlier pairs
+// of expert e in its own warp), so the order inside an expert's group is
+// ascending pair index, exactly as in group_kernel.
+
+constexpr uint32_t kGroupWarpPairs = 256;
+
+__global__ void group_count_kernel(const uint32_t *__restrict__ ids, uint32_t n_pairs, uint32_t experts,
+                                   uint32_t *__restrict__ warp_counts, int *status) {
+    extern __shared__ uint32_t s_hist[];
+    const uint32_t lane = threadIdx.x & 31u, wl = threadIdx.x >> 5;
+    const uint32_t w = blockIdx.x * (blockDim.x >> 5) + wl;
+    const uint32_t nw = (n_pairs + kGroupWarpPairs - 1) / kGroupWarpPairs;
+    if (w >= nw) return;
+    uint32_t *h = s_hist + wl * experts;
+    for (uint32_t e = lane; e < experts; e += 32) h[e] = 0;
+    __syncwarp();
+    for (uint32_t base = w * kGroupWarpPairs; base < min(n_pairs, (w + 1) * kGroupWarpPairs); base += 32) {
+        const uint32_t i = base + lane;
+        const bool valid = i < n_pairs;
+        const uint32_t e = valid ? ids[i] : 0xFFFFFFFFu;
+        const bool ok = valid && e < experts;
+        if (valid && !ok) raise_device_status(status, FM_STATUS_INVALID_EXPERT_ID);
+        const uint32_t key = ok ? e : 0xFFFFFFFEu - (valid ? 0u : 1u);
+        const uint32_t peers = __match_any_sync(0xFFFFFFFFu, key);
+        if (ok && __popc(peers & ((1u << lane) - 1u)) == 0) h[e] += __popc(peers);
+        __syncwarp();
+    }
+    for (uint32_t e = lane; e < experts; e += 32) warp_counts[static_cast<uint64_t>(w) * experts + e] = h[e];
+}
+
+// warp_counts[w][e] -> pairs of expert e in warps before w; counts, offsets.
+__global__ void group_scan_kernel(uint32_t *__restrict__ warp_counts, uint32_t n_warps, uint32_t experts,
+                                  uint32_t *__restrict__ counts, uint32_t *__restrict__ offsets) {
+    __shared__ uint32_t s_warp_tot[32];
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint32_t mine = 0;
+    if (tid < experts) {
+        for (uint32_t w = 0; w < n_warps; ++w) {
+            uint32_t *c = warp_counts + static_cast<uint64_t>(w) * experts + tid;
+            const uint32_t v = *c;
+            *c = mine;
+            mine += v;
+        }
+    }
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= static_cast<uint32_t>(o)) incl += n;
+    }
+    if (lane == 31) s_warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t wt = s_warp_tot[lane];
+        uint32_t wincl = wt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, wincl, o);
+            if (lane >= static_cast<uint32_t>(o)) wincl += n;
+        }
+        s_warp_tot[lane] = wincl - wt;
+    }
+    __syncthreads();
+    const uint32_t excl = incl - mine + s_warp_tot[warp];
+    if (tid < experts) {
+        counts[tid] = mine;
+        offsets[tid] = excl;
+        if (tid == experts - 1) offsets[experts] = excl + mine;
+    }
+}
+
+__global__ void group_place_kernel(const uint32_t *__restrict__ ids, uint32_t n_pairs, uint32_t experts,
+                                   const uint32_t *__restrict__ warp_base, const uint32_t *__restrict__ offsets,
+                                   uint32_t *__restrict__ pairs, uint32_t *__restrict__ slot_of) {
+    extern __shared__ uint32_t s_run[];
+    const uint32_t lane = threadIdx.x & 31u, wl = threadIdx.x >> 5;
+    const uint32_t w = blockIdx.x * (blockDim.x >> 5) + wl;
+    const uint32_t nw = (n_pairs + kGroupWarpPairs - 1) / kGroupWarpPairs;
+    if (w >= nw) return;
+    uint32_t *run = s_run + wl * experts;
+    for (uint32_t e = lane; e < experts; e += 32)
+        run[e] = offsets[e] + warp_base[static_cast<uint64_t>(w) * experts + e];
+    __syncwarp();
+    for (uint32_t base = w * kGroupWarpPairs; base < min(n_pairs, (w + 1) * kGroupWarpPairs); base += 32) {
+        const uint32_t i = base + lane;
+        const bool valid = i < n_pairs;
+        const uint32_t e = valid ? ids[i] : 0xFFFFFFFFu;
+        const bool ok = valid && e < experts;
+        const uint32_t key = ok ? e : 0xFFFFFFFEu - (valid ? 0u : 1u);
+        const uint32_t peers = __match_any_sync(0xFFFFFFFFu, key);
+        const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+        const uint32_t cur = ok ? run[e] : 0u;
+        __syncwarp();
+        if (ok) {
+            const uint32_t pos = cur + rank;
+            pairs[pos] = i;
+            if (slot_of) slot_of[i] = pos;
+            if (rank == 0) run[e] = cur + __popc(peers);
+        } else if (valid && slot_of) {
+            slot_of[i] = 0xFFFFFFFFu;
+        }
+        __syncwarp();
+    }
+}
+
+uint64_t group_scratch_bytes(uint32_t n_pairs, uint32_t experts) {
+    const uint64_t nw = (static_cast<uint64_t>(n_pairs) + kGroupWarpPairs - 1) / kGroupWarpPairs;
+    return nw * experts * 4;
+}
+
+int launch_group_large(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
+                       uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, uint32_t *scratch,
+                       cudaStream_t s) {
+    if (experts == 0 || experts > kMaxExperts)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "grouping takes 1..1024 experts");
+    const uint32_t nw = (n_pairs + kGroupWarpPairs - 1) / kGroupWarpPairs;
+    constexpr uint32_t kWarps = 4;
+    const uint32_t blocks = (nw + kWarps - 1) / kWarps;
+    const size_t smem = static_cast<size_t>(kWarps) * experts * 4;
+    if (nw) {
+        group_count_kernel<<<blocks, kWarps * 32, smem, s>>>(ids, n_pairs, experts, scratch, device_status_word());
+        int rc = check_launch("grouping count launch");
+        if (rc) return rc;
+    }
+    group_scan_kernel<<<1, 1024, 0, s>>>(scratch, nw, experts, counts, offsets);
+    int rc = check_launch("grouping scan launch");
+    if (rc || !nw) return rc;
+    group_place_kernel<<<blocks, kWarps * 32, smem, s>>>(ids, n_pairs, experts, scratch, offsets, pairs, slot_of);
+    return check_launch("grouping place launch");
+}
+
 int launch_group(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
                  uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, cudaStream_t s) {
     group_kernel<<<1, 1024, 0, s>>>(ids, n_pairs, experts, counts, offsets, pairs, slot_of,
@@ -240,4 +373,19 @@ extern "C" int fmcuda_group(const uint32_t *ids, uint32_t tokens, uint32_t top_k
     if (n > 0xFFFFFFF0ull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
     return launch_group(ids, static_cast<uint32_t>(n), experts, counts, offsets, pairs, slot_of,
                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" uint64_t fmcuda_group_scratch_bytes(uint32_t n_pairs, uint32_t experts) {
+    return group_scratch_bytes(n_pairs, experts);
+}
+
+extern "C" int fmcuda_group_batched(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t experts,
+                                    uint32_t *counts, uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of,
+                                    void *scratch, void *stream) {
+    if (!ids || !counts || !offsets || !pairs || !scratch)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "null grouping pointer");
+    const uint64_t n = static_cast<uint64_t>(tokens) * top_k;
+    if (n > 0xFFFFFFF0ull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
+    return launch_group_large(ids, static_cast<uint32_t>(n), experts, counts, offsets, pairs, slot_of,
+                              static_cast<uint32_t *>(scratch), static_cast<cudaStream_t>(stream));
 }

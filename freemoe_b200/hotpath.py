@@ -102,6 +102,21 @@ def group_by_expert(ids: torch.Tensor, experts: int, stream=None):
     return counts, offsets, pairs, slot_of
 
 
+def group_by_expert_batched(ids: torch.Tensor, experts: int, stream=None):
+    """The many-warp grouping for large batches (same outputs as group_by_expert)."""
+    tokens, top_k = ids.shape
+    dev = ids.device
+    counts = torch.empty(experts, dtype=torch.int32, device=dev)
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
+    pairs = torch.empty(tokens * top_k, dtype=torch.int32, device=dev)
+    slot_of = torch.empty(tokens * top_k, dtype=torch.int32, device=dev)
+    scratch = torch.empty(max(1, load().fmcuda_group_scratch_bytes(tokens * top_k, experts)), dtype=torch.uint8,
+                          device=dev)
+    check(load().fmcuda_group_batched(_ptr(ids), tokens, top_k, experts, _ptr(counts), _ptr(offsets),
+                                      _ptr(pairs), _ptr(slot_of), _ptr(scratch), _stream(stream)))
+    return counts, offsets, pairs, slot_of
+
+
 def moe_workspace_bytes(tokens: int, experts: int, top_k: int, d_model: int, ffn: int) -> int:
     v = C.c_uint64(0)
     check(load().fmcuda_moe_workspace_bytes(tokens, experts, top_k, d_model, ffn, C.byref(v)))

@@ -165,6 +165,14 @@ int fmcuda_group(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t 
                  uint32_t *counts, uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of,
                  void *stream);
 
+/* The same grouping computed by many warps, for large batches (prefill): the
+ * same outputs as fmcuda_group, bit for bit.  `scratch` is device memory of
+ * fmcuda_group_scratch_bytes() bytes. */
+uint64_t fmcuda_group_scratch_bytes(uint32_t n_pairs, uint32_t experts);
+int fmcuda_group_batched(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t experts,
+                         uint32_t *counts, uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of,
+                         void *scratch, void *stream);
+
 /* One routed-expert MoE block (src/engine.cpp:1603-1772) for `tokens` tokens:
  * router (softmax, top-k, renormalisation) on the given logits, grouping by
  * expert, per expert a fused gate/up GEMV with SwiGLU

@@ -196,6 +196,19 @@ def test_group_vs_oracle(cuda, oracle, E, k, T):
     assert np.array_equal(slot_of.cpu().numpy().astype(np.uint32), s_o)
 
 
+@pytest.mark.parametrize("E,k,T", [(8, 2, 1), (64, 6, 4096), (128, 8, 8192), (1024, 8, 3000), (7, 3, 1000)])
+def test_group_batched_vs_oracle(cuda, oracle, E, k, T):
+    # the many-warp grouping used by prefill: bit-identical to the oracle
+    rng = np.random.default_rng(T + E)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.uint32)
+    c_o, o_o, p_o, s_o = oracle.group(ids, E)
+    counts, offsets, pairs, slot_of = cuda.group_by_expert_batched(dev(ids.astype(np.int32)), E)
+    assert np.array_equal(counts.cpu().numpy().astype(np.uint32), c_o)
+    assert np.array_equal(offsets.cpu().numpy().astype(np.uint32), o_o)
+    assert np.array_equal(pairs.cpu().numpy().astype(np.uint32), p_o)
+    assert np.array_equal(slot_of.cpu().numpy().astype(np.uint32), s_o)
+
+
 # ---------------------------------------------------------------- MoE block
 
 def make_experts(oracle, rng, E, d, ffn, t):
