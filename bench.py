@@ -630,6 +630,101 @@ def run_layer(args):
     print(json.dumps(line), flush=True)
 
 
+def run_layer_ep(args):
+    """The Qwen3-shaped layer expert-parallel over the torchrun ranks (NCCL):
+    experts 128/G per rank, tokens 8192/G per rank (strong scaling), token rows
+    dispatched to the experts' owners and the outputs combined back with
+    all-to-all (freemoe_b200/ep.py)."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200.ep import DeviceOps, EPLayer
+
+    cfg = dict(LAYERS[args.config])
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    hotpath.init(local)
+    E, k, d, ffn, t = cfg["E"], cfg["k"], cfg["d"], cfg["ffn"], cfg["t"]
+    T = args.tokens if args.tokens_set else cfg["T"]
+    if E % world or T % world:
+        raise SystemExit(f"{E} experts / {T} tokens do not shard over {world} ranks")
+    per, tp = E // world, T // world
+    gb = ffn * row_bytes(t, d)
+    slots = []
+    for e in range(rank * per, (rank + 1) * per):  # the same seeds as the one-GPU layer
+        slots.append(torch.cat([hotpath.synth_weights(t, rows, cols, 1000 + 3 * e + j)
+                                for j, (rows, cols) in enumerate(((ffn, d), (ffn, d), (d, ffn)))]))
+    x_np, lg_np = layer_inputs(cfg, T, seed=1)
+    sl = slice(rank * tp, (rank + 1) * tp)
+    x = torch.from_numpy(x_np[sl]).cuda().to(torch.bfloat16)
+    logits = torch.from_numpy(lg_np[sl]).cuda()
+    ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
+                    local_slots=slots, up_offset=gb, down_offset=2 * gb)
+    layer = EPLayer(ops)
+    for _ in range(args.warmup):
+        y = layer.forward(x, logits)
+    torch.cuda.synchronize()
+    assert hotpath.device_status() == 0
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            y = layer.forward(x, logits)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms_t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    # e2e: host token rows and logits in, y out, every step
+    hx = torch.from_numpy(x_np[sl]).to(torch.bfloat16).pin_memory()
+    hl = torch.from_numpy(lg_np[sl]).pin_memory()
+    hy = torch.empty(tp, d, dtype=torch.float32).pin_memory()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        dx = hx.cuda(non_blocking=True)
+        dl = hl.cuda(non_blocking=True)
+        y = layer.forward(dx, dl)
+        hy.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms_e, op=dist.ReduceOp.MAX)
+    assert np.isfinite(hy.numpy()).all()
+    pairs = T * k
+    routed, _ = layer_flops(cfg, pairs, T)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    if rank == 0:
+        line = {"metric": METRIC, "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": {8: "q8_0", 12: "q4_k"}[t] + " -> fp16 tensor cores", "data": "synthetic",
+                "config": {"workload": f"{args.config} expert-parallel: {E} experts ({per}/rank) d {d} ffn {ffn} "
+                                       f"top-{k}, T={T} bf16 tokens ({tp}/rank), {cfg['logits']} router logits",
+                           "tokens": T, "parallelism": f"ep{world}", "exchange": "NCCL all-to-all (torch.distributed)"},
+                "e2e": {"value": T / (float(ms_e.item()) / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4,
+                        "ms_per_step": float(ms_e.item())},
+                "roofline": {"bound": "tensor", "kernel": "whole expert-parallel layer", "unit": "TFLOP/s",
+                             "achieved": routed / (ms / 1e3) / 1e12, "peak": peak * world,
+                             "peak_kind": "measured x ranks" if peaks else "fallback x ranks",
+                             "frac": routed / (ms / 1e3) / 1e12 / (peak * world), "traffic": None},
+                "gpu_launches": None, "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -645,7 +740,10 @@ def main():
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     args.tokens_set = any(a.startswith("--tokens") for a in sys.argv[1:])
     if args.config != "stack" and args.impl == "ours":
-        run_layer(args)
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            run_layer_ep(args)
+        else:
+            run_layer(args)
         return
     if args.impl == "reference":
         run_reference(args)

@@ -140,6 +140,12 @@ SIGNATURES = [
     ("fmcuda_moe_block_noalloc", C.c_int, [C.POINTER(MoeArgs), _P]),
     ("fmcuda_moe_prefill_workspace_bytes", C.c_int, [_U32, _U32, _U32, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
     ("fmcuda_moe_prefill", C.c_int, [C.POINTER(MoeArgs), C.POINTER(SharedExpert), _P, _U64, _P]),
+    ("fmcuda_ep_dispatch_scratch_bytes", C.c_uint64, [_U32, _U32, _U32]),
+    ("fmcuda_ep_dispatch", C.c_int, [_P, _U32, _U32, _U32, _U32, _P, _I32, _U32, _P, _P, _P, _P, _P, _P, _P, _P]),
+    ("fmcuda_moe_experts_workspace_bytes", C.c_uint64, [_U32, _U32, _U32, _U32]),
+    ("fmcuda_moe_experts", C.c_int, [_P, _P, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32, _U32, _U32, _P, _P,
+                                     _U64, _P]),
+    ("fmcuda_moe_combine", C.c_int, [_P, _P, _P, _U32, _U32, _U32, _P, _P]),
     ("fmcuda_synth_weights", C.c_int, [_U32, _P, _U64, _U32, _U64, _F, _P]),
 ]
 

@@ -1,0 +1,191 @@
+// ep.cu -- device pieces of the expert-parallel MoE layer (no reference
+// counterpart: FreeMoe runs every expert in one process).  Experts are sharded
+// contiguously over `world` ranks (expert e lives on rank e / experts_per_rank);
+// every rank routes its own tokens.  The exchange itself (token rows out, expert
+// outputs back) is done by the host's collective library between these calls:
+//
+//   fmcuda_route          ids, weights of the local tokens        (router.cu)
+//   fmcuda_ep_dispatch    pairs grouped by destination rank, fp16 token rows
+//                         and local expert ids packed in that order
+//   -- all-to-all of the packed rows and expert ids (counts first) --
+//   fmcuda_moe_experts    the received rows through the local experts: grouped
+//                         by local expert, gate/up + SwiGLU and down on the
+//                         tcgen05 grouped GEMM, outputs in received order
+//   -- all-to-all of the outputs back to the owners of the tokens --
+//   fmcuda_moe_combine    y[t] = sum over r of w[t,r] * out[slot_of(t,r)], in
+//                         top-k order (src/engine.cpp:1770)
+//
+// Each pair's expert output is the same number whichever rank computes it (a
+// grouped-GEMM column depends only on its own token row), so the layer's result
+// equals fmcuda_moe_prefill's on one GPU bit for bit.
+#include <functional>
+#include <string>
+
+#include "common.cuh"
+
+namespace fmb {
+
+uint64_t group_scratch_bytes(uint32_t n_pairs, uint32_t experts);
+int launch_group_large(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
+                       uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, uint32_t *scratch, cudaStream_t s);
+int launch_combine(const float *part, const float *weights, const uint32_t *slot_of, uint32_t tokens,
+                   uint32_t top_k, uint32_t d, float *y, cudaStream_t s);
+int run_expert_gemms(uint32_t experts, const void *const *slots, uint64_t up_offset, uint64_t down_offset,
+                     uint32_t gu_type, uint32_t dn_type, uint32_t d, uint32_t ffn, const uint32_t *counts,
+                     const uint32_t *offsets, uint32_t rows, const __half *xg, __half *act, float *part,
+                     const uint32_t *part_rows, const std::function<void(int)> *mark, cudaStream_t s);
+
+namespace {
+
+inline uint64_t a256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+__global__ void ep_dest_kernel(const uint32_t *__restrict__ ids, uint32_t n, uint32_t per_rank,
+                               uint32_t *__restrict__ dest) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dest[i] = ids[i] / per_rank; // >= world for a bad id: the grouping flags it
+}
+
+// send row i <- pair send_pairs[i]: fp16 copy of its token row and its local expert id.
+template <typename XT>
+__global__ void ep_pack_kernel(const XT *__restrict__ x, const uint32_t *__restrict__ ids,
+                               const uint32_t *__restrict__ send_pairs, const uint32_t *__restrict__ n_send,
+                               uint32_t top_k, uint32_t per_rank, uint32_t d, __half *__restrict__ send_x,
+                               uint32_t *__restrict__ send_expert) {
+    const uint32_t i = blockIdx.x;
+    if (i >= *n_send) return;
+    const uint32_t p = send_pairs[i];
+    const XT *src = x + static_cast<uint64_t>(p / top_k) * d;
+    __half *dst = send_x + static_cast<uint64_t>(i) * d;
+    for (uint32_t c = threadIdx.x * 2; c < d; c += blockDim.x * 2)
+        *reinterpret_cast<__half2 *>(dst + c) = __floats2half2_rn(load_x(src + c), load_x(src + c + 1));
+    if (threadIdx.x == 0) send_expert[i] = ids[p] % per_rank;
+}
+
+// xg[g] = x[pairs[g]] (fp16 rows, 16 bytes per thread step).
+__global__ void gather_f16_rows_kernel(const __half *__restrict__ x, const uint32_t *__restrict__ pairs,
+                                       const uint32_t *__restrict__ n_rows, uint32_t d, __half *__restrict__ xg) {
+    const uint32_t g = blockIdx.x;
+    if (g >= *n_rows) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<uint64_t>(pairs[g]) * d);
+    uint4 *dst = reinterpret_cast<uint4 *>(xg + static_cast<uint64_t>(g) * d);
+    for (uint32_t c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+struct ExpertsLayout {
+    uint64_t counts, offsets, pairs, gscratch, xg, act, total;
+};
+
+ExpertsLayout experts_layout(uint32_t rows, uint32_t experts, uint32_t d, uint32_t ffn) {
+    ExpertsLayout L{};
+    uint64_t o = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t at = o;
+        o += a256(bytes);
+        return at;
+    };
+    L.counts = take(static_cast<uint64_t>(experts) * 4);
+    L.offsets = take((static_cast<uint64_t>(experts) + 1) * 4);
+    L.pairs = take(static_cast<uint64_t>(rows) * 4);
+    L.gscratch = take(group_scratch_bytes(rows, experts));
+    L.xg = take(static_cast<uint64_t>(rows) * d * 2);
+    L.act = take(static_cast<uint64_t>(rows) * ffn * 2);
+    L.total = o;
+    return L;
+}
+
+} // namespace
+} // namespace fmb
+
+using namespace fmb;
+
+extern "C" uint64_t fmcuda_ep_dispatch_scratch_bytes(uint32_t tokens, uint32_t top_k, uint32_t world) {
+    const uint64_t P = static_cast<uint64_t>(tokens) * top_k;
+    return a256(P * 4) + group_scratch_bytes(static_cast<uint32_t>(P), world);
+}
+
+extern "C" int fmcuda_ep_dispatch(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t experts_per_rank,
+                                  uint32_t world, const void *x, int32_t x_dtype, uint32_t d_model,
+                                  uint32_t *send_counts, uint32_t *send_offsets, uint32_t *send_pairs,
+                                  uint32_t *slot_of, void *send_x, uint32_t *send_expert, void *scratch,
+                                  void *stream) {
+    if (!ids || !x || !send_counts || !send_offsets || !send_pairs || !slot_of || !send_x || !send_expert || !scratch)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "null dispatch pointer");
+    if (world == 0 || world > 1024 || experts_per_rank == 0)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "dispatch needs 1..1024 ranks and >= 1 expert per rank");
+    if (x_dtype != FM_X_F32 && x_dtype != FM_X_BF16)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "unknown activation dtype");
+    if (d_model == 0 || d_model % 2) return set_error(FM_STATUS_SHAPE_MISMATCH, "d_model must be even");
+    const uint64_t P64 = static_cast<uint64_t>(tokens) * top_k;
+    if (P64 > 0x7FFFFFFFull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
+    const uint32_t P = static_cast<uint32_t>(P64);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t *dest = static_cast<uint32_t *>(scratch);
+    uint32_t *gscratch = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(scratch) + a256(P64 * 4));
+    if (P) {
+        ep_dest_kernel<<<(P + 255) / 256, 256, 0, s>>>(ids, P, experts_per_rank, dest);
+        int rc = check_launch("dispatch destination launch");
+        if (rc) return rc;
+    }
+    int rc = launch_group_large(dest, P, world, send_counts, send_offsets, send_pairs, slot_of, gscratch, s);
+    if (rc || !P) return rc;
+    if (x_dtype == FM_X_F32)
+        ep_pack_kernel<float><<<P, 128, 0, s>>>(static_cast<const float *>(x), ids, send_pairs, send_offsets + world,
+                                                top_k, experts_per_rank, d_model, static_cast<__half *>(send_x),
+                                                send_expert);
+    else
+        ep_pack_kernel<__nv_bfloat16><<<P, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), ids, send_pairs,
+                                                        send_offsets + world, top_k, experts_per_rank, d_model,
+                                                        static_cast<__half *>(send_x), send_expert);
+    return check_launch("dispatch pack launch");
+}
+
+extern "C" uint64_t fmcuda_moe_experts_workspace_bytes(uint32_t rows, uint32_t experts, uint32_t d_model,
+                                                       uint32_t ffn) {
+    return experts_layout(rows, experts, d_model, ffn).total;
+}
+
+extern "C" int fmcuda_moe_experts(const void *x, const uint32_t *expert_of_row, uint32_t rows, uint32_t experts,
+                                  const void *const *expert_slots, uint64_t up_offset, uint64_t down_offset,
+                                  uint32_t gate_type, uint32_t up_type, uint32_t down_type, uint32_t d_model,
+                                  uint32_t ffn, float *out, void *workspace, uint64_t workspace_bytes,
+                                  void *stream) {
+    if (rows == 0) return FM_STATUS_OK;
+    if (!x || !expert_of_row || !expert_slots || !out)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "null expert-compute pointer");
+    if (experts == 0 || experts > 1024) return set_error(FM_STATUS_INVALID_ARGUMENT, "1..1024 local experts");
+    if (gate_type != up_type)
+        return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "fused gate/up needs one block type for both projections");
+    for (uint32_t t : {gate_type, down_type})
+        if (t != FM_TYPE_Q8_0 && t != FM_TYPE_Q4_K)
+            return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "the grouped GEMM takes Q8_0 or Q4_K weights");
+    const uint32_t kq = gate_type == FM_TYPE_Q4_K || down_type == FM_TYPE_Q4_K ? 256 : 64;
+    if (reinterpret_cast<uintptr_t>(x) % 16 || d_model % 128 || ffn % 128 || d_model % kq || ffn % kq)
+        return set_error(FM_STATUS_SHAPE_MISMATCH,
+                         "expert rows must be 16-byte aligned fp16; d_model and ffn multiples of 128 (256 for Q4_K)");
+    const ExpertsLayout L = experts_layout(rows, experts, d_model, ffn);
+    if (!workspace || workspace_bytes < L.total)
+        return set_error(FM_STATUS_INVALID_ARGUMENT,
+                         "expert workspace too small: need " + std::to_string(L.total) + " bytes");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    uint32_t *counts = reinterpret_cast<uint32_t *>(ws + L.counts);
+    uint32_t *offsets = reinterpret_cast<uint32_t *>(ws + L.offsets);
+    uint32_t *pairs = reinterpret_cast<uint32_t *>(ws + L.pairs);
+    __half *xg = reinterpret_cast<__half *>(ws + L.xg);
+    __half *act = reinterpret_cast<__half *>(ws + L.act);
+    int rc = launch_group_large(expert_of_row, rows, experts, counts, offsets, pairs, nullptr,
+                                reinterpret_cast<uint32_t *>(ws + L.gscratch), s);
+    if (rc) return rc;
+    gather_f16_rows_kernel<<<rows, 128, 0, s>>>(static_cast<const __half *>(x), pairs, offsets + experts, d_model, xg);
+    if ((rc = check_launch("expert gather launch"))) return rc;
+    // GEMM2 writes output row pairs[g] for grouped row g: the received order.
+    return run_expert_gemms(experts, expert_slots, up_offset, down_offset, gate_type, down_type, d_model, ffn, counts,
+                            offsets, rows, xg, act, out, pairs, nullptr, s);
+}
+
+extern "C" int fmcuda_moe_combine(const float *rows_out, const float *weights, const uint32_t *slot_of,
+                                  uint32_t tokens, uint32_t top_k, uint32_t d_model, float *y, void *stream) {
+    if (!rows_out || !weights || !slot_of || !y) return set_error(FM_STATUS_INVALID_ARGUMENT, "null combine pointer");
+    if (tokens == 0) return FM_STATUS_OK;
+    return launch_combine(rows_out, weights, slot_of, tokens, top_k, d_model, y, static_cast<cudaStream_t>(stream));
+}

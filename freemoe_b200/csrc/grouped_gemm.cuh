@@ -65,6 +65,7 @@ struct GGemmParams {
     const uint32_t *counts;      // tokens per expert
     const uint32_t *offsets;     // first grouped row of each expert
     void *out;                   // GEMM1: __half [rows][out_dim]; GEMM2: float [rows][out_dim]
+    const uint32_t *out_rows;    // optional: output row of grouped row g is out_rows[g] (else g)
     int *status;
 };
 
@@ -473,9 +474,12 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
                     tmem_wait_ld();
                     float *out = static_cast<float *>(p.out);
 #pragma unroll
-                    for (uint32_t t = 0; t < 32; ++t)
-                        if (j0 + t < g.n_tok)
-                            out[static_cast<uint64_t>(g.row_b0 + j0 + t) * p.out_dim + orow0] = __uint_as_float(a[t]);
+                    for (uint32_t t = 0; t < 32; ++t) {
+                        if (j0 + t < g.n_tok) {
+                            const uint32_t r = p.out_rows ? __ldg(p.out_rows + g.row_b0 + j0 + t) : g.row_b0 + j0 + t;
+                            out[static_cast<uint64_t>(r) * p.out_dim + orow0] = __uint_as_float(a[t]);
+                        }
+                    }
                 }
             }
             tc_fence_before();

@@ -211,12 +211,14 @@ int check_prefill_shape(uint32_t type_id, uint32_t in_dim, uint32_t out_dim, con
     return FM_STATUS_OK;
 }
 
+} // namespace
+
 // Gate/up + SwiGLU then down for one set of experts whose token rows are
 // grouped in xg (rows = pairs); act and part use the same row numbering.
 int run_expert_gemms(uint32_t experts, const void *const *slots, uint64_t up_offset, uint64_t down_offset,
                      uint32_t gu_type, uint32_t dn_type, uint32_t d, uint32_t ffn, const uint32_t *counts,
                      const uint32_t *offsets, uint32_t rows, const __half *xg, __half *act, float *part,
-                     const std::function<void(int)> *mark, cudaStream_t s) {
+                     const uint32_t *part_rows, const std::function<void(int)> *mark, cudaStream_t s) {
     int rc;
     const uint64_t gu_rb = row_bytes(gu_type, d), dn_rb = row_bytes(dn_type, ffn);
     const int g1 = copy_granule(gu_type, gu_rb, 0, up_offset);
@@ -251,10 +253,9 @@ int run_expert_gemms(uint32_t experts, const void *const *slots, uint64_t up_off
     p2.in_dim = ffn;
     p2.row_bytes = static_cast<uint32_t>(dn_rb);
     p2.out = part;
+    p2.out_rows = part_rows;
     return launch_gg<1, GG_EPI_F32>(dn_type, p2, map2, tiles_max * (d / GG_BM), g2, s);
 }
-
-} // namespace
 
 int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, void *workspace,
                     uint64_t workspace_bytes, cudaStream_t s) {
@@ -325,7 +326,7 @@ int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, vo
     if ((rc = check_launch("gather launch"))) return rc;
     mark(3);
     if ((rc = run_expert_gemms(a->experts, a->expert_slots, a->up_offset, a->down_offset, a->gate_type,
-                               a->down_type, a->d_model, a->ffn, counts, offsets, P, xg, act, part, &mark, s)))
+                               a->down_type, a->d_model, a->ffn, counts, offsets, P, xg, act, part, nullptr, &mark, s)))
         return rc;
     mark(6);
     if ((rc = launch_combine(part, weights, slot_of, a->tokens, a->top_k, a->d_model, a->y, s))) return rc;
@@ -339,7 +340,7 @@ int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, vo
         if ((rc = check_launch("shared expert group"))) return rc;
         if ((rc = run_expert_gemms(1, stab, sh->up_offset, sh->down_offset, sh->gate_type, sh->down_type,
                                    a->d_model, sh->ffn, sc, so, a->tokens,
-                                   xg + static_cast<uint64_t>(P) * a->d_model, sact, spart, nullptr, s)))
+                                   xg + static_cast<uint64_t>(P) * a->d_model, sact, spart, nullptr, nullptr, s)))
             return rc;
         const uint64_t n = static_cast<uint64_t>(a->tokens) * a->d_model;
         add_shared_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(a->y, spart, sh->gate_scalar,

@@ -1,0 +1,146 @@
+"""Expert-parallel MoE layer: experts sharded over the ranks of a process group,
+token rows dispatched to the experts' owners and the outputs combined back.
+
+No counterpart in the reference (FreeMoe runs every expert in one process);
+the per-rank arithmetic is the reference's expert loop (src/engine.cpp:1711-1772)
+on the grouped GEMM.  Expert e lives on rank e // (E / world).  One layer call:
+
+  route          ids, weights of this rank's tokens            (fmcuda_route)
+  dispatch       pairs grouped by destination rank, fp16 rows   (fmcuda_ep_dispatch)
+  all-to-all     counts, then rows and local expert ids
+  experts        the received rows through this rank's experts (fmcuda_moe_experts)
+  all-to-all     the f32 outputs back to the tokens' owners
+  combine        y[t] = sum over r of w[t, r] * out[slot_of(t, r)] in top-k order
+
+The exchange uses ``torch.distributed.all_to_all_single`` on the group (NCCL
+over NVLink on GPUs).  The arithmetic is pluggable (``ops``): :class:`DeviceOps`
+calls the sm_100a library; the CPU tests plug in a host implementation to check
+the exchange and ordering logic with gloo ranks.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Dispatch:
+    send_counts: torch.Tensor  # [world] int64, on the exchange device
+    send_x: torch.Tensor       # [>= S, d] rows in send order (fp16 on the device)
+    send_expert: torch.Tensor  # [>= S] int32 local expert ids
+    slot_of: torch.Tensor      # [T*k] int32: send row of pair t*k + r
+
+
+class DeviceOps:
+    """The sm_100a kernels through the C ABI (all tensors on one CUDA device)."""
+
+    def __init__(self, *, experts_total: int, top_k: int, d_model: int, ffn: int, gate_type: int,
+                 up_type: int, down_type: int, local_slots, up_offset: int, down_offset: int):
+        from . import hotpath
+        from ._lib import X_BF16, X_F32, check, load
+
+        self.h, self.lib, self.check = hotpath, load(), check
+        self.X_BF16, self.X_F32 = X_BF16, X_F32
+        self.E, self.k, self.d, self.ffn = experts_total, top_k, d_model, ffn
+        self.types = (gate_type, up_type, down_type)
+        self.up_offset, self.down_offset = up_offset, down_offset
+        self.slots = local_slots
+        self.table = hotpath.slot_table(local_slots, local_slots[0].device) if local_slots else None
+        self._ws = {}
+
+    def _buf(self, name, nbytes, device):
+        b = self._ws.get(name)
+        if b is None or b.numel() < nbytes:
+            b = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+            self._ws[name] = b
+        return b
+
+    def _stream(self):
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def route(self, logits: torch.Tensor):
+        T = logits.shape[0]
+        ids = torch.empty(T, self.k, dtype=torch.int32, device=logits.device)
+        w = torch.empty(T, self.k, dtype=torch.float32, device=logits.device)
+        self.check(self.lib.fmcuda_route(C.c_void_p(logits.data_ptr()), T, self.E, self.k, 1, 6.103515625e-5, 1.0,
+                                         C.c_void_p(ids.data_ptr()), C.c_void_p(w.data_ptr()), None, self._stream()))
+        return ids, w
+
+    def dispatch(self, ids: torch.Tensor, x: torch.Tensor, world: int) -> Dispatch:
+        T, k = ids.shape
+        P, dev, d = T * k, ids.device, self.d
+        per_rank = self.E // world
+        counts32 = torch.empty(world, dtype=torch.int32, device=dev)
+        offsets = torch.empty(world + 1, dtype=torch.int32, device=dev)
+        send_pairs = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+        slot_of = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+        send_x = torch.empty(max(P, 1), d, dtype=torch.float16, device=dev)
+        send_e = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+        scratch = self._buf("dispatch", self.lib.fmcuda_ep_dispatch_scratch_bytes(T, k, world), dev)
+        xdt = self.X_BF16 if x.dtype == torch.bfloat16 else self.X_F32
+        self.check(self.lib.fmcuda_ep_dispatch(
+            C.c_void_p(ids.data_ptr()), T, k, per_rank, world, C.c_void_p(x.data_ptr()), xdt, d,
+            C.c_void_p(counts32.data_ptr()), C.c_void_p(offsets.data_ptr()), C.c_void_p(send_pairs.data_ptr()),
+            C.c_void_p(slot_of.data_ptr()), C.c_void_p(send_x.data_ptr()), C.c_void_p(send_e.data_ptr()),
+            C.c_void_p(scratch.data_ptr()), self._stream()))
+        return Dispatch(counts32.to(torch.int64), send_x, send_e, slot_of)
+
+    def empty_rows(self, n: int, like: torch.Tensor) -> torch.Tensor:
+        return torch.empty(max(n, 1), self.d, dtype=like.dtype, device=like.device)
+
+    def experts(self, rows: torch.Tensor, expert: torch.Tensor, n: int) -> torch.Tensor:
+        dev = rows.device
+        out = torch.empty(max(n, 1), self.d, dtype=torch.float32, device=dev)
+        if n == 0:
+            return out
+        per_rank = len(self.slots)
+        ws = self._buf("experts", self.lib.fmcuda_moe_experts_workspace_bytes(n, per_rank, self.d, self.ffn), dev)
+        g, u, dn = self.types
+        self.check(self.lib.fmcuda_moe_experts(
+            C.c_void_p(rows.data_ptr()), C.c_void_p(expert.data_ptr()), n, per_rank, C.c_void_p(self.table.data_ptr()),
+            self.up_offset, self.down_offset, g, u, dn, self.d, self.ffn, C.c_void_p(out.data_ptr()),
+            C.c_void_p(ws.data_ptr()), ws.numel(), self._stream()))
+        return out
+
+    def combine(self, back: torch.Tensor, w: torch.Tensor, slot_of: torch.Tensor) -> torch.Tensor:
+        T = w.shape[0]
+        y = torch.empty(T, self.d, dtype=torch.float32, device=w.device)
+        self.check(self.lib.fmcuda_moe_combine(C.c_void_p(back.data_ptr()), C.c_void_p(w.data_ptr()),
+                                               C.c_void_p(slot_of.data_ptr()), T, self.k, self.d,
+                                               C.c_void_p(y.data_ptr()), self._stream()))
+        return y
+
+
+class EPLayer:
+    """One expert-parallel MoE layer on the ranks of ``group``."""
+
+    def __init__(self, ops, group=None):
+        self.ops, self.group = ops, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if ops.E % self.world:
+            raise ValueError(f"{ops.E} experts do not shard evenly over {self.world} ranks")
+        self.timing = {}
+
+    def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        ops, g = self.ops, self.group
+        ids, w = ops.route(logits)
+        plan = ops.dispatch(ids, x, self.world)
+        send_counts = plan.send_counts
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=g)
+        sc = send_counts.cpu().tolist()  # the host needs both sides' sizes
+        rc = recv_counts.cpu().tolist()
+        S, R = int(sum(sc)), int(sum(rc))
+        recv_x = ops.empty_rows(R, plan.send_x)
+        recv_e = torch.empty(max(R, 1), dtype=plan.send_expert.dtype, device=plan.send_expert.device)
+        dist.all_to_all_single(recv_x[:R], plan.send_x[:S], output_split_sizes=rc, input_split_sizes=sc, group=g)
+        dist.all_to_all_single(recv_e[:R], plan.send_expert[:S], output_split_sizes=rc, input_split_sizes=sc,
+                               group=g)
+        out = ops.experts(recv_x, recv_e, R)
+        back = torch.empty(max(S, 1), out.shape[1], dtype=out.dtype, device=out.device)
+        dist.all_to_all_single(back[:S], out[:R], output_split_sizes=sc, input_split_sizes=rc, group=g)
+        return ops.combine(back, w, plan.slot_of)

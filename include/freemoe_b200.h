@@ -260,6 +260,49 @@ int fmcuda_moe_prefill_workspace_bytes(uint32_t tokens, uint32_t experts, uint32
 int fmcuda_moe_prefill(const fmcuda_moe_args *args, const fmcuda_shared_expert *shared,
                        void *workspace, uint64_t workspace_bytes, void *stream);
 
+/* ===================== expert parallelism (device pieces) ===================== */
+
+/* No counterpart in the reference (FreeMoe runs all experts in one process).
+ * Experts are sharded contiguously over `world` ranks: expert e lives on rank
+ * e / experts_per_rank as local expert e % experts_per_rank.  Each rank routes
+ * its own tokens with fmcuda_route, then:
+ *
+ * fmcuda_ep_dispatch: groups the T*k pairs by destination rank (ascending pair
+ * order inside each rank's block) and packs, in that order, the fp16 token row
+ * [d_model] and the local expert id of every pair:
+ *   send_counts [world], send_offsets [world+1], send_pairs [T*k] (pair index
+ *   t*k + r of send row i), slot_of [T*k] (send row of pair p), send_x
+ *   [T*k * d_model] fp16, send_expert [T*k].
+ * `scratch`: fmcuda_ep_dispatch_scratch_bytes() bytes of device memory.
+ * The caller then exchanges rows and expert ids with its collective library
+ * (an all-to-all with send_counts / the peers' counts). */
+uint64_t fmcuda_ep_dispatch_scratch_bytes(uint32_t tokens, uint32_t top_k, uint32_t world);
+int fmcuda_ep_dispatch(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t experts_per_rank,
+                       uint32_t world, const void *x, int32_t x_dtype, uint32_t d_model,
+                       uint32_t *send_counts, uint32_t *send_offsets, uint32_t *send_pairs,
+                       uint32_t *slot_of, void *send_x, uint32_t *send_expert, void *scratch,
+                       void *stream);
+
+/* The routed experts of this rank applied to `rows` received token rows:
+ * x [rows * d_model] fp16 (16-byte aligned), expert_of_row [rows] local ids;
+ * out [rows * d_model] f32 = down(silu(gate x) * up x) of each row's expert,
+ * in the received order.  The rows are grouped by expert and run on the
+ * tcgen05 grouped GEMM, as in fmcuda_moe_prefill.  Shapes as
+ * fmcuda_moe_prefill; `workspace` of fmcuda_moe_experts_workspace_bytes(). */
+uint64_t fmcuda_moe_experts_workspace_bytes(uint32_t rows, uint32_t experts, uint32_t d_model,
+                                            uint32_t ffn);
+int fmcuda_moe_experts(const void *x, const uint32_t *expert_of_row, uint32_t rows, uint32_t experts,
+                       const void *const *expert_slots, uint64_t up_offset, uint64_t down_offset,
+                       uint32_t gate_type, uint32_t up_type, uint32_t down_type, uint32_t d_model,
+                       uint32_t ffn, float *out, void *workspace, uint64_t workspace_bytes,
+                       void *stream);
+
+/* y[t] = sum over r < top_k of weights[t*k + r] * rows_out[slot_of[t*k + r]]
+ * (multiply then add, in top-k order: src/engine.cpp:1770); rows_out are the
+ * expert outputs back at the token's owner, in its send order. */
+int fmcuda_moe_combine(const float *rows_out, const float *weights, const uint32_t *slot_of,
+                       uint32_t tokens, uint32_t top_k, uint32_t d_model, float *y, void *stream);
+
 /* Size of the scratch built into the library for fmcuda_moe_block_noalloc. */
 #define FM_MOE_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 

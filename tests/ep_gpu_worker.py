@@ -1,0 +1,61 @@
+"""One rank of the expert-parallel GPU test (launched by test_ep_gpu.py with
+torchrun, one process per GPU, NCCL).  Every rank builds the same expert stack
+and token batch from seeds, keeps its expert shard and its token shard, runs
+EPLayer, and rank 0 compares the gathered output with fmcuda_moe_prefill over
+all experts on one GPU: identical bits are expected."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    E, k, d, ffn, T, t = (int(v) for v in sys.argv[1:7])
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    from freemoe_b200 import hotpath
+    from freemoe_b200.ep import DeviceOps, EPLayer
+
+    hotpath.init(local)
+    rb = hotpath.row_bytes
+    slots = [torch.cat([hotpath.synth_weights(t, ffn, d, 5000 + 3 * e), hotpath.synth_weights(t, ffn, d, 5001 + 3 * e),
+                        hotpath.synth_weights(t, d, ffn, 5002 + 3 * e)]) for e in range(E)]
+    gb = rb(t, d) * ffn
+    rng = np.random.default_rng(11)
+    x = torch.from_numpy(rng.normal(0, 1, size=(T, d)).astype(np.float32)).cuda().to(torch.bfloat16)
+    logits = torch.from_numpy(rng.uniform(-1, 1, size=(T, E)).astype(np.float32)).cuda()
+    per, tp = E // world, T // world
+    ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
+                    local_slots=slots[rank * per:(rank + 1) * per], up_offset=gb, down_offset=2 * gb)
+    layer = EPLayer(ops)
+    y = layer.forward(x[rank * tp:(rank + 1) * tp].contiguous(), logits[rank * tp:(rank + 1) * tp].contiguous())
+    torch.cuda.synchronize()
+    assert hotpath.device_status() == 0
+    parts = [torch.empty_like(y) for _ in range(world)]
+    dist.all_gather(parts, y)
+    ok = torch.tensor([1], device="cuda")
+    if rank == 0:
+        y_ep = torch.cat(parts)
+        y_one = hotpath.moe_prefill(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
+        same = torch.equal(y_ep.view(torch.int32), y_one.view(torch.int32))
+        err = float((y_ep - y_one).abs().max() / y_one.abs().max())
+        print(f"ep world={world}: identical={same} max_rel={err:.3e}", flush=True)
+        ok[0] = int(same)
+    dist.broadcast(ok, 0)
+    dist.destroy_process_group()
+    sys.exit(0 if ok.item() else 1)
+
+
+if __name__ == "__main__":
+    main()
