@@ -665,11 +665,12 @@ def run_layer_ep(args):
     logits = torch.from_numpy(lg_np[sl]).cuda()
     ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
                     local_slots=slots, up_offset=gb, down_offset=2 * gb)
-    layer = EPLayer(ops)
+    layer = EPLayer(ops, record_timing=True)
     for _ in range(args.warmup):
         y = layer.forward(x, logits)
     torch.cuda.synchronize()
     assert hotpath.device_status() == 0
+    layer.phase_ms()  # drop the warm-up marks
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -684,6 +685,11 @@ def run_layer_ep(args):
     ms_t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device="cuda")
     dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = float(ms_t.item())
+    phases = layer.phase_ms()
+    ph_t = torch.tensor([phases[k] for k in EPLayer.PHASES], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ph_t, op=dist.ReduceOp.MAX)
+    phases = dict(zip(EPLayer.PHASES, ph_t.tolist()))
+    layer.record_timing = False
     # e2e: host token rows and logits in, y out, every step
     hx = torch.from_numpy(x_np[sl]).to(torch.bfloat16).pin_memory()
     hl = torch.from_numpy(lg_np[sl]).pin_memory()
@@ -712,6 +718,7 @@ def run_layer_ep(args):
                 "config": {"workload": f"{args.config} expert-parallel: {E} experts ({per}/rank) d {d} ffn {ffn} "
                                        f"top-{k}, T={T} bf16 tokens ({tp}/rank), {cfg['logits']} router logits",
                            "tokens": T, "parallelism": f"ep{world}", "exchange": "NCCL all-to-all (torch.distributed)"},
+                "phase_ms_max_over_ranks": phases,
                 "e2e": {"value": T / (float(ms_e.item()) / 1e3), "unit": "tokens/s",
                         "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4,
                         "ms_per_step": float(ms_e.item())},

@@ -15,7 +15,7 @@
 #define FMB_GEMV_MT 2
 #endif
 #ifndef FMB_GEMV_NW
-#define FMB_GEMV_NW 4
+#define FMB_GEMV_NW 2
 #endif
 #ifndef FMB_GEMV_P2
 #define FMB_GEMV_P2 2

@@ -117,30 +117,60 @@ class DeviceOps:
 class EPLayer:
     """One expert-parallel MoE layer on the ranks of ``group``."""
 
-    def __init__(self, ops, group=None):
+    PHASES = ("route", "dispatch", "counts", "rows_out", "experts", "rows_back", "combine")
+
+    def __init__(self, ops, group=None, record_timing: bool = False):
         self.ops, self.group = ops, group
+        self.record_timing = record_timing and torch.cuda.is_available()
+        self._events = []
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if ops.E % self.world:
             raise ValueError(f"{ops.E} experts do not shard evenly over {self.world} ranks")
         self.timing = {}
 
+    def _mark(self):
+        if self.record_timing:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._events.append(e)
+
+    def phase_ms(self) -> dict:
+        """Mean milliseconds per phase over the calls since the last reset
+        (record_timing=True); synchronises the device."""
+        torch.cuda.synchronize()
+        n = len(self.PHASES) + 1
+        calls = [self._events[i:i + n] for i in range(0, len(self._events) - n + 1, n)]
+        out = {ph: sum(c[j].elapsed_time(c[j + 1]) for c in calls) / max(len(calls), 1)
+               for j, ph in enumerate(self.PHASES)}
+        self._events = []
+        return out
+
     def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
         ops, g = self.ops, self.group
+        self._mark()
         ids, w = ops.route(logits)
+        self._mark()
         plan = ops.dispatch(ids, x, self.world)
+        self._mark()
         send_counts = plan.send_counts
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=g)
         sc = send_counts.cpu().tolist()  # the host needs both sides' sizes
         rc = recv_counts.cpu().tolist()
         S, R = int(sum(sc)), int(sum(rc))
+        self._mark()
         recv_x = ops.empty_rows(R, plan.send_x)
         recv_e = torch.empty(max(R, 1), dtype=plan.send_expert.dtype, device=plan.send_expert.device)
         dist.all_to_all_single(recv_x[:R], plan.send_x[:S], output_split_sizes=rc, input_split_sizes=sc, group=g)
         dist.all_to_all_single(recv_e[:R], plan.send_expert[:S], output_split_sizes=rc, input_split_sizes=sc,
                                group=g)
+        self._mark()
         out = ops.experts(recv_x, recv_e, R)
+        self._mark()
         back = torch.empty(max(S, 1), out.shape[1], dtype=out.dtype, device=out.device)
         dist.all_to_all_single(back[:S], out[:R], output_split_sizes=sc, input_split_sizes=rc, group=g)
-        return ops.combine(back, w, plan.slot_of)
+        self._mark()
+        y = ops.combine(back, w, plan.slot_of)
+        self._mark()
+        return y
