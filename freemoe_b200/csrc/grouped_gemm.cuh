@@ -238,6 +238,8 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
     uint64_t *b_full = bars, *b_empty = bars + SB;
     uint64_t *a_full = bars + 2 * SB, *a_empty = a_full + SA;
     uint64_t *acc_full = a_empty + SA, *acc_empty = acc_full + 1, *drain = acc_full + 2;
+    // with equal A and B ring depths one commit per K step releases both stages
+    uint64_t *b_release = (SA == SB) ? a_empty : b_empty;
     uint32_t *misc = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC); // [0] TMEM base, [1] abort, [2] bad
     volatile uint32_t *abort_flag = misc + 1;
     uint32_t *s_units = reinterpret_cast<uint32_t *>(smem + L::OFF_UNITS);
@@ -317,7 +319,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
                 const GUnit g = gg_unit(s_units, E, u, p.counts, p.offsets);
                 for (uint32_t s = 0; s < ksteps; ++s, ++it) {
                     const uint32_t st = it % SB;
-                    if (!gg_wait(&b_empty[st], ((it / SB) & 1u) ^ 1u, abort_flag, p.status)) goto producer_done;
+                    if (!gg_wait(&b_release[st], ((it / SB) & 1u) ^ 1u, abort_flag, p.status)) goto producer_done;
                     mbar_expect_tx(&b_full[st], L::B_STAGE);
                     tma_load_2d(sB + st * L::B_STAGE, &tmap_b, static_cast<int32_t>(s * GG_BK),
                                 static_cast<int32_t>(g.row_b0), &b_full[st]);
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
                                        bd, idesc, (s | kk) != 0u);
                     }
                     issued = true;
-                    tc_commit(&b_empty[bst]);
+                    if (SA != SB) tc_commit(&b_empty[bst]);
                     tc_commit(&a_empty[ast]);
                 }
                 tc_commit(acc_full);
