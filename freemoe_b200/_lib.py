@@ -146,6 +146,13 @@ SIGNATURES = [
     ("fmcuda_moe_experts", C.c_int, [_P, _P, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32, _U32, _U32, _P, _P,
                                      _U64, _P]),
     ("fmcuda_moe_combine", C.c_int, [_P, _P, _P, _U32, _U32, _U32, _P, _P]),
+    ("fmcuda_ep_dispatch_rows_scratch_bytes", C.c_uint64, [_U32, _U32]),
+    ("fmcuda_ep_dispatch_rows", C.c_int, [_P, _P, _U32, _U32, _U32, _U32, _P, _I32, _U32, _P, _P, _P, _P, _P, _P,
+                                          _P, _P, _P]),
+    ("fmcuda_moe_experts_partial_workspace_bytes", C.c_uint64, [_U32, _U32, _U32, _U32, _U32]),
+    ("fmcuda_moe_experts_partial", C.c_int, [_P, _P, _P, _U32, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32, _U32,
+                                             _U32, _P, _P, _U64, _P]),
+    ("fmcuda_ep_combine_rows", C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P]),
     ("fmcuda_synth_weights", C.c_int, [_U32, _P, _U64, _U32, _U64, _F, _P]),
 ]
 

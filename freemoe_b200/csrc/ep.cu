@@ -71,6 +71,71 @@ __global__ void gather_f16_rows_kernel(const __half *__restrict__ x, const uint3
     for (uint32_t c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = src[c];
 }
 
+// key of item t*world + dest: dest when token t has at least one pair on that
+// rank, else 0xFFFFFFFF (absent).
+__global__ void ep_row_keys_kernel(const uint32_t *__restrict__ ids, uint32_t tokens, uint32_t top_k,
+                                   uint32_t per_rank, uint32_t world, uint32_t *__restrict__ keys) {
+    const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (i >= static_cast<uint64_t>(tokens) * world) return;
+    const uint32_t t = static_cast<uint32_t>(i / world), dest = static_cast<uint32_t>(i % world);
+    bool any = false;
+    for (uint32_t r = 0; r < top_k; ++r) any |= ids[static_cast<uint64_t>(t) * top_k + r] / per_rank == dest;
+    keys[i] = any ? dest : 0xFFFFFFFFu;
+}
+
+// send row j <- item rows[j] = t*world + dest: the fp16 token row once, and for
+// each top-k slot r the local expert (or -1 when that pair goes elsewhere) and
+// its routing weight.
+template <typename XT>
+__global__ void ep_pack_rows_kernel(const XT *__restrict__ x, const uint32_t *__restrict__ ids,
+                                    const float *__restrict__ w, const uint32_t *__restrict__ rows,
+                                    const uint32_t *__restrict__ n_rows, uint32_t top_k, uint32_t per_rank,
+                                    uint32_t world, uint32_t d, __half *__restrict__ send_x,
+                                    int32_t *__restrict__ meta_e, float *__restrict__ meta_w) {
+    const uint32_t j = blockIdx.x;
+    if (j >= *n_rows) return;
+    const uint32_t item = rows[j], t = item / world, dest = item % world;
+    const XT *src = x + static_cast<uint64_t>(t) * d;
+    __half *dst = send_x + static_cast<uint64_t>(j) * d;
+    for (uint32_t c = threadIdx.x * 2; c < d; c += blockDim.x * 2)
+        *reinterpret_cast<__half2 *>(dst + c) = __floats2half2_rn(load_x(src + c), load_x(src + c + 1));
+    for (uint32_t r = threadIdx.x; r < top_k; r += blockDim.x) {
+        const uint32_t e = ids[static_cast<uint64_t>(t) * top_k + r];
+        const bool mine = e / per_rank == dest;
+        meta_e[static_cast<uint64_t>(j) * top_k + r] = mine ? static_cast<int32_t>(e % per_rank) : -1;
+        meta_w[static_cast<uint64_t>(j) * top_k + r] = mine ? w[static_cast<uint64_t>(t) * top_k + r] : 0.0f;
+    }
+}
+
+// partial[row] = sum over the row's slots r (top-k order) of w_r * out[row*k + r]
+__global__ void ep_partial_kernel(const float *__restrict__ out, const int32_t *__restrict__ meta_e,
+                                  const float *__restrict__ meta_w, uint32_t rows, uint32_t top_k, uint32_t d,
+                                  float *__restrict__ partial) {
+    const uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (id >= static_cast<uint64_t>(rows) * d) return;
+    const uint32_t row = static_cast<uint32_t>(id / d), c = static_cast<uint32_t>(id % d);
+    float acc = 0.0f;
+    for (uint32_t r = 0; r < top_k; ++r) {
+        const uint64_t slot = static_cast<uint64_t>(row) * top_k + r;
+        if (meta_e[slot] >= 0) acc = __fadd_rn(acc, __fmul_rn(meta_w[slot], out[slot * d + c]));
+    }
+    partial[id] = acc;
+}
+
+// y[t] = sum over destination ranks (ascending) of the returned partial rows.
+__global__ void ep_combine_rows_kernel(const float *__restrict__ back, const uint32_t *__restrict__ row_of,
+                                       uint32_t tokens, uint32_t world, uint32_t d, float *__restrict__ y) {
+    const uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (id >= static_cast<uint64_t>(tokens) * d) return;
+    const uint32_t t = static_cast<uint32_t>(id / d), c = static_cast<uint32_t>(id % d);
+    float acc = 0.0f;
+    for (uint32_t r = 0; r < world; ++r) {
+        const uint32_t row = row_of[static_cast<uint64_t>(t) * world + r];
+        if (row != 0xFFFFFFFFu) acc = __fadd_rn(acc, back[static_cast<uint64_t>(row) * d + c]);
+    }
+    y[id] = acc;
+}
+
 struct ExpertsLayout {
     uint64_t counts, offsets, pairs, gscratch, xg, act, total;
 };
@@ -93,10 +158,162 @@ ExpertsLayout experts_layout(uint32_t rows, uint32_t experts, uint32_t d, uint32
     return L;
 }
 
+struct PartialLayout {
+    uint64_t keys, counts, offsets, pairs, gscratch, xg, act, out, total;
+};
+
+PartialLayout partial_layout(uint32_t rows, uint32_t top_k, uint32_t experts, uint32_t d, uint32_t ffn) {
+    PartialLayout L{};
+    const uint64_t n = static_cast<uint64_t>(rows) * top_k;
+    uint64_t o = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t at = o;
+        o += a256(bytes);
+        return at;
+    };
+    L.keys = take(n * 4);
+    L.counts = take(static_cast<uint64_t>(experts) * 4);
+    L.offsets = take((static_cast<uint64_t>(experts) + 1) * 4);
+    L.pairs = take(n * 4);
+    L.gscratch = take(group_scratch_bytes(static_cast<uint32_t>(n), experts));
+    L.xg = take(n * d * 2);
+    L.act = take(n * ffn * 2);
+    L.out = take(n * d * 4);
+    L.total = o;
+    return L;
+}
+
+__global__ void ep_meta_keys_kernel(const int32_t *__restrict__ meta_e, uint64_t n, uint32_t *__restrict__ keys) {
+    const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (i < n) keys[i] = meta_e[i] >= 0 ? static_cast<uint32_t>(meta_e[i]) : 0xFFFFFFFFu;
+}
+
+// xg[g] = x[pairs[g] / k]
+__global__ void gather_pair_rows_kernel(const __half *__restrict__ x, const uint32_t *__restrict__ pairs,
+                                        const uint32_t *__restrict__ n_rows, uint32_t top_k, uint32_t d,
+                                        __half *__restrict__ xg) {
+    const uint32_t g = blockIdx.x;
+    if (g >= *n_rows) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<uint64_t>(pairs[g] / top_k) * d);
+    uint4 *dst = reinterpret_cast<uint4 *>(xg + static_cast<uint64_t>(g) * d);
+    for (uint32_t c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = src[c];
+}
+
 } // namespace
 } // namespace fmb
 
 using namespace fmb;
+
+extern "C" uint64_t fmcuda_ep_dispatch_rows_scratch_bytes(uint32_t tokens, uint32_t world) {
+    const uint64_t n = static_cast<uint64_t>(tokens) * world;
+    return a256(n * 4) + group_scratch_bytes(static_cast<uint32_t>(n), world);
+}
+
+extern "C" int fmcuda_ep_dispatch_rows(const uint32_t *ids, const float *weights, uint32_t tokens, uint32_t top_k,
+                                       uint32_t experts_per_rank, uint32_t world, const void *x, int32_t x_dtype,
+                                       uint32_t d_model, uint32_t *send_counts, uint32_t *send_offsets,
+                                       uint32_t *send_items, uint32_t *row_of, void *send_x, int32_t *meta_expert,
+                                       float *meta_weight, void *scratch, void *stream) {
+    if (!ids || !weights || !x || !send_counts || !send_offsets || !send_items || !row_of || !send_x ||
+        !meta_expert || !meta_weight || !scratch)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "null dispatch pointer");
+    if (world == 0 || world > 1024 || experts_per_rank == 0)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "dispatch needs 1..1024 ranks and >= 1 expert per rank");
+    if (x_dtype != FM_X_F32 && x_dtype != FM_X_BF16)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "unknown activation dtype");
+    if (d_model == 0 || d_model % 2) return set_error(FM_STATUS_SHAPE_MISMATCH, "d_model must be even");
+    const uint64_t n64 = static_cast<uint64_t>(tokens) * world;
+    if (n64 > 0x7FFFFFFFull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many token-rank items");
+    const uint32_t n = static_cast<uint32_t>(n64);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t *keys = static_cast<uint32_t *>(scratch);
+    uint32_t *gscratch = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(scratch) + a256(n64 * 4));
+    if (n) {
+        ep_row_keys_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, tokens, top_k, experts_per_rank, world, keys);
+        int rc = check_launch("dispatch row keys launch");
+        if (rc) return rc;
+    }
+    int rc = launch_group_large(keys, n, world, send_counts, send_offsets, send_items, row_of, gscratch, s);
+    if (rc || !n) return rc;
+    if (x_dtype == FM_X_F32)
+        ep_pack_rows_kernel<float><<<n, 128, 0, s>>>(static_cast<const float *>(x), ids, weights, send_items,
+                                                     send_offsets + world, top_k, experts_per_rank, world, d_model,
+                                                     static_cast<__half *>(send_x), meta_expert, meta_weight);
+    else
+        ep_pack_rows_kernel<__nv_bfloat16><<<n, 128, 0, s>>>(
+            static_cast<const __nv_bfloat16 *>(x), ids, weights, send_items, send_offsets + world, top_k,
+            experts_per_rank, world, d_model, static_cast<__half *>(send_x), meta_expert, meta_weight);
+    return check_launch("dispatch row pack launch");
+}
+
+extern "C" uint64_t fmcuda_moe_experts_partial_workspace_bytes(uint32_t rows, uint32_t top_k, uint32_t experts,
+                                                               uint32_t d_model, uint32_t ffn) {
+    return partial_layout(rows, top_k, experts, d_model, ffn).total;
+}
+
+extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_expert, const float *meta_weight,
+                                          uint32_t rows, uint32_t top_k, uint32_t experts,
+                                          const void *const *expert_slots, uint64_t up_offset,
+                                          uint64_t down_offset, uint32_t gate_type, uint32_t up_type,
+                                          uint32_t down_type, uint32_t d_model, uint32_t ffn, float *partial,
+                                          void *workspace, uint64_t workspace_bytes, void *stream) {
+    if (rows == 0) return FM_STATUS_OK;
+    if (!x || !meta_expert || !meta_weight || !expert_slots || !partial)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "null expert-compute pointer");
+    if (experts == 0 || experts > 1024) return set_error(FM_STATUS_INVALID_ARGUMENT, "1..1024 local experts");
+    if (gate_type != up_type)
+        return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "fused gate/up needs one block type for both projections");
+    for (uint32_t t : {gate_type, down_type})
+        if (t != FM_TYPE_Q8_0 && t != FM_TYPE_Q4_K)
+            return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "the grouped GEMM takes Q8_0 or Q4_K weights");
+    const uint32_t kq = gate_type == FM_TYPE_Q4_K || down_type == FM_TYPE_Q4_K ? 256 : 64;
+    if (reinterpret_cast<uintptr_t>(x) % 16 || d_model % 128 || ffn % 128 || d_model % kq || ffn % kq)
+        return set_error(FM_STATUS_SHAPE_MISMATCH,
+                         "expert rows must be 16-byte aligned fp16; d_model and ffn multiples of 128 (256 for Q4_K)");
+    const uint64_t n64 = static_cast<uint64_t>(rows) * top_k;
+    if (n64 > 0x7FFFFFFFull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
+    const uint32_t n = static_cast<uint32_t>(n64);
+    const PartialLayout L = partial_layout(rows, top_k, experts, d_model, ffn);
+    if (!workspace || workspace_bytes < L.total)
+        return set_error(FM_STATUS_INVALID_ARGUMENT,
+                         "expert workspace too small: need " + std::to_string(L.total) + " bytes");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    uint32_t *keys = reinterpret_cast<uint32_t *>(ws + L.keys);
+    uint32_t *counts = reinterpret_cast<uint32_t *>(ws + L.counts);
+    uint32_t *offsets = reinterpret_cast<uint32_t *>(ws + L.offsets);
+    uint32_t *pairs = reinterpret_cast<uint32_t *>(ws + L.pairs);
+    __half *xg = reinterpret_cast<__half *>(ws + L.xg);
+    __half *act = reinterpret_cast<__half *>(ws + L.act);
+    float *out = reinterpret_cast<float *>(ws + L.out);
+    ep_meta_keys_kernel<<<static_cast<unsigned>((n64 + 255) / 256), 256, 0, s>>>(meta_expert, n64, keys);
+    int rc = check_launch("expert keys launch");
+    if (rc) return rc;
+    if ((rc = launch_group_large(keys, n, experts, counts, offsets, pairs, nullptr,
+                                 reinterpret_cast<uint32_t *>(ws + L.gscratch), s)))
+        return rc;
+    gather_pair_rows_kernel<<<n, 128, 0, s>>>(static_cast<const __half *>(x), pairs, offsets + experts, top_k,
+                                              d_model, xg);
+    if ((rc = check_launch("expert gather launch"))) return rc;
+    // GEMM2 writes the output of grouped pair g to slot pairs[g] = row * k + r
+    if ((rc = run_expert_gemms(experts, expert_slots, up_offset, down_offset, gate_type, down_type, d_model, ffn,
+                               counts, offsets, n, xg, act, out, pairs, nullptr, s)))
+        return rc;
+    const uint64_t m = static_cast<uint64_t>(rows) * d_model;
+    ep_partial_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, s>>>(out, meta_expert, meta_weight, rows,
+                                                                             top_k, d_model, partial);
+    return check_launch("expert partial-sum launch");
+}
+
+extern "C" int fmcuda_ep_combine_rows(const float *back, const uint32_t *row_of, uint32_t tokens, uint32_t world,
+                                      uint32_t d_model, float *y, void *stream) {
+    if (!back || !row_of || !y) return set_error(FM_STATUS_INVALID_ARGUMENT, "null combine pointer");
+    if (tokens == 0) return FM_STATUS_OK;
+    const uint64_t m = static_cast<uint64_t>(tokens) * d_model;
+    ep_combine_rows_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        back, row_of, tokens, world, d_model, y);
+    return check_launch("combine rows launch");
+}
 
 extern "C" uint64_t fmcuda_ep_dispatch_scratch_bytes(uint32_t tokens, uint32_t top_k, uint32_t world) {
     const uint64_t P = static_cast<uint64_t>(tokens) * top_k;

@@ -200,7 +200,8 @@ int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_
     return check_launch("router launch");
 }
 
-// ---- grouping for large batches (prefill): the same outputs as group_kernel,
+// ---- grouping for large batches (prefill): the same outputs as group_kernel
+// (a key of 0xFFFFFFFF is an absent item: no group, no error),
 // computed by many warps.  Each warp owns 256 consecutive pairs; a pair's
 // place is offsets[e] + (pairs of expert e in earlier warps) + (earlier pairs
 // of expert e in its own warp), so the order inside an expert's group is
@@ -223,7 +224,8 @@ __global__ void group_count_kernel(const uint32_t *__restrict__ ids, uint32_t n_
         const bool valid = i < n_pairs;
         const uint32_t e = valid ? ids[i] : 0xFFFFFFFFu;
         const bool ok = valid && e < experts;
-        if (valid && !ok) raise_device_status(status, FM_STATUS_INVALID_EXPERT_ID);
+        // key 0xFFFFFFFF marks "no item" (skipped silently); any other key >= experts is an error
+        if (valid && !ok && e != 0xFFFFFFFFu) raise_device_status(status, FM_STATUS_INVALID_EXPERT_ID);
         const uint32_t key = ok ? e : 0xFFFFFFFEu - (valid ? 0u : 1u);
         const uint32_t peers = __match_any_sync(0xFFFFFFFFu, key);
         if (ok && __popc(peers & ((1u << lane) - 1u)) == 0) h[e] += __popc(peers);

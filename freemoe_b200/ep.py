@@ -12,6 +12,12 @@ on the grouped GEMM.  Expert e lives on rank e // (E / world).  One layer call:
   all-to-all     the f32 outputs back to the tokens' owners
   combine        y[t] = sum over r of w[t, r] * out[slot_of(t, r)] in top-k order
 
+That is ``mode="pairs"``: one row per (token, expert) pair each way, and a result
+equal to the one-GPU block bit for bit.  ``mode="rows"`` (the default) sends a
+token once to each rank that owns any of its experts (fmcuda_ep_dispatch_rows)
+and gets back one f32 partial sum per (token, rank) (fmcuda_moe_experts_partial,
+fmcuda_ep_combine_rows): less traffic, the same terms summed grouped by rank.
+
 The exchange uses ``torch.distributed.all_to_all_single`` on the group (NCCL
 over NVLink on GPUs).  The arithmetic is pluggable (``ops``): :class:`DeviceOps`
 calls the sm_100a library; the CPU tests plug in a host implementation to check
@@ -24,6 +30,15 @@ from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
+
+
+@dataclass
+class RowDispatch:
+    send_counts: torch.Tensor  # [world] int64
+    send_x: torch.Tensor       # [>= S, d] token rows, one per (token, destination)
+    meta_e: torch.Tensor       # [>= S, k] int32 local expert per top-k slot, -1 elsewhere
+    meta_w: torch.Tensor       # [>= S, k] f32 routing weight per slot, 0 elsewhere
+    row_of: torch.Tensor       # [T * world] int32 send row of (t, dest), -1 if none
 
 
 @dataclass
@@ -105,6 +120,48 @@ class DeviceOps:
             C.c_void_p(ws.data_ptr()), ws.numel(), self._stream()))
         return out
 
+    def dispatch_rows(self, ids: torch.Tensor, w: torch.Tensor, x: torch.Tensor, world: int) -> RowDispatch:
+        T, k = ids.shape
+        n, dev, d = T * world, ids.device, self.d
+        counts32 = torch.empty(world, dtype=torch.int32, device=dev)
+        offsets = torch.empty(world + 1, dtype=torch.int32, device=dev)
+        items = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        row_of = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+        send_x = torch.empty(max(n, 1), d, dtype=torch.float16, device=dev)
+        meta_e = torch.empty(max(n, 1), k, dtype=torch.int32, device=dev)
+        meta_w = torch.empty(max(n, 1), k, dtype=torch.float32, device=dev)
+        scratch = self._buf("dispatch_rows", self.lib.fmcuda_ep_dispatch_rows_scratch_bytes(T, world), dev)
+        xdt = self.X_BF16 if x.dtype == torch.bfloat16 else self.X_F32
+        P = C.c_void_p
+        self.check(self.lib.fmcuda_ep_dispatch_rows(
+            P(ids.data_ptr()), P(w.data_ptr()), T, k, self.E // world, world, P(x.data_ptr()), xdt, d,
+            P(counts32.data_ptr()), P(offsets.data_ptr()), P(items.data_ptr()), P(row_of.data_ptr()),
+            P(send_x.data_ptr()), P(meta_e.data_ptr()), P(meta_w.data_ptr()), P(scratch.data_ptr()),
+            self._stream()))
+        return RowDispatch(counts32.to(torch.int64), send_x, meta_e, meta_w, row_of)
+
+    def experts_partial(self, rows: torch.Tensor, meta_e: torch.Tensor, meta_w: torch.Tensor, n: int):
+        dev = rows.device
+        out = torch.empty(max(n, 1), self.d, dtype=torch.float32, device=dev)
+        if n == 0:
+            return out
+        per_rank = len(self.slots)
+        ws = self._buf("experts_partial", self.lib.fmcuda_moe_experts_partial_workspace_bytes(
+            n, self.k, per_rank, self.d, self.ffn), dev)
+        g, u, dn = self.types
+        P = C.c_void_p
+        self.check(self.lib.fmcuda_moe_experts_partial(
+            P(rows.data_ptr()), P(meta_e.data_ptr()), P(meta_w.data_ptr()), n, self.k, per_rank,
+            P(self.table.data_ptr()), self.up_offset, self.down_offset, g, u, dn, self.d, self.ffn,
+            P(out.data_ptr()), P(ws.data_ptr()), ws.numel(), self._stream()))
+        return out
+
+    def combine_rows(self, back: torch.Tensor, row_of: torch.Tensor, tokens: int, world: int) -> torch.Tensor:
+        y = torch.empty(tokens, self.d, dtype=torch.float32, device=back.device)
+        self.check(self.lib.fmcuda_ep_combine_rows(C.c_void_p(back.data_ptr()), C.c_void_p(row_of.data_ptr()),
+                                                   tokens, world, self.d, C.c_void_p(y.data_ptr()), self._stream()))
+        return y
+
     def combine(self, back: torch.Tensor, w: torch.Tensor, slot_of: torch.Tensor) -> torch.Tensor:
         T = w.shape[0]
         y = torch.empty(T, self.d, dtype=torch.float32, device=w.device)
@@ -119,8 +176,10 @@ class EPLayer:
 
     PHASES = ("route", "dispatch", "counts", "rows_out", "experts", "rows_back", "combine")
 
-    def __init__(self, ops, group=None, record_timing: bool = False):
-        self.ops, self.group = ops, group
+    def __init__(self, ops, group=None, record_timing: bool = False, mode: str = "rows"):
+        if mode not in ("rows", "pairs"):
+            raise ValueError(f"unknown exchange mode {mode!r}")
+        self.ops, self.group, self.mode = ops, group, mode
         self.record_timing = record_timing and torch.cuda.is_available()
         self._events = []
         self.world = dist.get_world_size(group)
@@ -146,31 +205,57 @@ class EPLayer:
         self._events = []
         return out
 
+    def _exchange_counts(self, send_counts):
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc = send_counts.cpu().tolist()  # the host needs both sides' sizes
+        rc = recv_counts.cpu().tolist()
+        return sc, rc
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits, group=self.group)
+
     def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
-        ops, g = self.ops, self.group
+        ops = self.ops
         self._mark()
         ids, w = ops.route(logits)
         self._mark()
-        plan = ops.dispatch(ids, x, self.world)
-        self._mark()
-        send_counts = plan.send_counts
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=g)
-        sc = send_counts.cpu().tolist()  # the host needs both sides' sizes
-        rc = recv_counts.cpu().tolist()
-        S, R = int(sum(sc)), int(sum(rc))
-        self._mark()
-        recv_x = ops.empty_rows(R, plan.send_x)
-        recv_e = torch.empty(max(R, 1), dtype=plan.send_expert.dtype, device=plan.send_expert.device)
-        dist.all_to_all_single(recv_x[:R], plan.send_x[:S], output_split_sizes=rc, input_split_sizes=sc, group=g)
-        dist.all_to_all_single(recv_e[:R], plan.send_expert[:S], output_split_sizes=rc, input_split_sizes=sc,
-                               group=g)
-        self._mark()
-        out = ops.experts(recv_x, recv_e, R)
-        self._mark()
-        back = torch.empty(max(S, 1), out.shape[1], dtype=out.dtype, device=out.device)
-        dist.all_to_all_single(back[:S], out[:R], output_split_sizes=sc, input_split_sizes=rc, group=g)
-        self._mark()
-        y = ops.combine(back, w, plan.slot_of)
+        if self.mode == "pairs":
+            plan = ops.dispatch(ids, x, self.world)
+            self._mark()
+            sc, rc = self._exchange_counts(plan.send_counts)
+            S, R = int(sum(sc)), int(sum(rc))
+            self._mark()
+            recv_x = ops.empty_rows(R, plan.send_x)
+            recv_e = torch.empty(max(R, 1), dtype=plan.send_expert.dtype, device=plan.send_expert.device)
+            self._a2a(recv_x[:R], plan.send_x[:S], rc, sc)
+            self._a2a(recv_e[:R], plan.send_expert[:S], rc, sc)
+            self._mark()
+            out = ops.experts(recv_x, recv_e, R)
+            self._mark()
+            back = torch.empty(max(S, 1), out.shape[1], dtype=out.dtype, device=out.device)
+            self._a2a(back[:S], out[:R], sc, rc)
+            self._mark()
+            y = ops.combine(back, w, plan.slot_of)
+        else:
+            plan = ops.dispatch_rows(ids, w, x, self.world)
+            self._mark()
+            sc, rc = self._exchange_counts(plan.send_counts)
+            S, R = int(sum(sc)), int(sum(rc))
+            self._mark()
+            k = plan.meta_e.shape[1]
+            recv_x = ops.empty_rows(R, plan.send_x)
+            recv_e = torch.empty(max(R, 1), k, dtype=plan.meta_e.dtype, device=plan.meta_e.device)
+            recv_w = torch.empty(max(R, 1), k, dtype=plan.meta_w.dtype, device=plan.meta_w.device)
+            self._a2a(recv_x[:R], plan.send_x[:S], rc, sc)
+            self._a2a(recv_e[:R], plan.meta_e[:S], rc, sc)
+            self._a2a(recv_w[:R], plan.meta_w[:S], rc, sc)
+            self._mark()
+            part = ops.experts_partial(recv_x, recv_e, recv_w, R)
+            self._mark()
+            back = torch.empty(max(S, 1), part.shape[1], dtype=part.dtype, device=part.device)
+            self._a2a(back[:S], part[:R], sc, rc)
+            self._mark()
+            y = ops.combine_rows(back, plan.row_of, x.shape[0], self.world)
         self._mark()
         return y

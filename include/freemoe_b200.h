@@ -303,6 +303,44 @@ int fmcuda_moe_experts(const void *x, const uint32_t *expert_of_row, uint32_t ro
 int fmcuda_moe_combine(const float *rows_out, const float *weights, const uint32_t *slot_of,
                        uint32_t tokens, uint32_t top_k, uint32_t d_model, float *y, void *stream);
 
+/* The de-duplicated exchange: a token goes once to each rank that owns at
+ * least one of its experts, and comes back as one partial sum per rank.
+ *
+ * fmcuda_ep_dispatch_rows: items t*world + dest (token t has a pair on rank
+ * dest) grouped by destination, ascending token order inside each block:
+ *   send_counts [world], send_offsets [world+1], send_items [T*world] (item of
+ *   send row j), row_of [T*world] (send row of item t*world + dest, or
+ *   0xFFFFFFFF), send_x [T*world * d_model] fp16, meta_expert [T*world * k]
+ *   (local expert of top-k slot r of send row j, -1 when that pair goes to
+ *   another rank), meta_weight [T*world * k] (its routing weight, else 0).
+ * `scratch`: fmcuda_ep_dispatch_rows_scratch_bytes() bytes.
+ *
+ * fmcuda_moe_experts_partial: for each received row, the outputs of its
+ * slots' experts combined in top-k order: partial[row] = sum over r of
+ * meta_weight[row*k + r] * down(silu(gate x) * up x) of expert meta_expert[...]
+ * (multiply then add, src/engine.cpp:1770).  Shapes as fmcuda_moe_prefill.
+ *
+ * fmcuda_ep_combine_rows: y[t] = sum over ranks (ascending) of the returned
+ * partial rows back[row_of[t*world + rank]].  The sum of each token's pairs is
+ * therefore grouped by rank: equal to the reference's top-k-order sum within
+ * the f32 rounding of the regrouping. */
+uint64_t fmcuda_ep_dispatch_rows_scratch_bytes(uint32_t tokens, uint32_t world);
+int fmcuda_ep_dispatch_rows(const uint32_t *ids, const float *weights, uint32_t tokens, uint32_t top_k,
+                            uint32_t experts_per_rank, uint32_t world, const void *x, int32_t x_dtype,
+                            uint32_t d_model, uint32_t *send_counts, uint32_t *send_offsets,
+                            uint32_t *send_items, uint32_t *row_of, void *send_x, int32_t *meta_expert,
+                            float *meta_weight, void *scratch, void *stream);
+uint64_t fmcuda_moe_experts_partial_workspace_bytes(uint32_t rows, uint32_t top_k, uint32_t experts,
+                                                    uint32_t d_model, uint32_t ffn);
+int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_expert, const float *meta_weight,
+                               uint32_t rows, uint32_t top_k, uint32_t experts,
+                               const void *const *expert_slots, uint64_t up_offset, uint64_t down_offset,
+                               uint32_t gate_type, uint32_t up_type, uint32_t down_type, uint32_t d_model,
+                               uint32_t ffn, float *partial, void *workspace, uint64_t workspace_bytes,
+                               void *stream);
+int fmcuda_ep_combine_rows(const float *back, const uint32_t *row_of, uint32_t tokens, uint32_t world,
+                           uint32_t d_model, float *y, void *stream);
+
 /* Size of the scratch built into the library for fmcuda_moe_block_noalloc. */
 #define FM_MOE_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 

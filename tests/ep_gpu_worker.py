@@ -2,7 +2,9 @@
 torchrun, one process per GPU, NCCL).  Every rank builds the same expert stack
 and token batch from seeds, keeps its expert shard and its token shard, runs
 EPLayer, and rank 0 compares the gathered output with fmcuda_moe_prefill over
-all experts on one GPU: identical bits are expected."""
+all experts on one GPU: identical bits in the per-pair exchange ("pairs"); in
+the de-duplicated exchange ("rows") the terms are summed grouped by rank, so
+the bar is 1e-5 of max |y|."""
 from __future__ import annotations
 
 import datetime
@@ -20,6 +22,7 @@ import torch.distributed as dist  # noqa: E402
 
 def main():
     E, k, d, ffn, T, t = (int(v) for v in sys.argv[1:7])
+    mode = sys.argv[7] if len(sys.argv) > 7 else "pairs"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -38,7 +41,7 @@ def main():
     per, tp = E // world, T // world
     ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
                     local_slots=slots[rank * per:(rank + 1) * per], up_offset=gb, down_offset=2 * gb)
-    layer = EPLayer(ops)
+    layer = EPLayer(ops, mode=mode)
     y = layer.forward(x[rank * tp:(rank + 1) * tp].contiguous(), logits[rank * tp:(rank + 1) * tp].contiguous())
     torch.cuda.synchronize()
     assert hotpath.device_status() == 0
@@ -50,8 +53,8 @@ def main():
         y_one = hotpath.moe_prefill(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
         same = torch.equal(y_ep.view(torch.int32), y_one.view(torch.int32))
         err = float((y_ep - y_one).abs().max() / y_one.abs().max())
-        print(f"ep world={world}: identical={same} max_rel={err:.3e}", flush=True)
-        ok[0] = int(same)
+        print(f"ep world={world} mode={mode}: identical={same} max_rel={err:.3e}", flush=True)
+        ok[0] = int(same) if mode == "pairs" else int(err <= 1e-5)
     dist.broadcast(ok, 0)
     dist.destroy_process_group()
     sys.exit(0 if ok.item() else 1)

@@ -5,7 +5,10 @@ arithmetic is plugged in as a host implementation built on the oracle (router,
 per-row expert FFN, combine), so the test checks what EPLayer itself does: the
 grouping by destination, the count and row exchanges with ragged and empty
 splits, the return of the outputs and the combine order.  The result must equal
-the oracle's single-process MoE block bit for bit.
+the oracle's single-process MoE block: bit for bit in the per-pair exchange
+(mode "pairs"); in the de-duplicated exchange (mode "rows", one row per token and
+destination rank, partial sums back) the same terms are summed grouped by rank,
+so the bar there is the f32 rounding of that regrouping.
 """
 from __future__ import annotations
 
@@ -67,6 +70,53 @@ class HostOps:
                                        self.ffn, self.t)
         return torch.from_numpy(out)
 
+    def dispatch_rows(self, ids, w, x, world):
+        from freemoe_b200.ep import RowDispatch
+
+        ids_np = ids.numpy().astype(np.int64)
+        T, k = ids_np.shape
+        per_rank = self.E // world
+        dest_of = ids_np // per_rank
+        items = [t * world + dst for dst in range(world) for t in range(T) if (dest_of[t] == dst).any()]
+        counts = np.bincount([i % world for i in items], minlength=world)
+        row_of = np.full(T * world, -1, dtype=np.int32)
+        row_of[np.array(items, dtype=np.int64)] = np.arange(len(items))
+        xs = x.numpy()
+        send_x = np.stack([xs[i // world] for i in items]) if items else np.zeros((1, self.d), np.float32)
+        meta_e = np.full((max(len(items), 1), k), -1, dtype=np.int32)
+        meta_w = np.zeros((max(len(items), 1), k), dtype=np.float32)
+        wn = w.numpy()
+        for j, i in enumerate(items):
+            t, dst = i // world, i % world
+            for r in range(k):
+                if dest_of[t, r] == dst:
+                    meta_e[j, r] = ids_np[t, r] % per_rank
+                    meta_w[j, r] = wn[t, r]
+        return RowDispatch(torch.from_numpy(counts.astype(np.int64)), torch.from_numpy(np.ascontiguousarray(send_x)),
+                           torch.from_numpy(meta_e), torch.from_numpy(meta_w), torch.from_numpy(row_of))
+
+    def experts_partial(self, rows, meta_e, meta_w, n):
+        out = np.zeros((max(n, 1), self.d), dtype=np.float32)
+        me, mw, xr = meta_e.numpy(), meta_w.numpy(), rows.numpy()
+        for j in range(n):
+            acc = np.zeros(self.d, dtype=np.float32)
+            for r in range(self.k):
+                if me[j, r] >= 0:
+                    o = self.o.moe_block(xr[j:j + 1], np.array([[me[j, r]]], np.uint32), np.ones((1, 1), np.float32),
+                                         self.slots, self.d, self.ffn, self.t)[0]
+                    acc = acc + np.float32(mw[j, r]) * o
+            out[j] = acc
+        return torch.from_numpy(out)
+
+    def combine_rows(self, back, row_of, tokens, world):
+        b, ro = back.numpy(), row_of.numpy()
+        y = np.zeros((tokens, self.d), dtype=np.float32)
+        for t in range(tokens):
+            for r in range(world):
+                if ro[t * world + r] >= 0:
+                    y[t] = y[t] + b[ro[t * world + r]]
+        return torch.from_numpy(y)
+
     def combine(self, back, w, slot_of):
         back, w, s = back.numpy(), w.numpy(), slot_of.numpy()
         T = w.shape[0]
@@ -92,7 +142,7 @@ def problem(oracle, case):
     return t, slots, x, logits
 
 
-def worker(rank, world, port, case, out_dir):
+def worker(rank, world, port, case, out_dir, mode):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import sys
 
@@ -106,7 +156,7 @@ def worker(rank, world, port, case, out_dir):
         t, slots, x, logits = problem(oracle, case)
         per = E // world
         ops = HostOps(oracle, slots, slots[rank * per:(rank + 1) * per], t)
-        layer = EPLayer(ops)
+        layer = EPLayer(ops, mode=mode)
         sl = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
         y = layer.forward(torch.from_numpy(x[sl]), torch.from_numpy(logits[sl]))
         np.save(os.path.join(out_dir, f"y{rank}.npy"), y.numpy())
@@ -114,13 +164,17 @@ def worker(rank, world, port, case, out_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["pairs", "rows"])
 @pytest.mark.parametrize("case", [0, 1])
-def test_ep_two_gloo_ranks_match_single_process(oracle, tmp_path, case):
+def test_ep_two_gloo_ranks_match_single_process(oracle, tmp_path, case, mode):
     world = 2
-    mp.start_processes(worker, args=(world, free_port(), case, str(tmp_path)), nprocs=world, start_method="spawn",
-                       join=True)
+    mp.start_processes(worker, args=(world, free_port(), case, str(tmp_path), mode), nprocs=world,
+                       start_method="spawn", join=True)
     y = np.concatenate([np.load(tmp_path / f"y{r}.npy") for r in range(world)])
     t, slots, x, logits = problem(oracle, case)
     rc, ids, w, _ = oracle.route(logits, K)
     y_ref = oracle.moe_block(x, ids, w, slots, D, FFN, t)
-    assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+    if mode == "pairs":
+        assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+    else:
+        assert np.max(np.abs(y - y_ref)) <= 1e-6 * np.max(np.abs(y_ref))
