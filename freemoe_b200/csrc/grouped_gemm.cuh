@@ -10,10 +10,13 @@
 // matrix (grouped order, see router.cu) and W are the expert's GGUF rows in
 // their stored Q8_0 / Q4_K bytes (src/quant.cpp:223-228, :297-318).
 //
-// Work unit = (expert e, tile of 128 weight rows, tile of <= 128 tokens); the
+// Work unit = (expert e, tile of 128 weight rows, tile of <= 192 tokens for
+// gate/up, <= 256 tokens for down; more tokens per unit = fewer conversions of
+// the same weights per FLOP, bounded by the 512 TMEM columns); the
 // persistent CTAs (one per SM) take units round-robin.  Inside a CTA:
-//   warp 0      TMA producer: 128-token x 64-value fp16 tiles of X (or act),
-//               128-byte swizzled, into a 4-stage ring (B operand);
+//   warp 0      TMA producer: 192-token (gate/up) or 256-token (down) x 64-value
+//               fp16 tiles of X (or act), 128-byte swizzled, into a 3- or 2-stage
+//               ring (B operand);
 //   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16,
 //               M = 128 weight rows, N = tokens of the tile (rounded to 16),
 //               K = 16 per instruction, A from TMEM, B from shared memory;
@@ -45,10 +48,25 @@
 namespace fmb {
 
 constexpr uint32_t GG_BM = 128;     // weight rows per tile (TMEM lanes)
-constexpr uint32_t GG_BN = 128;     // tokens per tile
+#ifndef FMB_GG_BN2
+#define FMB_GG_BN2 192
+#endif
+#ifndef FMB_GG_SA2
+#define FMB_GG_SA2 2
+#endif
+#ifndef FMB_GG_SB2
+#define FMB_GG_SB2 3
+#endif
+#ifndef FMB_GG_BN1
+#define FMB_GG_BN1 256
+#endif
+#ifndef FMB_GG_SB1
+#define FMB_GG_SB1 2
+#endif
+constexpr uint32_t GG_BN = FMB_GG_BN2;  // tokens per tile of the gate/up GEMM (two accumulators)
+constexpr uint32_t GG_BN1 = FMB_GG_BN1; // tokens per tile of the one-matrix GEMM (one accumulator)
 constexpr uint32_t GG_BK = 64;      // K values per MMA stage (one 128-byte fp16 row)
 constexpr uint32_t GG_CHUNK = 256;  // K values per raw chunk (one Q4_K block, eight Q8_0 blocks)
-constexpr uint32_t GG_SB = 4;       // B ring stages
 constexpr uint32_t GG_THREADS = 384;
 constexpr uint32_t GG_TMEM_COLS = 512;
 constexpr uint32_t GG_MAX_EXPERTS = 1024;
@@ -80,20 +98,24 @@ template <> struct GGeom<FM_TYPE_Q4_K> {
 };
 
 template <int TYPE, int NMAT> struct GGLayout {
-    static constexpr uint32_t SA = NMAT == 2 ? 4 : 8;          // A stages in TMEM
-    static constexpr uint32_t A_COL0 = NMAT * GG_BN;            // accumulators first
+    static constexpr uint32_t BN = NMAT == 2 ? GG_BN : GG_BN1;  // tokens per unit
+    static constexpr uint32_t SB = NMAT == 2 ? FMB_GG_SB2 : FMB_GG_SB1; // B ring stages
+    static constexpr uint32_t SA = NMAT == 2 ? FMB_GG_SA2 : 8;          // A stages in TMEM
+    static constexpr uint32_t A_COL0 = NMAT * BN;               // accumulators first
     static constexpr uint32_t A_STAGE_COLS = NMAT * (GG_BK / 2); // fp16 pairs per column
     static constexpr uint32_t PITCH = GGeom<TYPE>::CB;         // raw row pitch (odd multiple of 16)
     static constexpr uint32_t RS = GGeom<TYPE>::RS;
-    static constexpr uint32_t B_STAGE = GG_BN * GG_BK * 2;
+    static constexpr uint32_t B_STAGE = BN * GG_BK * 2;
     static constexpr uint32_t RAW_SLOT = 32 * PITCH;
     static constexpr uint32_t RAW_WARP = RS * RAW_SLOT;
-    static constexpr uint32_t OFF_RAW = GG_SB * B_STAGE;
+    static constexpr uint32_t OFF_RAW = SB * B_STAGE;
     static constexpr uint32_t OFF_BAR = OFF_RAW + 8 * RAW_WARP;
-    static constexpr uint32_t NBAR = 2 * GG_SB + 2 * SA + 3;
+    static constexpr uint32_t NBAR = 2 * SB + 2 * SA + 3;
     static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr uint32_t OFF_UNITS = OFF_MISC + 16;
     static_assert(A_COL0 + SA * A_STAGE_COLS <= GG_TMEM_COLS, "TMEM budget");
+    static_assert(BN % 64 == 0 && BN <= 256, "token tile: two warpgroups x 32-column loads");
+    static_assert((SB * B_STAGE) % 1024 == 0, "1024-byte aligned raw rings");
     static_assert(PITCH % 16 == 0 && (PITCH / 16) % 2 == 1, "conflict-free 16-byte row reads");
     static constexpr uint32_t smem_bytes(uint32_t experts) { return 1024 + OFF_UNITS + 4 * (experts + 1); }
 };
@@ -105,6 +127,7 @@ struct GUnit {
 // Unit u -> (expert, row tile, token tile).  s_units[e] is the first unit of
 // expert e (exclusive prefix over experts of token_tiles * row_tiles); token
 // tiles vary fastest, so CTAs running side by side share a weight tile in L2.
+template <uint32_t BN>
 __device__ __forceinline__ GUnit gg_unit(const uint32_t *s_units, uint32_t experts, uint32_t u,
                                          const uint32_t *counts, const uint32_t *offsets) {
     uint32_t lo = 0, hi = experts;
@@ -116,12 +139,12 @@ __device__ __forceinline__ GUnit gg_unit(const uint32_t *s_units, uint32_t exper
     GUnit g;
     g.e = lo;
     const uint32_t cnt = __ldg(counts + lo);
-    const uint32_t tiles = (cnt + GG_BN - 1) / GG_BN;
+    const uint32_t tiles = (cnt + BN - 1) / BN;
     const uint32_t local = u - s_units[lo];
     g.rt = local / tiles;
     const uint32_t tt = local - g.rt * tiles;
-    g.n_tok = min(GG_BN, cnt - tt * GG_BN);
-    g.row_b0 = __ldg(offsets + lo) + tt * GG_BN;
+    g.n_tok = min(BN, cnt - tt * BN);
+    g.row_b0 = __ldg(offsets + lo) + tt * BN;
     return g;
 }
 
@@ -229,7 +252,7 @@ template <int TYPE, int NMAT, int EPI, int G>
 __global__ void __launch_bounds__(GG_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_b, const GGemmParams p) {
     using L = GGLayout<TYPE, NMAT>;
-    constexpr uint32_t SB = GG_SB, SA = L::SA, RS = L::RS, CB = GGeom<TYPE>::CB;
+    constexpr uint32_t SB = L::SB, SA = L::SA, RS = L::RS, CB = GGeom<TYPE>::CB, BN = L::BN;
     extern __shared__ uint8_t gg_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gg_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sB = smem;
@@ -261,7 +284,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
         for (uint32_t base = 0; base < E; base += 32) {
             const uint32_t e = base + lane;
             uint32_t v = 0;
-            if (e < E) v = ((__ldg(p.counts + e) + GG_BN - 1) / GG_BN) * row_tiles;
+            if (e < E) v = ((__ldg(p.counts + e) + BN - 1) / BN) * row_tiles;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, v, o);
@@ -316,7 +339,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
         if (lane == 0) {
             uint32_t it = 0;
             for (uint32_t u = blockIdx.x; u < U && !*abort_flag; u += gridDim.x) {
-                const GUnit g = gg_unit(s_units, E, u, p.counts, p.offsets);
+                const GUnit g = gg_unit<BN>(s_units, E, u, p.counts, p.offsets);
                 for (uint32_t s = 0; s < ksteps; ++s, ++it) {
                     const uint32_t st = it % SB;
                     if (!gg_wait(&b_release[st], ((it / SB) & 1u) ^ 1u, abort_flag, p.status)) goto producer_done;
@@ -335,7 +358,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
             uint32_t it = 0, acc_it = 0;
             bool issued = false;
             for (uint32_t u = blockIdx.x; u < U; u += gridDim.x, ++acc_it) {
-                const GUnit g = gg_unit(s_units, E, u, p.counts, p.offsets);
+                const GUnit g = gg_unit<BN>(s_units, E, u, p.counts, p.offsets);
                 const uint32_t idesc = idesc_f16_m128((g.n_tok + 15u) & ~15u);
                 if (!gg_wait(acc_empty, (acc_it & 1u) ^ 1u, abort_flag, p.status)) break;
                 tc_fence_after();
@@ -350,7 +373,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
                         const uint64_t bd = smem_desc_sw128(bsa + kk * 32u);
 #pragma unroll
                         for (uint32_t m = 0; m < static_cast<uint32_t>(NMAT); ++m)
-                            mma_f16_ts(tmem + m * GG_BN, tmem + L::A_COL0 + ast * L::A_STAGE_COLS + m * 32u + kk * 8u,
+                            mma_f16_ts(tmem + m * BN, tmem + L::A_COL0 + ast * L::A_STAGE_COLS + m * 32u + kk * 8u,
                                        bd, idesc, (s | kk) != 0u);
                     }
                     issued = true;
@@ -391,7 +414,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
             if (j < njobs) {
                 const uint32_t n_ord = j / J, ch = c0 + (j - n_ord * J) * cstep;
                 if (n_ord != iss_nord) {
-                    const GUnit g = gg_unit(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
+                    const GUnit g = gg_unit<BN>(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
                     iss_row0 = p.slots[g.e] + w_off + static_cast<uint64_t>(g.rt * GG_BM + wq * 32u) * p.row_bytes;
                     iss_nord = n_ord;
                 }
@@ -419,7 +442,7 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
         for (uint32_t j = 0; j < RS; ++j) issue(j);
         uint32_t j = 0;
         for (uint32_t n_ord = 0; n_ord < my_units; ++n_ord) {
-            const GUnit g = gg_unit(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
+            const GUnit g = gg_unit<BN>(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
             for (uint32_t jj = 0; jj < J; ++jj, ++j) {
                 const uint32_t ch = c0 + jj * cstep;
                 cp_async_wait<RS - 1>();
@@ -453,15 +476,15 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
             if (!gg_wait(acc_full, n_ord & 1u, abort_flag, p.status)) goto conv_done;
             tc_fence_after();
 #pragma unroll 1
-            for (uint32_t h = 0; h < 2; ++h) {
-                const uint32_t j0 = wg * 64u + h * 32u;
+            for (uint32_t h = 0; h < BN / 64; ++h) {
+                const uint32_t j0 = wg * (BN / 2) + h * 32u;
                 if (j0 >= g.n_tok) break;
                 uint32_t a[32];
                 tmem_ld32(tmem + lane_addr + j0, a);
                 const uint32_t orow0 = g.rt * GG_BM + row_in_tile;
                 if constexpr (EPI == GG_EPI_SWIGLU) {
                     uint32_t b[32];
-                    tmem_ld32(tmem + lane_addr + GG_BN + j0, b);
+                    tmem_ld32(tmem + lane_addr + BN + j0, b);
                     tmem_wait_ld();
                     __half *out = static_cast<__half *>(p.out);
 #pragma unroll

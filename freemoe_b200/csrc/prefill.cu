@@ -130,13 +130,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// fp16 matrix [rows][cols], row-major, as 64 x 128 boxes with 128-byte swizzle.
-int make_b_map(CUtensorMap *map, const __half *base, uint32_t rows, uint32_t cols) {
+// fp16 matrix [rows][cols], row-major, as 64-value x box_rows boxes with 128-byte swizzle.
+int make_b_map(CUtensorMap *map, const __half *base, uint32_t rows, uint32_t cols, uint32_t box_rows) {
     auto enc = tensor_map_encoder();
     if (!enc) return set_error(FM_STATUS_INTERNAL_ERROR, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-    const cuuint32_t box[2] = {GG_BK, GG_BN};
+    const cuuint32_t box[2] = {GG_BK, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -223,11 +223,11 @@ int run_expert_gemms(uint32_t experts, const void *const *slots, uint64_t up_off
     const uint64_t gu_rb = row_bytes(gu_type, d), dn_rb = row_bytes(dn_type, ffn);
     const int g1 = copy_granule(gu_type, gu_rb, 0, up_offset);
     const int g2 = copy_granule(dn_type, dn_rb, down_offset, down_offset);
-    const uint32_t tiles_max = rows / GG_BN + experts;
+    const uint32_t tiles_max1 = rows / GG_BN + experts, tiles_max2 = rows / GG_BN1 + experts;
 
     CUtensorMap map1, map2;
-    if ((rc = make_b_map(&map1, xg, rows, d))) return rc;
-    if ((rc = make_b_map(&map2, act, rows, ffn))) return rc;
+    if ((rc = make_b_map(&map1, xg, rows, d, GG_BN))) return rc;
+    if ((rc = make_b_map(&map2, act, rows, ffn, GG_BN1))) return rc;
     GGemmParams p1{};
     p1.slots = reinterpret_cast<const uint8_t *const *>(slots);
     p1.w_off0 = 0;
@@ -240,7 +240,7 @@ int run_expert_gemms(uint32_t experts, const void *const *slots, uint64_t up_off
     p1.offsets = offsets;
     p1.out = act;
     p1.status = device_status_word();
-    if ((rc = launch_gg<2, GG_EPI_SWIGLU>(gu_type, p1, map1, tiles_max * (ffn / GG_BM), g1, s))) return rc;
+    if ((rc = launch_gg<2, GG_EPI_SWIGLU>(gu_type, p1, map1, tiles_max1 * (ffn / GG_BM), g1, s))) return rc;
     if (mark) {
         (*mark)(4);
         (*mark)(5);
@@ -254,7 +254,7 @@ int run_expert_gemms(uint32_t experts, const void *const *slots, uint64_t up_off
     p2.row_bytes = static_cast<uint32_t>(dn_rb);
     p2.out = part;
     p2.out_rows = part_rows;
-    return launch_gg<1, GG_EPI_F32>(dn_type, p2, map2, tiles_max * (d / GG_BM), g2, s);
+    return launch_gg<1, GG_EPI_F32>(dn_type, p2, map2, tiles_max2 * (d / GG_BM), g2, s);
 }
 
 int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, void *workspace,
