@@ -94,6 +94,41 @@ __global__ void gather_rows_kernel(const XT *__restrict__ x, const uint32_t *__r
     }
 }
 
+// The same gather, 8 values per thread step (16-byte fp16 stores); x rows
+// 16-byte aligned.
+template <typename XT>
+__global__ void gather_rows8_kernel(const XT *__restrict__ x, const uint32_t *__restrict__ pairs, uint32_t top_k,
+                                    uint32_t n_pairs, uint32_t n_rows, uint32_t d, __half *__restrict__ xg) {
+    const uint32_t i = blockIdx.x;
+    if (i >= n_rows) return;
+    const uint32_t tok = i < n_pairs ? pairs[i] / top_k : i - n_pairs;
+    const XT *src = x + static_cast<uint64_t>(tok) * d;
+    uint4 *dst = reinterpret_cast<uint4 *>(xg + static_cast<uint64_t>(i) * d);
+    for (uint32_t c = threadIdx.x; c < d / 8; c += blockDim.x) {
+        float v[8];
+        if constexpr (sizeof(XT) == 2) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(src) + c);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                v[2 * q] = bf16_bits_to_f32(static_cast<uint16_t>(w[q] & 0xFFFFu));
+                v[2 * q + 1] = bf16_bits_to_f32(static_cast<uint16_t>(w[q] >> 16));
+            }
+        } else {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(src) + 2 * c);
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(src) + 2 * c + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        uint4 o;
+        o.x = pack_half2(v[0], v[1]);
+        o.y = pack_half2(v[2], v[3]);
+        o.z = pack_half2(v[4], v[5]);
+        o.w = pack_half2(v[6], v[7]);
+        dst[c] = o;
+    }
+}
+
 // One-expert group for the shared expert: all tokens, in order.
 __global__ void shared_group_kernel(uint32_t *counts, uint32_t *offsets, const void **slot_tab, const void *slot,
                                     uint32_t tokens) {
@@ -317,12 +352,22 @@ int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, vo
         return rc;
     mark(2);
     const uint32_t n_rows = P + (sh ? a->tokens : 0);
-    if (a->x_dtype == FM_X_F32)
-        gather_rows_kernel<float><<<n_rows, 128, 0, s>>>(static_cast<const float *>(a->x), pairs, a->top_k, P,
-                                                          n_rows, a->d_model, xg);
-    else
-        gather_rows_kernel<__nv_bfloat16><<<n_rows, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(a->x), pairs,
-                                                                  a->top_k, P, n_rows, a->d_model, xg);
+    const bool x16 = reinterpret_cast<uintptr_t>(a->x) % 16 == 0; // rows then aligned too (d % 128 == 0)
+    if (a->x_dtype == FM_X_F32) {
+        if (x16)
+            gather_rows8_kernel<float><<<n_rows, 128, 0, s>>>(static_cast<const float *>(a->x), pairs, a->top_k, P,
+                                                               n_rows, a->d_model, xg);
+        else
+            gather_rows_kernel<float><<<n_rows, 128, 0, s>>>(static_cast<const float *>(a->x), pairs, a->top_k, P,
+                                                              n_rows, a->d_model, xg);
+    } else {
+        if (x16)
+            gather_rows8_kernel<__nv_bfloat16><<<n_rows, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(a->x),
+                                                                       pairs, a->top_k, P, n_rows, a->d_model, xg);
+        else
+            gather_rows_kernel<__nv_bfloat16><<<n_rows, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(a->x),
+                                                                      pairs, a->top_k, P, n_rows, a->d_model, xg);
+    }
     if ((rc = check_launch("gather launch"))) return rc;
     mark(3);
     if ((rc = run_expert_gemms(a->experts, a->expert_slots, a->up_offset, a->down_offset, a->gate_type,
