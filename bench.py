@@ -630,6 +630,105 @@ def run_layer(args):
     print(json.dumps(line), flush=True)
 
 
+# The quantised GEMV shapes of the reference's own kernel benchmark
+# (`freemoe bench`, src/main.cpp:631-637): attention projections, a small
+# expert and the output head, one token.
+GEMV_SHAPES = (
+    ("qkv_1280x1280_q8_0", 1280, 1280, 8),
+    ("qkv_1280x1280_q4_k", 1280, 1280, 12),
+    ("expert_gate_1792x1280_q4_k", 1792, 1280, 12),
+    ("expert_down_1280x1792_q4_k", 1280, 1792, 12),
+    ("output_head_32000x1280_q4_k", 32000, 1280, 12),
+)
+
+
+def run_gemv_shapes(args):
+    """fmcuda_gemv on the reference benchmark's quantised GEMV shapes at T=1
+    (bf16 x), device-resident and through host buffers, beside the reference's
+    own gemv_quant on the host cores."""
+    import numpy as np
+    import torch
+
+    from freemoe_b200 import hotpath
+
+    hotpath.init(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    rows = []
+    ref = None
+    if not args.no_cpu:
+        from oracle.oracle import Reference, reference_available
+
+        ref = Reference() if reference_available() else None
+    with ClockSampler(0) as clocks:
+        for label, out_dim, in_dim, t in GEMV_SHAPES:
+            w = hotpath.synth_weights(t, out_dim, in_dim, seed=11)
+            x = torch.randn(1, in_dim, device=dev).to(torch.bfloat16)
+            y = torch.empty(1, out_dim, dtype=torch.float32, device=dev)
+            lib = hotpath.load()
+            gs = torch.cuda.Stream()
+            call = (t, C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), 1, out_dim,
+                    in_dim, C.c_void_p(gs.cuda_stream))
+            with torch.cuda.stream(gs):
+                for _ in range(max(args.warmup, 3)):
+                    hotpath.check(lib.fmcuda_gemv(*call))
+            torch.cuda.synchronize()
+            # device time: the calls captured once into a CUDA graph (host launch
+            # overhead out of the measurement), replayed
+            reps = 100
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=gs):
+                for _ in range(reps):
+                    hotpath.check(lib.fmcuda_gemv(*call))
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n_rep = max(1, args.steps // reps)
+            e0.record(stream)
+            for _ in range(n_rep):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / (n_rep * reps) * 1e3
+            del graph
+            hx = x.cpu().pin_memory()
+            hy = torch.empty(1, out_dim, dtype=torch.float32).pin_memory()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                dx = hx.to(dev, non_blocking=True)
+                y = hotpath.gemv_quant(t, w, dx, out_dim, in_dim)
+                hy.copy_(y, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us_e2e = e0.elapsed_time(e1) / args.steps * 1e3
+            nbytes = out_dim * row_bytes(t, in_dim)
+            row = {"shape": label, "us": us, "gbytes_per_s": nbytes / us / 1e3, "e2e_us": us_e2e,
+                   "weights_bytes": nbytes, "l2": "weights L2-resident between calls" if nbytes < 100e6 else "HBM"}
+            if ref is not None:
+                wh = w.cpu().numpy()
+                xh = x.float().cpu().numpy().ravel()
+                threads = os.cpu_count() or 1
+                ref.gemv_quant(t, wh, xh, out_dim, in_dim, threads=threads)
+                n, t0 = 0, time.perf_counter()
+                while n < 20 or time.perf_counter() - t0 < 1.0:
+                    ref.gemv_quant(t, wh, xh, out_dim, in_dim, threads=threads)
+                    n += 1
+                cpu_us = (time.perf_counter() - t0) / n * 1e6
+                row["reference_cpu_us"] = cpu_us
+                row["reference_cpu_gbytes_per_s"] = nbytes / cpu_us / 1e3
+                row["reference_cpu_threads"] = threads
+            rows.append(row)
+    head = rows[-1]
+    line = {"metric": METRIC, "value": head["gbytes_per_s"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["us"] / 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k/q8_0", "data": "synthetic",
+            "config": {"workload": "quantised GEMV shapes of the reference kernel benchmark (src/main.cpp:631-637), "
+                                   "T=1 bf16; value = output head", "tokens": 1},
+            "shapes": rows, "gpu_launches": args.steps * 2, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_layer_ep(args):
     """The Qwen3-shaped layer expert-parallel over the torchrun ranks (NCCL):
     experts 128/G per rank, tokens 8192/G per rank (strong scaling), token rows
@@ -741,11 +840,14 @@ def main():
     ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--config", default="stack", choices=["stack", *LAYERS],
+    ap.add_argument("--config", default="stack", choices=["stack", *LAYERS, "gemv"],
                     help="stack (default, the headline) or a layer configuration")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     args.tokens_set = any(a.startswith("--tokens") for a in sys.argv[1:])
+    if args.config == "gemv" and args.impl == "ours":
+        run_gemv_shapes(args)
+        return
     if args.config != "stack" and args.impl == "ours":
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:
             run_layer_ep(args)

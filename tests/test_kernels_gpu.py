@@ -209,6 +209,21 @@ def test_group_batched_vs_oracle(cuda, oracle, E, k, T):
     assert np.array_equal(slot_of.cpu().numpy().astype(np.uint32), s_o)
 
 
+@pytest.mark.parametrize("out_dim,in_dim,t", [(1280, 1280, TYPE_Q8_0), (1280, 1280, TYPE_Q4_K),
+                                               (1792, 1280, TYPE_Q4_K), (1280, 1792, TYPE_Q4_K),
+                                               (32000, 1280, TYPE_Q4_K)])
+def test_gemv_reference_bench_shapes(cuda, oracle, out_dim, in_dim, t):
+    # the quantised GEMV shapes of the reference's kernel benchmark (src/main.cpp:631-637)
+    w = cuda.synth_weights(t, out_dim, in_dim, seed=out_dim + in_dim)
+    x = torch.randn(1, in_dim, device="cuda")
+    y = cuda.gemv_quant(t, w, x, out_dim, in_dim).cpu().numpy().ravel()
+    rows = np.arange(0, out_dim, max(1, out_dim // 512))
+    rb = w.numel() // out_dim
+    wr = w.cpu().numpy().reshape(out_dim, rb)[rows].ravel()
+    ref = oracle.gemv_f64(t, wr, x.cpu().numpy().ravel(), len(rows), in_dim)[0]
+    assert rel_err(y[rows], ref) < TOL
+
+
 # ---------------------------------------------------------------- MoE block
 
 def make_experts(oracle, rng, E, d, ffn, t):
