@@ -81,6 +81,24 @@ class MoeArgs(C.Structure):
         ("ids_out", C.c_void_p),
         ("weights_out", C.c_void_p),
         ("stage_events", C.c_void_p),
+        ("router", C.c_void_p),
+    ]
+
+
+GATING_SOFTMAX, GATING_SIGMOID, GATING_SQRT_SOFTPLUS, GATING_SOFTMAX_WEIGHT = 0, 1, 2, 3
+
+
+class RouterConfig(C.Structure):
+    _fields_ = [
+        ("gating", C.c_int32),
+        ("logit_bias", C.c_void_p),
+        ("selection_bias", C.c_void_p),
+        ("groups", C.c_uint32),
+        ("groups_used", C.c_uint32),
+        ("normalise", C.c_int32),
+        ("epsilon_additive", C.c_int32),
+        ("epsilon", C.c_double),
+        ("scale", C.c_double),
     ]
 
 
@@ -132,6 +150,7 @@ SIGNATURES = [
     ("fmcuda_gemv", C.c_int, [_U32, _P, _P, _I32, _P, _U32, _U32, _U32, _P]),
     ("fmcuda_matvec_f32", C.c_int, [_P, _P, _P, _U32, _U32, _I32, _P]),
     ("fmcuda_route", C.c_int, [_P, _U32, _U32, _U32, _I32, _D, _D, _P, _P, _P, _P]),
+    ("fmcuda_route_ex", C.c_int, [_P, _U32, _U32, _U32, C.POINTER(RouterConfig), _P, _P, _P, _P]),
     ("fmcuda_group", C.c_int, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _P]),
     ("fmcuda_group_scratch_bytes", C.c_uint64, [_U32, _U32]),
     ("fmcuda_group_batched", C.c_int, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _P, _P]),

@@ -22,9 +22,9 @@
 
 namespace fmb {
 
-int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
-                 int32_t normalise, double epsilon, double scale, uint32_t *ids, float *weights,
-                 float *probs, cudaStream_t s);
+int launch_route_cfg(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                     const fmcuda_router_config *cfg, int32_t normalise, double epsilon, double scale,
+                     uint32_t *ids, float *weights, float *probs, cudaStream_t s);
 int launch_group(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
                  uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, cudaStream_t s);
 int check_route_args(uint32_t experts, uint32_t top_k);
@@ -343,7 +343,7 @@ int moe_prefill_run(const fmcuda_moe_args *a, const fmcuda_shared_expert *sh, vo
     };
 
     mark(0);
-    if ((rc = launch_route(a->logits, a->tokens, a->experts, a->top_k, a->normalise, a->epsilon, a->scale, ids,
+    if ((rc = launch_route_cfg(a->logits, a->tokens, a->experts, a->top_k, a->router, a->normalise, a->epsilon, a->scale, ids,
                            weights, nullptr, s)))
         return rc;
     mark(1);

@@ -10,11 +10,17 @@
 //            w = float(w / max(double(total), eps)), then float(w * scale).
 // The double sum runs in index order on one lane so that it rounds exactly as
 // the reference's loop does.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace fmb {
 
 constexpr int kMaxExperts = 1024;
+
+int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                 int32_t normalise, double epsilon, double scale, uint32_t *ids, float *weights,
+                 float *probs, cudaStream_t s);
 
 __global__ void route_kernel(const float *__restrict__ logits, uint32_t tokens, uint32_t experts,
                              uint32_t top_k, int normalise, double epsilon, double scale,
@@ -189,6 +195,219 @@ __global__ void group_kernel(const uint32_t *__restrict__ ids, uint32_t n_pairs,
 using namespace fmb;
 
 namespace fmb {
+// ---- the router's model-family variants (src/engine.cpp:1603-1702) ---------
+//
+//   logit bias      scores[e] += bias[e] (float)                     :1608-1613
+//   gating          softmax (Engine::softmax), sigmoid float(1/(1+exp(-(double)s))),
+//                   sqrt-softplus float(sqrt(log1p(exp((double)s)))), or
+//                   softmax-weight (probabilities = the logits)      :1618-1633
+//   selection bias  selection[e] = probs[e] + bias[e] (float), picks only :1637-1643
+//   groups          keep the groups_used groups whose two best selection values
+//                   sum highest (float; stable, ties to the lower group), mask
+//                   the others to -inf                               :1644-1675
+//   top-k           Engine::topk on the selection; NaN or +inf is INTERNAL_ERROR,
+//                   -inf (masked) is allowed                         :1676, :395-411
+//   weights         probs of the picked experts; total = float sum in top-k order;
+//                   softmax-weight softmaxes the picked weights; renormalise by
+//                   max(double(total), eps) or double(total) + eps; float(w*scale)
+//                                                                    :1677-1702
+// One warp per token, as route_kernel.
+
+__device__ __forceinline__ void warp_top2(float &a, float &b) {
+    // merge each lane's (a >= b) pair across the warp
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xFFFFFFFFu, a, o), ob = __shfl_xor_sync(0xFFFFFFFFu, b, o);
+        const float hi = fmaxf(a, oa), lo = fmaxf(fminf(a, oa), fmaxf(b, ob));
+        a = hi;
+        b = lo;
+    }
+}
+
+__global__ void route_ex_kernel(const float *__restrict__ logits, uint32_t tokens, uint32_t experts,
+                                uint32_t top_k, fmcuda_router_config cfg, uint32_t *__restrict__ ids,
+                                float *__restrict__ weights, float *__restrict__ probs_out, int *status) {
+    extern __shared__ unsigned char smem_raw[];
+    const int warps = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t per_warp = static_cast<size_t>(experts) * 20; // double ex + float pr, sel, gsum
+    unsigned char *base = smem_raw + static_cast<size_t>(warp) * per_warp;
+    double *ex = reinterpret_cast<double *>(base);
+    float *pr = reinterpret_cast<float *>(base + static_cast<size_t>(experts) * 8);
+    float *sel = pr + experts;
+    float *gsum = sel + experts;
+    const uint32_t t = blockIdx.x * warps + warp;
+    if (t >= tokens) return;
+    const float *v = logits + static_cast<uint64_t>(t) * experts;
+    auto fail_token = [&]() {
+        if (lane == 0) raise_device_status(status, FM_STATUS_INTERNAL_ERROR);
+        for (uint32_t r = lane; r < top_k; r += 32) {
+            ids[static_cast<uint64_t>(t) * top_k + r] = 0xFFFFFFFFu;
+            weights[static_cast<uint64_t>(t) * top_k + r] = 0.0f;
+        }
+    };
+
+    // scores (+ logit bias) and the gating function
+    float mx = -INFINITY;
+    bool bad = false;
+    for (uint32_t e = lane; e < experts; e += 32) {
+        float x = v[e];
+        if (cfg.logit_bias) x = __fadd_rn(x, cfg.logit_bias[e]);
+        pr[e] = x;
+        bad |= !isfinite(x);
+        mx = fmaxf(mx, x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (cfg.gating == FM_GATING_SOFTMAX && __any_sync(0xFFFFFFFFu, bad)) { // Engine::softmax's check
+        fail_token();
+        return;
+    }
+    __syncwarp();
+    if (cfg.gating == FM_GATING_SOFTMAX) {
+        for (uint32_t e = lane; e < experts; e += 32)
+            ex[e] = exp(static_cast<double>(pr[e]) - static_cast<double>(mx));
+        __syncwarp();
+        double sum = 0.0;
+        if (lane == 0)
+            for (uint32_t e = 0; e < experts; ++e) sum += ex[e];
+        sum = __shfl_sync(0xFFFFFFFFu, sum, 0);
+        for (uint32_t e = lane; e < experts; e += 32) pr[e] = static_cast<float>(ex[e] / sum);
+    } else if (cfg.gating == FM_GATING_SIGMOID) {
+        for (uint32_t e = lane; e < experts; e += 32)
+            pr[e] = static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(pr[e]))));
+    } else if (cfg.gating == FM_GATING_SQRT_SOFTPLUS) {
+        for (uint32_t e = lane; e < experts; e += 32)
+            pr[e] = static_cast<float>(sqrt(log1p(exp(static_cast<double>(pr[e])))));
+    } // FM_GATING_SOFTMAX_WEIGHT: the probabilities are the scores
+    __syncwarp();
+    bad = false;
+    for (uint32_t e = lane; e < experts; e += 32) {
+        if (probs_out) probs_out[static_cast<uint64_t>(t) * experts + e] = pr[e];
+        float s = pr[e];
+        if (cfg.selection_bias) s = __fadd_rn(s, cfg.selection_bias[e]);
+        sel[e] = s;
+        bad |= isnan(s) || s == INFINITY;
+    }
+    if (__any_sync(0xFFFFFFFFu, bad)) { // Engine::topk's check
+        fail_token();
+        return;
+    }
+    __syncwarp();
+
+    // group-limited selection
+    if (cfg.groups > 1) {
+        const uint32_t per = experts / cfg.groups;
+        for (uint32_t g = 0; g < cfg.groups; ++g) {
+            float a = -INFINITY, b = -INFINITY;
+            for (uint32_t e = lane; e < per; e += 32) {
+                const float x = sel[g * per + e];
+                if (x > a) {
+                    b = a;
+                    a = x;
+                } else if (x > b) {
+                    b = x;
+                }
+            }
+            warp_top2(a, b);
+            if (lane == 0) gsum[g] = per >= 2 ? __fadd_rn(__fadd_rn(0.0f, a), b) : __fadd_rn(0.0f, a);
+        }
+        __syncwarp();
+        for (uint32_t g = lane; g < cfg.groups; g += 32) {
+            uint32_t rank = 0;
+            for (uint32_t h = 0; h < cfg.groups; ++h)
+                rank += (gsum[h] > gsum[g]) || (gsum[h] == gsum[g] && h < g);
+            if (rank >= cfg.groups_used)
+                for (uint32_t e = 0; e < per; ++e) sel[g * per + e] = -INFINITY;
+        }
+        __syncwarp();
+    }
+
+    // top-k over the selection: value descending, id ascending; taken = NaN
+    uint32_t my_id = 0xFFFFFFFFu;
+    float my_w = 0.0f;
+    for (uint32_t r = 0; r < top_k; ++r) {
+        float bv = -INFINITY;
+        uint32_t bi = 0xFFFFFFFFu;
+        for (uint32_t e = lane; e < experts; e += 32) {
+            const float p = sel[e];
+            if (p > bv || (bi == 0xFFFFFFFFu && p == bv)) {
+                bv = p;
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+            if (oi != 0xFFFFFFFFu && (bi == 0xFFFFFFFFu || ov > bv || (ov == bv && oi < bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == static_cast<int>(r)) {
+            my_id = bi;
+            my_w = pr[bi];
+        }
+        __syncwarp();
+        if (lane == 0) sel[bi] = __int_as_float(0x7FC00000); // NaN: never picked again
+        __syncwarp();
+    }
+    float total = 0.0f;
+    for (uint32_t r = 0; r < top_k; ++r) total = __fadd_rn(total, __shfl_sync(0xFFFFFFFFu, my_w, r));
+    float w = my_w;
+    if (cfg.gating == FM_GATING_SOFTMAX_WEIGHT &&
+        __any_sync(0xFFFFFFFFu, static_cast<uint32_t>(lane) < top_k && !isfinite(w))) { // Engine::softmax's check
+        fail_token();
+        return;
+    }
+    if (cfg.gating == FM_GATING_SOFTMAX_WEIGHT) {
+        // Engine::softmax over the k picked values (lane r holds value r)
+        float m = static_cast<uint32_t>(lane) < top_k ? w : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        const double e_r = static_cast<uint32_t>(lane) < top_k ? exp(static_cast<double>(w) - static_cast<double>(m)) : 0.0;
+        double sum = 0.0;
+        for (uint32_t r = 0; r < top_k; ++r) sum += __shfl_sync(0xFFFFFFFFu, e_r, r);
+        w = static_cast<float>(e_r / sum);
+    }
+    if (static_cast<uint32_t>(lane) < top_k) {
+        if (cfg.normalise) {
+            const double tot = static_cast<double>(total);
+            const double denom = cfg.epsilon_additive ? tot + cfg.epsilon : (tot > cfg.epsilon ? tot : cfg.epsilon);
+            w = static_cast<float>(static_cast<double>(w) / denom);
+        }
+        w = static_cast<float>(static_cast<double>(w) * cfg.scale);
+        ids[static_cast<uint64_t>(t) * top_k + lane] = my_id;
+        weights[static_cast<uint64_t>(t) * top_k + lane] = w;
+    }
+}
+
+int launch_route_ex(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                    const fmcuda_router_config &cfg, uint32_t *ids, float *weights, float *probs, cudaStream_t s) {
+    if (cfg.gating < FM_GATING_SOFTMAX || cfg.gating > FM_GATING_SOFTMAX_WEIGHT)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, "unknown gating function");
+    if (cfg.groups > 1 && (experts % cfg.groups || cfg.groups_used == 0 || cfg.groups_used > cfg.groups))
+        return set_error(FM_STATUS_SHAPE_MISMATCH, "group-limited routing needs E % groups == 0 and 1 <= used <= groups");
+    const size_t per_warp = static_cast<size_t>(experts) * 20;
+    const int warps = static_cast<int>(std::max<size_t>(1, std::min<size_t>(4, (48u * 1024u) / per_warp)));
+    route_ex_kernel<<<(tokens + warps - 1) / warps, warps * 32, per_warp * warps, s>>>(
+        logits, tokens, experts, top_k, cfg, ids, weights, probs, device_status_word());
+    return check_launch("router launch");
+}
+
+// The default configuration (softmax, no biases, no groups) goes to the
+// original kernel; any other to route_ex_kernel.
+int launch_route_cfg(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                     const fmcuda_router_config *cfg, int32_t normalise, double epsilon, double scale,
+                     uint32_t *ids, float *weights, float *probs, cudaStream_t s) {
+    if (!cfg || (cfg->gating == FM_GATING_SOFTMAX && !cfg->logit_bias && !cfg->selection_bias && cfg->groups <= 1 &&
+                 !cfg->epsilon_additive))
+        return launch_route(logits, tokens, experts, top_k, cfg ? cfg->normalise : normalise,
+                            cfg ? cfg->epsilon : epsilon, cfg ? cfg->scale : scale, ids, weights, probs, s);
+    return launch_route_ex(logits, tokens, experts, top_k, *cfg, ids, weights, probs, s);
+}
+
 int launch_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
                  int32_t normalise, double epsilon, double scale, uint32_t *ids, float *weights,
                  float *probs, cudaStream_t s) {
@@ -390,4 +609,16 @@ extern "C" int fmcuda_group_batched(const uint32_t *ids, uint32_t tokens, uint32
     if (n > 0xFFFFFFF0ull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
     return launch_group_large(ids, static_cast<uint32_t>(n), experts, counts, offsets, pairs, slot_of,
                               static_cast<uint32_t *>(scratch), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fmcuda_route_ex(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                               const fmcuda_router_config *config, uint32_t *ids, float *weights, float *probs,
+                               void *stream) {
+    if (!config) return set_error(FM_STATUS_INVALID_ARGUMENT, "null router configuration");
+    int rc = check_route_args(experts, top_k);
+    if (rc) return rc;
+    if (tokens == 0) return FM_STATUS_OK;
+    if (!logits || !ids || !weights) return set_error(FM_STATUS_INVALID_ARGUMENT, "null router pointer");
+    return launch_route_cfg(logits, tokens, experts, top_k, config, 1, 0.0, 1.0, ids, weights, probs,
+                            static_cast<cudaStream_t>(stream));
 }

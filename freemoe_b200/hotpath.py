@@ -10,7 +10,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import (GEOMETRY, ORDER_ANY, TYPE_F32, X_BF16, X_F32, DeviceInfo, FmError, MoeArgs, SharedExpert,
+from ._lib import (GEOMETRY, ORDER_ANY, TYPE_F32, X_BF16, X_F32, DeviceInfo, FmError, MoeArgs, RouterConfig, SharedExpert,
                    check, load)
 
 
@@ -89,6 +89,34 @@ def route(logits: torch.Tensor, top_k: int, normalise: bool = True, epsilon: flo
     return (ids, w, probs) if want_probs else (ids, w)
 
 
+def router_config(gating: int = 0, logit_bias: torch.Tensor | None = None,
+                  selection_bias: torch.Tensor | None = None, groups: int = 1, groups_used: int = 1,
+                  normalise: bool = True, epsilon_additive: bool = False, epsilon: float = 6.103515625e-5,
+                  scale: float = 1.0) -> RouterConfig:
+    """The C struct of a router variant (src/engine.cpp:1603-1702); the caller
+    keeps the bias tensors alive."""
+    c = RouterConfig()
+    c.gating = gating
+    c.logit_bias = logit_bias.data_ptr() if logit_bias is not None else None
+    c.selection_bias = selection_bias.data_ptr() if selection_bias is not None else None
+    c.groups, c.groups_used = groups, groups_used
+    c.normalise = 1 if normalise else 0
+    c.epsilon_additive = 1 if epsilon_additive else 0
+    c.epsilon, c.scale = epsilon, scale
+    return c
+
+
+def route_ex(logits: torch.Tensor, top_k: int, config: RouterConfig, want_probs: bool = False, stream=None):
+    """Router variants: ids [T, k] int32, weights [T, k] f32 (and probs [T, E])."""
+    T, E = logits.shape
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=logits.device)
+    probs = torch.empty(T, E, dtype=torch.float32, device=logits.device) if want_probs else None
+    check(load().fmcuda_route_ex(_ptr(logits.contiguous()), T, E, top_k, C.byref(config), _ptr(ids), _ptr(w),
+                                 _ptr(probs) if probs is not None else None, _stream(stream)))
+    return (ids, w, probs) if want_probs else (ids, w)
+
+
 def group_by_expert(ids: torch.Tensor, experts: int, stream=None):
     """Grouping of (token, rank) pairs by expert: counts, offsets, pairs, slot_of."""
     tokens, top_k = ids.shape
@@ -125,7 +153,7 @@ def moe_workspace_bytes(tokens: int, experts: int, top_k: int, d_model: int, ffn
 
 def moe_args(x, logits, slot_table, *, experts, top_k, d_model, ffn, gate_type, up_type, down_type,
              up_offset, down_offset, y, ids_out=None, weights_out=None, normalise=True,
-             epsilon=6.103515625e-5, scale=1.0, stage_events=None) -> MoeArgs:
+             epsilon=6.103515625e-5, scale=1.0, stage_events=None, router=None) -> MoeArgs:
     """Fills the C struct; ``stage_events`` is a ctypes array of 8 cudaEvent_t
     handles (or None).  The caller keeps every referenced tensor alive."""
     a = MoeArgs()
@@ -148,6 +176,8 @@ def moe_args(x, logits, slot_table, *, experts, top_k, d_model, ffn, gate_type, 
     a.ids_out = ids_out.data_ptr() if ids_out is not None else None
     a.weights_out = weights_out.data_ptr() if weights_out is not None else None
     a.stage_events = C.cast(stage_events, C.c_void_p) if stage_events is not None else None
+    a.router = C.cast(C.pointer(router), C.c_void_p) if router is not None else None
+    a._router_ref = router  # keep the struct alive with the args
     return a
 
 

@@ -156,6 +156,34 @@ int fmcuda_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_
                  int32_t normalise, double epsilon, double scale, uint32_t *ids, float *weights,
                  float *probs, void *stream);
 
+/* The router's model-family variants (src/engine.cpp:1603-1702; parsed from
+ * GGUF metadata at src/gguf.cpp:1445-1480, :1531-1535, :1946).  A NULL config,
+ * or the default below, is the native router of fmcuda_route. */
+enum {
+    FM_GATING_SOFTMAX = 0,        /* Engine::softmax over all experts */
+    FM_GATING_SIGMOID = 1,        /* float(1 / (1 + exp(-(double)s))) */
+    FM_GATING_SQRT_SOFTPLUS = 2,  /* float(sqrt(log1p(exp((double)s)))) */
+    FM_GATING_SOFTMAX_WEIGHT = 3  /* probabilities = logits; softmax over the picked k */
+};
+typedef struct fmcuda_router_config {
+    int32_t gating;               /* FM_GATING_* (expert_gating) */
+    const float *logit_bias;      /* optional device [E] (ffn_gate_inp.bias), added before gating */
+    const float *selection_bias;  /* optional device [E] (ffn_exp_probs_b.bias), picks only */
+    uint32_t groups;              /* expert_groups (<= 1: no group limit) */
+    uint32_t groups_used;         /* expert_groups_used */
+    int32_t normalise;            /* expert_weights_norm */
+    int32_t epsilon_additive;     /* expert_weights_epsilon_additive: total + eps, else max(total, eps) */
+    double epsilon;               /* expert_weights_epsilon */
+    double scale;                 /* expert_weights_scale */
+} fmcuda_router_config;
+
+/* fmcuda_route with a router configuration: logits -> ids, weights, probs (the
+ * gated probabilities, before any selection bias; optional).  NaN or +inf in the
+ * selection, or a non-finite logit under softmax gating, sets INTERNAL_ERROR. */
+int fmcuda_route_ex(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
+                    const fmcuda_router_config *config, uint32_t *ids, float *weights, float *probs,
+                    void *stream);
+
 /* Grouping of the T*k (token, rank) pairs by expert:
  *   counts [E], offsets [E+1] (exclusive scan), pairs [T*k] (for each expert,
  *   its flat pair indices t*k + r in ascending token order), slot_of [T*k]
@@ -212,6 +240,8 @@ typedef struct fmcuda_moe_args {
      * planes, gate/up, act planes, down, combine), for live per-kernel timing;
      * NULL disables.  Entries may be NULL. */
     void *const *stage_events;
+    /* optional router variant; NULL = softmax with normalise/epsilon/scale above */
+    const fmcuda_router_config *router;
 } fmcuda_moe_args;
 
 enum { FM_MOE_STAGES = 7 };

@@ -297,6 +297,115 @@ done:
     return rc;
 }
 
+/* Engine::softmax (src/engine.cpp:378-393) over n values; 0 or INTERNAL_ERROR. */
+static int softmax_ref(const float *v, uint32_t n, float *out, double *ex) {
+    float mx = v[0];
+    for (uint32_t i = 1; i < n; ++i)
+        if (v[i] > mx) mx = v[i];
+    double sum = 0.0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!isfinite(v[i])) return FMO_INTERNAL_ERROR;
+        ex[i] = exp((double)v[i] - (double)mx);
+        sum += ex[i];
+    }
+    for (uint32_t i = 0; i < n; ++i) out[i] = (float)(ex[i] / sum);
+    return FMO_OK;
+}
+
+/* The router's model-family variants, src/engine.cpp:1603-1702: optional logit
+ * bias (:1608-1613), gating (:1618-1633), selection bias (:1637-1643), group-
+ * limited routing (:1644-1675), Engine::topk on the selection (:395-411, -inf
+ * allowed), weights = probs of the picked experts with the float total taken
+ * before softmax-weight re-softmaxes them (:1677-1684), renormalisation with
+ * the clamped or additive epsilon and the scale (:1685-1702). */
+int fmo_route_ex(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k, int gating,
+                 const float *logit_bias, const float *selection_bias, uint32_t groups, uint32_t groups_used,
+                 int normalise, int epsilon_additive, double epsilon, double scale, uint32_t *ids,
+                 float *weights, float *probs_out) {
+    if (experts == 0 || top_k > experts) return FMO_INVALID_ARGUMENT;
+    if (groups > 1 && (experts % groups || groups_used == 0 || groups_used > groups)) return FMO_INVALID_ARGUMENT;
+    float *scores = (float *)malloc(sizeof(float) * experts);
+    float *probs = (float *)malloc(sizeof(float) * experts);
+    float *sel = (float *)malloc(sizeof(float) * experts);
+    double *ex = (double *)malloc(sizeof(double) * (experts > top_k ? experts : top_k));
+    unsigned char *taken = (unsigned char *)malloc(experts);
+    float *gsum = (float *)malloc(sizeof(float) * (groups > 1 ? groups : 1));
+    unsigned char *keep = (unsigned char *)malloc(groups > 1 ? groups : 1);
+    float *sw = (float *)malloc(sizeof(float) * (top_k ? top_k : 1));
+    int rc = FMO_OK;
+    if (!scores || !probs || !sel || !ex || !taken || !gsum || !keep || !sw) { rc = FMO_INTERNAL_ERROR; goto done; }
+    for (uint32_t t = 0; t < tokens; ++t) {
+        const float *v = logits + (uint64_t)t * experts;
+        for (uint32_t e = 0; e < experts; ++e) scores[e] = logit_bias ? v[e] + logit_bias[e] : v[e];
+        if (gating == 1) {
+            for (uint32_t e = 0; e < experts; ++e) probs[e] = (float)(1.0 / (1.0 + exp(-(double)scores[e])));
+        } else if (gating == 2) {
+            for (uint32_t e = 0; e < experts; ++e) probs[e] = (float)sqrt(log1p(exp((double)scores[e])));
+        } else if (gating == 3) {
+            memcpy(probs, scores, sizeof(float) * experts);
+        } else {
+            if ((rc = softmax_ref(scores, experts, probs, ex))) goto done;
+        }
+        if (probs_out) memcpy(probs_out + (uint64_t)t * experts, probs, sizeof(float) * experts);
+        for (uint32_t e = 0; e < experts; ++e) sel[e] = selection_bias ? probs[e] + selection_bias[e] : probs[e];
+        for (uint32_t e = 0; e < experts; ++e)
+            if (isnan(sel[e]) || sel[e] == INFINITY) { rc = FMO_INTERNAL_ERROR; goto done; }
+        if (groups > 1) {
+            const uint32_t per = experts / groups;
+            for (uint32_t g = 0; g < groups; ++g) {
+                float b0 = -INFINITY, b1 = -INFINITY; /* the two largest of the group */
+                for (uint32_t e = 0; e < per; ++e) {
+                    const float x = sel[g * per + e];
+                    if (x > b0) { b1 = b0; b0 = x; }
+                    else if (x > b1) b1 = x;
+                }
+                float sum = 0.0f;
+                sum += b0;
+                if (per >= 2) sum += b1;
+                gsum[g] = sum;
+            }
+            for (uint32_t g = 0; g < groups; ++g) {
+                uint32_t rank = 0;
+                for (uint32_t h = 0; h < groups; ++h)
+                    rank += (gsum[h] > gsum[g]) || (gsum[h] == gsum[g] && h < g);
+                keep[g] = rank < groups_used;
+            }
+            for (uint32_t g = 0; g < groups; ++g)
+                if (!keep[g])
+                    for (uint32_t e = 0; e < per; ++e) sel[g * per + e] = -INFINITY;
+        }
+        memset(taken, 0, experts);
+        for (uint32_t r = 0; r < top_k; ++r) {
+            uint32_t best = UINT32_MAX;
+            for (uint32_t e = 0; e < experts; ++e) {
+                if (taken[e]) continue;
+                if (best == UINT32_MAX || sel[e] > sel[best]) best = e;
+            }
+            taken[best] = 1;
+            ids[(uint64_t)t * top_k + r] = best;
+        }
+        float *w = weights + (uint64_t)t * top_k;
+        float total = 0.0f;
+        for (uint32_t r = 0; r < top_k; ++r) {
+            w[r] = probs[ids[(uint64_t)t * top_k + r]];
+            total += w[r];
+        }
+        if (gating == 3) {
+            if ((rc = softmax_ref(w, top_k, sw, ex))) goto done;
+            memcpy(w, sw, sizeof(float) * top_k);
+        }
+        if (normalise) {
+            const double denom = epsilon_additive ? (double)total + epsilon
+                                                  : ((double)total > epsilon ? (double)total : epsilon);
+            for (uint32_t r = 0; r < top_k; ++r) w[r] = (float)((double)w[r] / denom);
+        }
+        for (uint32_t r = 0; r < top_k; ++r) w[r] = (float)((double)w[r] * scale);
+    }
+done:
+    free(scores); free(probs); free(sel); free(ex); free(taken); free(gsum); free(keep); free(sw);
+    return rc;
+}
+
 int fmo_group_by_expert(const uint32_t *ids, uint32_t tokens, uint32_t top_k, uint32_t experts,
                         uint32_t *counts, uint32_t *offsets, uint32_t *pairs,
                         uint32_t *slot_of) {

@@ -83,6 +83,14 @@ int fmo_gemv_quant_fused_scalar(uint32_t type_id, const uint8_t *w, const float 
  *   renorm   src/engine.cpp:1680-1702 (float total in top-k order, w/max(total,eps),
  *                                      then w*scale; gguf.cpp:3027-3028 sets norm=1, scale=1)
  * logits [T*E]; ids/weights [T*k]; probs [T*E] (may be NULL). */
+/* Router variants (src/engine.cpp:1603-1702): gating 0 softmax, 1 sigmoid,
+ * 2 sqrt-softplus, 3 softmax-weight; optional logit / selection biases [E];
+ * groups > 1 enables group-limited routing. */
+int fmo_route_ex(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k, int gating,
+                 const float *logit_bias, const float *selection_bias, uint32_t groups, uint32_t groups_used,
+                 int normalise, int epsilon_additive, double epsilon, double scale, uint32_t *ids,
+                 float *weights, float *probs_out);
+
 int fmo_route(const float *logits, uint32_t tokens, uint32_t experts, uint32_t top_k,
               int normalise, double epsilon, double scale, uint32_t *ids, float *weights,
               float *probs);

@@ -59,6 +59,7 @@ class Oracle:
             "fmo_gemv_quant_f64": (_i, [_u32, _P, _P, _P, _u32, _u32, _u32]),
             "fmo_gemv_quant_fused_scalar": (_i, [_u32, _P, _P, _P, _u32, _u32, _u32]),
             "fmo_route": (_i, [_P, _u32, _u32, _u32, _i, _d, _d, _P, _P, _P]),
+            "fmo_route_ex": (_i, [_P, _u32, _u32, _u32, _i, _P, _P, _u32, _u32, _i, _i, _d, _d, _P, _P, _P]),
             "fmo_group_by_expert": (_i, [_P, _u32, _u32, _u32, _P, _P, _P, _P]),
             "fmo_swiglu": (_f, [_f, _f]),
             "fmo_moe_block": (_i, [_P, _u32, _u32, _u32, _u32, _P, _P, _P, _u32, _u32, _u32, _P]),
@@ -115,6 +116,21 @@ class Oracle:
         probs = np.empty((T, E), dtype=np.float32)
         rc = self.lib.fmo_route(_ptr(lg), T, E, top_k, 1 if normalise else 0, epsilon, scale,
                                 _ptr(ids), _ptr(w), _ptr(probs))
+        return rc, ids, w, probs
+
+    def route_ex(self, logits, top_k, gating=0, logit_bias=None, selection_bias=None, groups=1, groups_used=1,
+                 normalise=True, epsilon_additive=False, epsilon=EPS, scale=1.0):
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        T, E = lg.shape
+        ids = np.empty((T, top_k), dtype=np.uint32)
+        w = np.empty((T, top_k), dtype=np.float32)
+        probs = np.empty((T, E), dtype=np.float32)
+        lb = None if logit_bias is None else np.ascontiguousarray(logit_bias, dtype=np.float32)
+        sb = None if selection_bias is None else np.ascontiguousarray(selection_bias, dtype=np.float32)
+        rc = self.lib.fmo_route_ex(_ptr(lg), T, E, top_k, gating, _ptr(lb) if lb is not None else None,
+                                   _ptr(sb) if sb is not None else None, groups, groups_used,
+                                   1 if normalise else 0, 1 if epsilon_additive else 0, epsilon, scale,
+                                   _ptr(ids), _ptr(w), _ptr(probs))
         return rc, ids, w, probs
 
     def group(self, ids: np.ndarray, experts: int):

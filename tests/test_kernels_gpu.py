@@ -196,6 +196,40 @@ def test_group_vs_oracle(cuda, oracle, E, k, T):
     assert np.array_equal(slot_of.cpu().numpy().astype(np.uint32), s_o)
 
 
+@pytest.mark.parametrize("gating,groups,used,biased,eps_add,E,k",
+                         [(1, 8, 4, True, False, 256, 8), (1, 1, 1, True, False, 64, 6), (2, 1, 1, False, True, 128, 8),
+                          (3, 1, 1, True, False, 32, 4), (0, 4, 2, True, False, 64, 6), (0, 1, 1, True, True, 1024, 8),
+                          (1, 32, 3, False, False, 1024, 32)])
+def test_route_ex_vs_oracle(cuda, oracle, gating, groups, used, biased, eps_add, E, k):
+    # router variants of src/engine.cpp:1603-1702: ids, weights and probabilities bit-exact
+    rng = np.random.default_rng(E + 7 * gating + groups)
+    T = 2000
+    lg = rng.normal(0, 1.5, size=(T, E)).astype(np.float32)
+    lb = rng.normal(0, 0.3, size=E).astype(np.float32) if biased else None
+    sb = rng.normal(0, 0.1, size=E).astype(np.float32) if biased else None
+    rc, ids_o, w_o, p_o = oracle.route_ex(lg, k, gating=gating, logit_bias=lb, selection_bias=sb, groups=groups,
+                                          groups_used=used, epsilon_additive=eps_add)
+    assert rc == 0
+    lbd = dev(lb) if biased else None
+    sbd = dev(sb) if biased else None
+    cfg = cuda.router_config(gating=gating, logit_bias=lbd, selection_bias=sbd, groups=groups, groups_used=used,
+                             epsilon_additive=eps_add)
+    ids, w, p = cuda.route_ex(dev(lg), k, cfg, want_probs=True)
+    assert cuda.device_status() == 0
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
+    assert np.array_equal(bits(w.cpu().numpy()), bits(w_o))
+    assert np.array_equal(bits(p.cpu().numpy()), bits(p_o))
+
+
+def test_route_ex_nan_selection_flags(cuda):
+    lg = torch.randn(4, 16, device="cuda")
+    sb = torch.zeros(16, device="cuda")
+    sb[3] = float("nan")
+    cfg = cuda.router_config(gating=1, selection_bias=sb)
+    cuda.route_ex(lg, 2, cfg)
+    assert cuda.device_status(clear=True) == 28  # INTERNAL_ERROR (Engine::topk's check)
+
+
 @pytest.mark.parametrize("E,k,T", [(8, 2, 1), (64, 6, 4096), (128, 8, 8192), (1024, 8, 3000), (7, 3, 1000)])
 def test_group_batched_vs_oracle(cuda, oracle, E, k, T):
     # the many-warp grouping used by prefill: bit-identical to the oracle

@@ -136,3 +136,72 @@ def test_oracle_matches_live_reference(oracle):
     lg = rng.normal(size=(256, 64)).astype(np.float32)
     a, b = oracle.route(lg, 6), ref.route(lg, 6)
     assert a[0] == b[0] == 0 and np.array_equal(a[1], b[1]) and np.array_equal(bits(a[2]), bits(b[2]))
+
+
+def test_route_ex_default_is_the_native_router(oracle):
+    # the variant router with its defaults reduces to the pinned native router
+    rng = np.random.default_rng(41)
+    lg = rng.normal(0, 2, size=(300, 64)).astype(np.float32)
+    rc0, ids0, w0, p0 = oracle.route(lg, 6)
+    rc1, ids1, w1, p1 = oracle.route_ex(lg, 6)
+    assert rc0 == rc1 == 0
+    assert np.array_equal(ids0, ids1)
+    assert np.array_equal(w0.view(np.uint32), w1.view(np.uint32))
+    assert np.array_equal(p0.view(np.uint32), p1.view(np.uint32))
+
+
+def _route_ex_numpy(lg, k, gating, lbias, sbias, groups, used, eps_add, eps=6.103515625e-5, scale=1.0):
+    """An independent restatement of src/engine.cpp:1603-1702 in numpy."""
+    T, E = lg.shape
+    ids = np.zeros((T, k), np.uint32)
+    ws = np.zeros((T, k), np.float32)
+    for t in range(T):
+        s = lg[t].astype(np.float32)
+        if lbias is not None:
+            s = (s + lbias).astype(np.float32)
+        if gating == 1:
+            p = (1.0 / (1.0 + np.exp(-s.astype(np.float64)))).astype(np.float32)
+        elif gating == 2:
+            p = np.sqrt(np.log1p(np.exp(s.astype(np.float64)))).astype(np.float32)
+        elif gating == 3:
+            p = s.copy()
+        else:
+            ex = np.exp(s.astype(np.float64) - np.float64(s.max()))
+            p = (ex / ex.sum()).astype(np.float32)
+        sel = p.copy() if sbias is None else (p + sbias).astype(np.float32)
+        if groups > 1:
+            per = E // groups
+            gs = [np.float32(np.float32(0) + np.sort(sel[g * per:(g + 1) * per])[::-1][0]) +
+                  np.float32(np.sort(sel[g * per:(g + 1) * per])[::-1][1]) for g in range(groups)]
+            order = sorted(range(groups), key=lambda g: (-gs[g], g))
+            for g in order[used:]:
+                sel[g * per:(g + 1) * per] = -np.inf
+        pick = sorted(range(E), key=lambda e: (-sel[e], e))[:k]
+        w = p[pick].astype(np.float32)
+        total = np.float32(0)
+        for v in w:
+            total = np.float32(total + v)
+        if gating == 3:
+            ex = np.exp(w.astype(np.float64) - np.float64(w.max()))
+            w = (ex / ex.sum()).astype(np.float32)
+        den = np.float64(total) + eps if eps_add else max(np.float64(total), eps)
+        w = (w.astype(np.float64) / den).astype(np.float32)
+        w = (w.astype(np.float64) * scale).astype(np.float32)
+        ids[t], ws[t] = pick, w
+    return ids, ws
+
+
+@pytest.mark.parametrize("gating,groups,used,biased,eps_add", [(1, 8, 4, True, False), (2, 1, 1, False, True),
+                                                              (3, 1, 1, True, False), (0, 4, 2, True, False)])
+def test_route_ex_matches_numpy_restatement(oracle, gating, groups, used, biased, eps_add):
+    rng = np.random.default_rng(gating * 10 + groups)
+    T, E, k = 64, 64, 6
+    lg = rng.normal(0, 1.5, size=(T, E)).astype(np.float32)
+    lb = rng.normal(0, 0.3, size=E).astype(np.float32) if biased else None
+    sb = rng.normal(0, 0.1, size=E).astype(np.float32) if biased else None
+    rc, ids, w, _ = oracle.route_ex(lg, k, gating=gating, logit_bias=lb, selection_bias=sb, groups=groups,
+                                    groups_used=used, epsilon_additive=eps_add)
+    assert rc == 0
+    ids_n, w_n = _route_ex_numpy(lg, k, gating, lb, sb, groups, used, eps_add)
+    assert np.array_equal(ids, ids_n)
+    assert np.allclose(w, w_n, rtol=2e-7, atol=0)

@@ -224,3 +224,34 @@ def test_prefill_qwen3_shape(cuda, oracle):
     logits = rng.uniform(-1, 1, size=(T, E)).astype(np.float32)
     sample = np.sort(rng.choice(T, size=6, replace=False))
     run_and_check(cuda, oracle, x, logits, slots_host, slots_dev, k, d, ffn, t, sample=sample)
+
+
+def test_prefill_router_variant(cuda, oracle):
+    # DeepSeek-V3-style routing through the prefill block: sigmoid gating, a
+    # selection bias and group-limited routing (8 groups, 4 kept)
+    rng = np.random.default_rng(77)
+    E, k, d, ffn, T, t = 64, 6, 256, 256, 300, TYPE_Q8_0
+    slots = host_experts(oracle, rng, E, d, ffn, t)
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    sb = rng.normal(0, 0.2, size=E).astype(np.float32)
+    sbd = dev(sb)
+    cfg = cuda.router_config(gating=1, selection_bias=sbd, groups=8, groups_used=4, scale=2.5)
+    table = cuda.slot_table([dev(s) for s in slots], "cuda")
+    xt, lt = dev(x, torch.bfloat16), dev(logits)
+    gb = cuda.row_bytes(t, d) * ffn
+    y = torch.empty(T, d, dtype=torch.float32, device="cuda")
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    a = cuda.moe_args(xt, lt, table, experts=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
+                      up_offset=gb, down_offset=2 * gb, y=y, ids_out=ids, router=cfg)
+    need = cuda.moe_prefill_workspace_bytes(T, E, k, d, ffn)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    import ctypes as C
+    from freemoe_b200._lib import check, load
+    check(load().fmcuda_moe_prefill(C.byref(a), None, C.c_void_p(ws.data_ptr()), need, None))
+    torch.cuda.synchronize()
+    assert cuda.device_status() == 0
+    rc, ids_o, w_o, _ = oracle.route_ex(logits, k, gating=1, selection_bias=sb, groups=8, groups_used=4, scale=2.5)
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, t)
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
