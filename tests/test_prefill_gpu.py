@@ -237,7 +237,8 @@ def test_prefill_router_variant(cuda, oracle):
     sb = rng.normal(0, 0.2, size=E).astype(np.float32)
     sbd = dev(sb)
     cfg = cuda.router_config(gating=1, selection_bias=sbd, groups=8, groups_used=4, scale=2.5)
-    table = cuda.slot_table([dev(s) for s in slots], "cuda")
+    dslots = [dev(s) for s in slots]  # the slot table holds raw pointers: keep the tensors alive
+    table = cuda.slot_table(dslots, "cuda")
     xt, lt = dev(x, torch.bfloat16), dev(logits)
     gb = cuda.row_bytes(t, d) * ffn
     y = torch.empty(T, d, dtype=torch.float32, device="cuda")
