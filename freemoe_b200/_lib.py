@@ -26,13 +26,13 @@ ERROR_NAMES = {
     27: "NOT_IMPLEMENTED", 28: "INTERNAL_ERROR",
 }
 
-TYPE_F32, TYPE_Q8_0, TYPE_Q4_K = 0, 8, 12
+TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 8, 12, 14
 MOE_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024  # FM_MOE_NOALLOC_SCRATCH_BYTES
 X_F32, X_BF16 = 0, 1
 ORDER_ANY, ORDER_SCALAR, ORDER_AVX2 = 0, 1, 2
 
 # {block_size, block_bytes} (src/gguf.cpp:58-106 of the reference)
-GEOMETRY = {TYPE_F32: (1, 4), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144)}
+GEOMETRY = {TYPE_F32: (1, 4), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}
 
 
 class FmError(RuntimeError):

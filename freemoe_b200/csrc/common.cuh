@@ -38,6 +38,7 @@ inline bool block_geometry(uint32_t type_id, uint32_t *bs, uint32_t *bb) {
     case FM_TYPE_F32: *bs = 1; *bb = 4; return true;
     case FM_TYPE_Q8_0: *bs = 32; *bb = 34; return true;
     case FM_TYPE_Q4_K: *bs = 256; *bb = 144; return true;
+    case FM_TYPE_Q6_K: *bs = 256; *bb = 210; return true;
     default: return false;
     }
 }

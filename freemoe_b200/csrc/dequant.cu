@@ -114,6 +114,47 @@ __global__ void synth_q8_0_kernel(uint8_t *dst, uint64_t n_blocks, uint64_t seed
     }
 }
 
+// One thread per Q6_K block: a scale per 16 values (int8, relative to the fp16
+// block scale d), codes q + 32 in six bits packed as src/quant.cpp:347-372 reads them.
+__global__ void synth_q6_k_kernel(uint8_t *dst, uint64_t n_blocks, uint64_t seed, float std) {
+    for (uint64_t blk = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+         blk < n_blocks; blk += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        float gs[16];
+        float smax = 0.0f;
+        for (int g = 0; g < 16; ++g) {
+            float amax = 0.0f;
+            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(std * gauss(seed, blk * 256 + 16 * g + j)));
+            gs[g] = amax / 31.0f;
+            smax = fmaxf(smax, gs[g]);
+        }
+        const uint16_t dh = f32_to_fp16_bits(smax / 127.0f);
+        const float d = fp16_bits_to_f32(dh);
+        uint8_t *b = dst + blk * 210;
+        int8_t sc[16];
+        for (int g = 0; g < 16; ++g) {
+            const float r = d != 0.0f ? rintf(gs[g] / d) : 0.0f;
+            sc[g] = static_cast<int8_t>(fminf(127.0f, fmaxf(1.0f, r)));
+            b[192 + g] = static_cast<uint8_t>(sc[g]);
+        }
+        b[208] = static_cast<uint8_t>(dh & 0xFF);
+        b[209] = static_cast<uint8_t>(dh >> 8);
+        for (int h = 0; h < 2; ++h)
+            for (int l = 0; l < 32; ++l) {
+                int q[4];
+                for (int i = 0; i < 4; ++i) {
+                    const int v = 128 * h + l + 32 * i;
+                    const float step = d * static_cast<float>(sc[v / 16]);
+                    const float x = std * gauss(seed, blk * 256 + v);
+                    q[i] = static_cast<int>(fminf(31.0f, fmaxf(-32.0f, step != 0.0f ? rintf(x / step) : 0.0f))) + 32;
+                }
+                b[64 * h + l] = static_cast<uint8_t>((q[0] & 0x0F) | ((q[2] & 0x0F) << 4));
+                b[64 * h + l + 32] = static_cast<uint8_t>((q[1] & 0x0F) | ((q[3] & 0x0F) << 4));
+                b[128 + 32 * h + l] =
+                    static_cast<uint8_t>((q[0] >> 4) | ((q[1] >> 4) << 2) | ((q[2] >> 4) << 4) | ((q[3] >> 4) << 6));
+            }
+    }
+}
+
 // One thread per Q4_K block: per-sub-block affine fit, 6-bit scales and mins
 // relative to the fp16 super-block scale and min.
 __global__ void synth_q4_k_kernel(uint8_t *dst, uint64_t n_blocks, uint64_t seed, float std) {
@@ -176,6 +217,34 @@ __global__ void synth_q4_k_kernel(uint8_t *dst, uint64_t n_blocks, uint64_t seed
 
 using namespace fmb;
 
+// 32 threads per Q6_K block (src/quant.cpp:347-372): thread l of the block
+// writes y[l], y[l+32], y[l+64], y[l+96] of both 128-value halves,
+// y = (d * scale) * q with q = 6-bit code - 32, two float roundings as there.
+__global__ void dequant_q6_k_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst,
+                                    uint64_t n_blocks) {
+    const uint64_t tid = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    const uint64_t blk = tid >> 5;
+    if (blk >= n_blocks) return;
+    const int l = tid & 31;
+    const uint8_t *b = src + blk * 210;
+    const float d = fp16_bits_to_f32(static_cast<uint16_t>(b[208] | (b[209] << 8)));
+    const int is = l / 16;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t *ql = b + 64 * h, *qh = b + 128 + 32 * h;
+        const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192 + 8 * h);
+        const int q1 = static_cast<int>((ql[l] & 0x0F) | (((qh[l] >> 0) & 3) << 4)) - 32;
+        const int q2 = static_cast<int>((ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4)) - 32;
+        const int q3 = static_cast<int>((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+        const int q4 = static_cast<int>((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+        float *y = dst + blk * 256 + 128 * h;
+        y[l] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc[is])), static_cast<float>(q1));
+        y[l + 32] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc[is + 2])), static_cast<float>(q2));
+        y[l + 64] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc[is + 4])), static_cast<float>(q3));
+        y[l + 96] = __fmul_rn(__fmul_rn(d, static_cast<float>(sc[is + 6])), static_cast<float>(q4));
+    }
+}
+
 extern "C" int fmcuda_dequant(uint32_t type_id, const void *src, float *dst, uint64_t n_elems,
                               void *stream) {
     uint32_t bs, bb;
@@ -198,6 +267,10 @@ extern "C" int fmcuda_dequant(uint32_t type_id, const void *src, float *dst, uin
     if (type_id == FM_TYPE_Q8_0) {
         const uint64_t total = n_blocks * 8;
         dequant_q8_0_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0,
+                              s>>>(static_cast<const uint8_t *>(src), dst, n_blocks);
+    } else if (type_id == FM_TYPE_Q6_K) {
+        const uint64_t total = n_blocks * 32;
+        dequant_q6_k_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0,
                               s>>>(static_cast<const uint8_t *>(src), dst, n_blocks);
     } else {
         const uint64_t total = n_blocks * 32;
@@ -223,6 +296,8 @@ extern "C" int fmcuda_synth_weights(uint32_t type_id, void *dst, uint64_t rows, 
         synth_f32_kernel<<<grid, 256, 0, s>>>(static_cast<float *>(dst), n, seed, std);
     else if (type_id == FM_TYPE_Q8_0)
         synth_q8_0_kernel<<<grid, 128, 0, s>>>(static_cast<uint8_t *>(dst), n / 32, seed, std);
+    else if (type_id == FM_TYPE_Q6_K)
+        synth_q6_k_kernel<<<grid, 128, 0, s>>>(static_cast<uint8_t *>(dst), n / 256, seed, std);
     else
         synth_q4_k_kernel<<<grid, 128, 0, s>>>(static_cast<uint8_t *>(dst), n / 256, seed, std);
     return check_launch("synthetic weights launch");

@@ -143,6 +143,40 @@ int plane_workspace(uint64_t need, void **out) {
 inline uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
 // Launches the x-plane preparation for `rows` x `k_dim` values.
+// fp16 hi (and lo) planes of x in natural element order, for the Q6_K kernel.
+template <typename XT>
+__global__ void xplanes_natural_kernel(const XT *__restrict__ x, uint64_t n, __half *__restrict__ xh,
+                                       __half *__restrict__ xl) {
+    const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (i >= n) return;
+    const float v = load_x<XT>(x + i);
+    const __half h = __float2half_rn(v);
+    xh[i] = h;
+    if (xl) xl[i] = __float2half_rn(v - __half2float(h));
+}
+
+int launch_xplanes_natural(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, __half *xh, __half *xl,
+                           cudaStream_t s) {
+    const uint64_t n = static_cast<uint64_t>(rows) * k_dim;
+    if (n == 0) return FM_STATUS_OK;
+    const unsigned grid = static_cast<unsigned>((n + 255) / 256);
+    if (x_dtype == FM_X_BF16)
+        xplanes_natural_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), n, xh, xl);
+    else
+        xplanes_natural_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float *>(x), n, xh, xl);
+    return check_launch("x-plane launch");
+}
+
+int launch_xplanes(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, __half *xh,
+                   __half *xl, float *xs, cudaStream_t s);
+
+// The x planes the register-fed kernel of `type_id` reads.
+int launch_xplanes_for(uint32_t type_id, const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim,
+                       __half *xh, __half *xl, float *xs, cudaStream_t s) {
+    if (type_id == FM_TYPE_Q6_K) return launch_xplanes_natural(x, x_dtype, rows, k_dim, xh, xl, s);
+    return launch_xplanes(x, x_dtype, rows, k_dim, xh, xl, xs, s);
+}
+
 int launch_xplanes(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, __half *xh,
                    __half *xl, float *xs, cudaStream_t s) {
     const uint64_t n = static_cast<uint64_t>(rows) * (k_dim / 32);
@@ -180,6 +214,14 @@ int launch_qgemv(const QGemvParams &prm, int planes, uint32_t grid_y, uint32_t g
             if (mt2) FM_LAUNCH(FM_TYPE_Q4_K, 2, 4, 2);
             else FM_LAUNCH(FM_TYPE_Q4_K, 1, 8, 2);
         }
+    } else if (prm.type_id == FM_TYPE_Q6_K) {
+        if (planes == 1) {
+            if (mt2) FM_LAUNCH(FM_TYPE_Q6_K, 2, 4, 1);
+            else FM_LAUNCH(FM_TYPE_Q6_K, 1, 8, 1);
+        } else {
+            if (mt2) FM_LAUNCH(FM_TYPE_Q6_K, 2, 4, 2);
+            else FM_LAUNCH(FM_TYPE_Q6_K, 1, 8, 2);
+        }
     } else {
         if (planes == 1) {
             if (mt2) FM_LAUNCH(FM_TYPE_Q8_0, 2, 4, 1);
@@ -216,7 +258,8 @@ int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what) {
 // length keeps every row 16-byte aligned (bulk copies need 16-byte aligned
 // sources); everything on the BASELINE shapes qualifies.
 bool staged_shape(uint32_t type_id, uint32_t in_dim) {
-    return type_id != FM_TYPE_F32 && in_dim % 256 == 0 && row_bytes(type_id, in_dim) % 16 == 0;
+    return (type_id == FM_TYPE_Q8_0 || type_id == FM_TYPE_Q4_K) && in_dim % 256 == 0 &&
+           row_bytes(type_id, in_dim) % 16 == 0;
 }
 
 int xplane_layout(uint32_t type_id) { return type_id == FM_TYPE_Q4_K ? XL_Q4K : XL_Q8; }
@@ -332,7 +375,7 @@ extern "C" int fmcuda_gemv(uint32_t type_id, const void *w, const void *x, int32
                             : nullptr;
     float *xs = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + plane_bytes * planes);
     rc = staged ? launch_xplanes_staged(x, x_dtype, tokens, in_dim, xplane_layout(type_id), xh, xl, xs, s)
-                : launch_xplanes(x, x_dtype, tokens, in_dim, xh, xl, xs, s);
+                : launch_xplanes_for(type_id, x, x_dtype, tokens, in_dim, xh, xl, xs, s);
     if (rc) return rc;
     QGemvParams prm{};
     prm.w = static_cast<const uint8_t *>(w);

@@ -158,6 +158,63 @@ __global__ void __launch_bounds__(NW * 32)
                     q4k_mtile_block<PLANES>(h0, h1, q0, q1, c, xb, xm, tot[m][mt]);
                 }
         }
+    } else if (TYPE == FM_TYPE_Q6_K) {
+        // Q6_K (src/quant.cpp:347-372): one MMA per 16-value scale group j of a
+        // block; lane (g, c) takes values 16j + 4c .. 16j + 4c + 3 of rows g and
+        // g+8, so x is read in its natural order (4 consecutive fp16 per lane).
+        // The 6-bit code c6 becomes fp16 1024 + c6 (0x6400 | c6) and 1056 is
+        // subtracted exactly: A holds q = c6 - 32 exactly; the accumulator of
+        // each group is scaled by d * scale (exact product) in f32.
+        const uint32_t nblk = p.in_dim / 256;
+        for (uint32_t b = warp; b < nblk; b += NW) {
+#pragma unroll 2
+            for (uint32_t j = 0; j < 16; ++j) {
+                uint32_t xb[PLANES][2];
+#pragma unroll
+                for (int pl = 0; pl < PLANES; ++pl) {
+                    if (col_ok) {
+                        const uint2 v = *reinterpret_cast<const uint2 *>((pl == 0 ? xh_row : xl_row) + b * 256 + 16 * j +
+                                                                         4 * c);
+                        xb[pl][0] = v.x;
+                        xb[pl][1] = v.y;
+                    } else {
+                        xb[pl][0] = xb[pl][1] = 0u;
+                    }
+                }
+                const uint32_t u = 16 * (j & 7) + 4 * c;          // value index inside the 128-value half
+                const uint32_t h = j >> 3, grp = u >> 5, l = u & 31;
+                const uint32_t ql_off = 64 * h + (grp & 1) * 32 + l, qh_off = 128 + 32 * h + l;
+                const uint32_t nib = (grp >> 1) * 4, qsh = 2 * grp;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        uint32_t a[2][2];
+                        float ds[2];
+#pragma unroll
+                        for (int hr = 0; hr < 2; ++hr) {
+                            const uint8_t *bp = rowp[m][mt][hr] + 210ull * b;
+                            const uint32_t ql = ldg_nc_u16(bp + ql_off) | (ldg_nc_u16(bp + ql_off + 2) << 16);
+                            const uint32_t qh = ldg_nc_u16(bp + qh_off) | (ldg_nc_u16(bp + qh_off + 2) << 16);
+                            const uint32_t c6 = ((ql >> nib) & 0x0F0F0F0Fu) | (((qh >> qsh) & 0x03030303u) << 4);
+                            a[hr][0] = hsub2_u32(prmt(c6, 0x64646464u, 0x5140u), 0x64206420u);
+                            a[hr][1] = hsub2_u32(prmt(c6, 0x64646464u, 0x7362u), 0x64206420u);
+                            const float d = fp16_bits_to_f32(static_cast<uint16_t>(ldg_nc_u16(bp + 208)));
+                            const int8_t sc = static_cast<int8_t>(ldg_nc_u16(bp + 192 + (j & ~1u)) >> (8 * (j & 1)));
+                            ds[hr] = __fmul_rn(d, static_cast<float>(sc));
+                        }
+                        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int pl = 0; pl < PLANES; ++pl)
+                            mma_f16(acc, a[0][0], a[1][0], a[0][1], a[1][1], xb[pl][0], xb[pl][1]);
+                        float *t = tot[m][mt];
+                        t[0] = fmaf(ds[0], acc[0], t[0]);
+                        t[1] = fmaf(ds[0], acc[1], t[1]);
+                        t[2] = fmaf(ds[1], acc[2], t[2]);
+                        t[3] = fmaf(ds[1], acc[3], t[3]);
+                    }
+            }
+        }
     } else { // Q8_0
         const uint32_t nblk = p.in_dim / 32;
         const uint32_t xr_a = s_xrow[2 * c], xr_b = s_xrow[2 * c + 1];

@@ -22,8 +22,8 @@ int launch_route_cfg(const float *logits, uint32_t tokens, uint32_t experts, uin
 int launch_group(const uint32_t *ids, uint32_t n_pairs, uint32_t experts, uint32_t *counts,
                  uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, cudaStream_t s);
 int check_route_args(uint32_t experts, uint32_t top_k);
-int launch_xplanes(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, __half *xh,
-                   __half *xl, float *xs, cudaStream_t s);
+int launch_xplanes_for(uint32_t type_id, const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim,
+                       __half *xh, __half *xl, float *xs, cudaStream_t s);
 template <int MODE>
 int launch_qgemv(const QGemvParams &prm, int planes, uint32_t grid_y, uint32_t grid_z,
                  cudaStream_t s);
@@ -193,8 +193,8 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     const bool dn_staged = staged_shape(a->down_type, a->ffn);
     rc = gu_staged ? launch_xplanes_staged(a->x, a->x_dtype, a->tokens, a->d_model,
                                            xplane_layout(a->gate_type), xh, xplanes > 1 ? xl : nullptr, xs, s)
-                   : launch_xplanes(a->x, a->x_dtype, a->tokens, a->d_model, xh, xplanes > 1 ? xl : nullptr,
-                                    xs, s);
+                   : launch_xplanes_for(a->gate_type, a->x, a->x_dtype, a->tokens, a->d_model, xh,
+                                        xplanes > 1 ? xl : nullptr, xs, s);
     if (rc) return rc;
     mark(3);
 
@@ -221,7 +221,7 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     mark(4);
 
     rc = dn_staged ? launch_xplanes_staged(act, FM_X_F32, P, a->ffn, xplane_layout(a->down_type), ah, al, as, s)
-                   : launch_xplanes(act, FM_X_F32, P, a->ffn, ah, al, as, s);
+                   : launch_xplanes_for(a->down_type, act, FM_X_F32, P, a->ffn, ah, al, as, s);
     if (rc) return rc;
     mark(5);
 

@@ -38,7 +38,10 @@ enum {
 };
 
 /* ---- GGUF tensor types on the path (src/gguf.cpp:58-106) ---- */
-enum { FM_TYPE_F32 = 0, FM_TYPE_Q8_0 = 8, FM_TYPE_Q4_K = 12 };
+enum { FM_TYPE_F32 = 0, FM_TYPE_Q8_0 = 8, FM_TYPE_Q4_K = 12, FM_TYPE_Q6_K = 14 };
+/* Q6_K (src/quant.cpp:347-372) is decoded and multiplied on the device too: it is
+ * the down projection of mixed-type expert records (Q4_K gate/up + Q6_K down);
+ * its GEMV is the register-fed kernel, not the streamed one. */
 
 /* ---- activation dtypes ---- */
 enum { FM_X_F32 = 0, FM_X_BF16 = 1 };

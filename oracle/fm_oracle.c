@@ -18,6 +18,7 @@ int fmo_block_geometry(uint32_t type_id, uint32_t *block_size, uint32_t *block_b
     case FMO_TYPE_F32: bs = 1; bb = 4; break;
     case FMO_TYPE_Q8_0: bs = 32; bb = 34; break;
     case FMO_TYPE_Q4_K: bs = 256; bb = 144; break;
+    case FMO_TYPE_Q6_K: bs = 256; bb = 210; break;
     default: return FMO_UNSUPPORTED_QUANTISATION;
     }
     if (block_size) *block_size = bs;
@@ -126,6 +127,31 @@ int fmo_dequant_block(uint32_t type_id, const uint8_t *src, float *dst) {
             for (int l = 0; l < 32; ++l) y[l] = d1 * (float)(qs[l] & 0x0F) - m1;
             for (int l = 0; l < 32; ++l) y[32 + l] = d2 * (float)(qs[l] >> 4) - m2;
             qs += 32;
+        }
+        return FMO_OK;
+    }
+    case FMO_TYPE_Q6_K: { /* src/quant.cpp:347-372: (d * scale) * q, q = 6-bit code - 32 */
+        const uint8_t *ql = src;
+        const uint8_t *qh = src + 128;
+        const int8_t *scales = (const int8_t *)(src + 192);
+        const float d = fmo_fp16_to_f32(rd16(src + 208));
+        float *y = dst;
+        for (int n = 0; n < 256; n += 128) {
+            for (int l = 0; l < 32; ++l) {
+                const int is = l / 16;
+                const int q1 = (int)((ql[l] & 0x0F) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                const int q2 = (int)((ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                const int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                const int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                y[l] = d * (float)scales[is + 0] * (float)q1;
+                y[l + 32] = d * (float)scales[is + 2] * (float)q2;
+                y[l + 64] = d * (float)scales[is + 4] * (float)q3;
+                y[l + 96] = d * (float)scales[is + 6] * (float)q4;
+            }
+            y += 128;
+            ql += 64;
+            qh += 32;
+            scales += 8;
         }
         return FMO_OK;
     }
@@ -555,4 +581,45 @@ uint64_t fmo_fnv1a64(const uint8_t *data, uint64_t size) {
         h *= 0x100000001B3ull;
     }
     return h;
+}
+
+void fmo_quantize_q6_k(const float *x, uint8_t *dst, uint64_t n_elems) {
+    for (uint64_t blk = 0; blk < n_elems / 256; ++blk) {
+        const float *v = x + blk * 256;
+        uint8_t *b = dst + blk * 210;
+        float gs[16], smax = 0.0f;
+        for (int g = 0; g < 16; ++g) {
+            float amax = 0.0f;
+            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[16 * g + j]));
+            gs[g] = amax / 31.0f;
+            if (gs[g] > smax) smax = gs[g];
+        }
+        const uint16_t dh = fmo_f32_to_fp16(smax / 127.0f);
+        const float d = fmo_fp16_to_f32(dh);
+        int8_t sc[16];
+        for (int g = 0; g < 16; ++g) {
+            float r = d != 0.0f ? rintf(gs[g] / d) : 0.0f;
+            if (r < 1.0f) r = 1.0f;
+            if (r > 127.0f) r = 127.0f;
+            sc[g] = (int8_t)r;
+            b[192 + g] = (uint8_t)sc[g];
+        }
+        b[208] = (uint8_t)(dh & 0xFF);
+        b[209] = (uint8_t)(dh >> 8);
+        for (int h = 0; h < 2; ++h)
+            for (int l = 0; l < 32; ++l) {
+                int q[4];
+                for (int i = 0; i < 4; ++i) {
+                    const int idx = 128 * h + l + 32 * i;
+                    const float step = d * (float)sc[idx / 16];
+                    float r = step != 0.0f ? rintf(v[idx] / step) : 0.0f;
+                    if (r < -32.0f) r = -32.0f;
+                    if (r > 31.0f) r = 31.0f;
+                    q[i] = (int)r + 32;
+                }
+                b[64 * h + l] = (uint8_t)((q[0] & 0x0F) | ((q[2] & 0x0F) << 4));
+                b[64 * h + l + 32] = (uint8_t)((q[1] & 0x0F) | ((q[3] & 0x0F) << 4));
+                b[128 + 32 * h + l] = (uint8_t)((q[0] >> 4) | ((q[1] >> 4) << 2) | ((q[2] >> 4) << 4) | ((q[3] >> 4) << 6));
+            }
+    }
 }

@@ -36,7 +36,7 @@ enum {
 };
 
 /* GGUF tensor type ids covered by the hot path (src/gguf.cpp:58-106). */
-enum { FMO_TYPE_F32 = 0, FMO_TYPE_Q8_0 = 8, FMO_TYPE_Q4_K = 12 };
+enum { FMO_TYPE_F32 = 0, FMO_TYPE_Q8_0 = 8, FMO_TYPE_Q4_K = 12, FMO_TYPE_Q6_K = 14 };
 
 /* {block_size, block_bytes} from the quantisation table (src/gguf.cpp:58-106). */
 int fmo_block_geometry(uint32_t type_id, uint32_t *block_size, uint32_t *block_bytes);
@@ -124,6 +124,9 @@ int fmo_moe_block(const float *x, uint32_t tokens, uint32_t d, uint32_t ffn, uin
  * that the min path is exercised. */
 void fmo_quantize_q8_0(const float *x, uint8_t *dst, uint64_t n_elems);
 void fmo_quantize_q4_k(const float *x, uint8_t *dst, uint64_t n_elems);
+/* Q6_K: one int8 scale per 16 values relative to an fp16 block scale, 6-bit
+ * codes q + 32 packed as src/quant.cpp:347-372 reads them. */
+void fmo_quantize_q6_k(const float *x, uint8_t *dst, uint64_t n_elems);
 
 /* FNV-1a 64 over a byte range (include/fm/common.hpp:73-85). */
 uint64_t fmo_fnv1a64(const uint8_t *data, uint64_t size);

@@ -21,8 +21,8 @@ ORACLE_SO = HERE / "libfm_oracle.so"
 REF_SO = HERE / "_ref" / "libfmref.so"
 REF_TREE = Path(os.environ.get("FM_REFERENCE", "/root/reference"))
 
-TYPE_F32, TYPE_Q8_0, TYPE_Q4_K = 0, 8, 12
-GEOMETRY = {TYPE_F32: (1, 4), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144)}
+TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 8, 12, 14
+GEOMETRY = {TYPE_F32: (1, 4), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}
 EPS = 6.103515625e-5
 
 _P = C.c_void_p
@@ -65,6 +65,7 @@ class Oracle:
             "fmo_moe_block": (_i, [_P, _u32, _u32, _u32, _u32, _P, _P, _P, _u32, _u32, _u32, _P]),
             "fmo_quantize_q8_0": (None, [_P, _P, _u64]),
             "fmo_quantize_q4_k": (None, [_P, _P, _u64]),
+            "fmo_quantize_q6_k": (None, [_P, _P, _u64]),
             "fmo_fnv1a64": (_u64, [_P, _u64]),
         }
         for name, (res, args) in sig.items():
@@ -173,7 +174,8 @@ class Oracle:
             return x.view(np.uint8).copy()
         bs, bb = GEOMETRY[type_id]
         out = np.empty(x.size // bs * bb, dtype=np.uint8)
-        fn = self.lib.fmo_quantize_q8_0 if type_id == TYPE_Q8_0 else self.lib.fmo_quantize_q4_k
+        fn = {TYPE_Q8_0: self.lib.fmo_quantize_q8_0, TYPE_Q4_K: self.lib.fmo_quantize_q4_k,
+              TYPE_Q6_K: self.lib.fmo_quantize_q6_k}[type_id]
         fn(_ptr(x), _ptr(out), x.size)
         return out
 

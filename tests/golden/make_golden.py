@@ -32,10 +32,10 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 
-from oracle.oracle import (REF_TREE, TYPE_F32, TYPE_Q4_K, TYPE_Q8_0, Oracle,  # noqa: E402
+from oracle.oracle import (REF_TREE, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0, Oracle,  # noqa: E402
                            Reference, bf16_round)
 
-HOT_TYPES = (TYPE_F32, TYPE_Q8_0, TYPE_Q4_K)
+HOT_TYPES = (TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K)
 
 
 def extract_quant_reference() -> tuple[bytes, str]:
@@ -55,9 +55,9 @@ def extract_quant_reference() -> tuple[bytes, str]:
 
 
 def random_blocks(rng, type_id: int, nb: int) -> np.ndarray:
-    bs, bb = {TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144)}[type_id]
+    bs, bb = {TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}[type_id]
     raw = rng.integers(0, 256, size=(nb, bb), dtype=np.uint8)
-    offs = [0] if type_id == TYPE_Q8_0 else [0, 2]
+    offs = {TYPE_Q8_0: [0], TYPE_Q4_K: [0, 2], TYPE_Q6_K: [208]}[type_id]
     for off in offs:
         h = rng.integers(0, 0x7C00, size=nb).astype(np.uint16)
         h |= (rng.integers(0, 2, size=nb).astype(np.uint16) << 15)
@@ -121,6 +121,19 @@ def main() -> None:
     g = np.concatenate([rng.normal(0, 4, size=1000), [0.0, -0.0, 80.0, -80.0, 1e-30, -1e-30]]).astype(np.float32)
     u = rng.normal(0, 1, size=g.size).astype(np.float32)
     out["swiglu_gate"], out["swiglu_up"], out["swiglu_out"] = g, u, ref.swiglu(g, u)
+
+    # Q6_K (the down projection of mixed-type records): decode and GEMV, drawn
+    # after everything above so the earlier vectors keep their values
+    raw = random_blocks(rng, TYPE_Q6_K, 64)
+    out["dequant_q6_k_src"] = raw
+    out["dequant_q6_k_out"] = ref.dequant(TYPE_Q6_K, raw, 64 * 256)
+    w = orc.quantize(TYPE_Q6_K, rng.normal(0, 0.02, size=out_dim * in_dim).astype(np.float32))
+    x = bf16_round(rng.normal(0, 1, size=(tokens, in_dim)).astype(np.float32))
+    out["gemv_q6_k_w"] = w
+    out["gemv_q6_k_x"] = x
+    out["gemv_q6_k_y_auto"] = np.stack([ref.gemv_quant(TYPE_Q6_K, w, xt, out_dim, in_dim) for xt in x])
+    out["gemv_q6_k_y_scalar"] = np.stack(
+        [ref.gemv_quant(TYPE_Q6_K, w, xt, out_dim, in_dim, scalar=True) for xt in x])
 
     qr, qr_sha = extract_quant_reference()
     (HERE / "quant_reference_hotpath.bin").write_bytes(qr)

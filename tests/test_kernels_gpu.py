@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle.oracle import TYPE_F32, TYPE_Q4_K, TYPE_Q8_0, bf16_round
+from oracle.oracle import TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0, bf16_round
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
@@ -37,14 +37,14 @@ def rel_err(got, ref):
 
 # ---------------------------------------------------------------- K1 dequant
 
-@pytest.mark.parametrize("name,t", [("q8_0", TYPE_Q8_0), ("q4_k", TYPE_Q4_K)])
+@pytest.mark.parametrize("name,t", [("q8_0", TYPE_Q8_0), ("q4_k", TYPE_Q4_K), ("q6_k", TYPE_Q6_K)])
 def test_dequant_golden_bitexact(cuda, golden, name, t):
     src, exp = golden[f"dequant_{name}_src"], golden[f"dequant_{name}_out"]
     got = cuda.dequantize_tensor_region(t, dev(src), exp.size).cpu().numpy()
     assert np.array_equal(bits(got), bits(exp))
 
 
-@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
+@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K])
 def test_dequant_full_matrix_bitexact(cuda, oracle, t):
     # a Mixtral-shaped gate matrix [14336 x 4096], synthesised on the device
     rows, cols = 14336, 4096
@@ -64,7 +64,7 @@ def test_dequant_f32_and_errors(cuda):
 
 # ---------------------------------------------------------------- K2 GEMV
 
-@pytest.mark.parametrize("name,t", [("q8_0", TYPE_Q8_0), ("q4_k", TYPE_Q4_K)])
+@pytest.mark.parametrize("name,t", [("q8_0", TYPE_Q8_0), ("q4_k", TYPE_Q4_K), ("q6_k", TYPE_Q6_K)])
 def test_gemv_golden(cuda, golden, name, t):
     o, i, T = (int(v) for v in golden["gemv_shape"])
     x = golden[f"gemv_{name}_x"]
@@ -72,7 +72,7 @@ def test_gemv_golden(cuda, golden, name, t):
     assert rel_err(y, golden[f"gemv_{name}_y_auto"]) < TOL
 
 
-@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
+@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K])
 @pytest.mark.parametrize("tokens", [1, 2, 3, 8, 9, 17])
 @pytest.mark.parametrize("xdt", ["bf16", "f32"])
 def test_gemv_vs_oracle(cuda, oracle, t, tokens, xdt):
@@ -92,7 +92,7 @@ def test_gemv_vs_oracle(cuda, oracle, t, tokens, xdt):
     assert err < 1e-4  # what the design delivers; the stated bar is TOL
 
 
-@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
+@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K])
 def test_gemv_mixtral_shapes(cuda, oracle, t):
     # gate [14336 x 4096] and down [4096 x 14336] at T = 1 and T = 8 (bf16 x)
     for out_dim, in_dim in ((14336, 4096), (4096, 14336)):
@@ -288,6 +288,28 @@ def test_moe_block_vs_oracle(cuda, oracle, t, T, xdt):
     assert cuda.device_status() == 0
     assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
     assert np.array_equal(bits(w.cpu().numpy()), bits(w_o))
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_moe_block_mixed_record(cuda, oracle, T):
+    # mixed-type expert records: Q4_K gate/up with a Q6_K down projection
+    rng = np.random.default_rng(900 + T)
+    E, k, d, ffn = 8, 2, 512, 768
+    slots = []
+    for _ in range(E):
+        parts = [oracle.quantize(TYPE_Q4_K, rng.normal(0, 0.02, size=ffn * d).astype(np.float32)),
+                 oracle.quantize(TYPE_Q4_K, rng.normal(0, 0.02, size=ffn * d).astype(np.float32)),
+                 oracle.quantize(TYPE_Q6_K, rng.normal(0, 0.02, size=d * ffn).astype(np.float32))]
+        slots.append(np.concatenate(parts))
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, TYPE_Q4_K, TYPE_Q4_K, TYPE_Q6_K)
+    dslots = [dev(s) for s in slots]
+    y = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), dslots, top_k=k, ffn=ffn, gate_type=TYPE_Q4_K,
+                       down_type=TYPE_Q6_K)
+    assert cuda.device_status() == 0
     assert rel_err(y.cpu().numpy(), y_o) < TOL
 
 

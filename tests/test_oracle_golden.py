@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 from conftest import GOLDEN
-from oracle.oracle import TYPE_F32, TYPE_Q4_K, TYPE_Q8_0, Reference, reference_available
+from oracle.oracle import TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0, Reference, reference_available
 
 
 def bits(a):
@@ -39,18 +39,18 @@ def read_fmqr(path):
 
 def test_quant_reference_records(oracle):
     recs = read_fmqr(GOLDEN / "quant_reference_hotpath.bin")
-    assert sorted(r[0] for r in recs) == [TYPE_F32, TYPE_Q8_0, TYPE_Q4_K]
-    geo = {TYPE_F32: (1, 4), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144)}
+    assert sorted(r[0] for r in recs) == [TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K]
+    geo = {TYPE_F32: (1, 4), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}
     for t, bb, nf, raw, exp in recs:
         assert geo[t] == (nf, bb)
         got = oracle.dequant(t, raw, nf)
         # the reference's own acceptance bound for this fixture
         np.testing.assert_allclose(got, exp, rtol=1e-6, atol=0)
-        # and in fact bit-exact for these three decoders
+        # and in fact bit-exact for these four decoders
         assert np.array_equal(bits(got), bits(exp)), f"type {t}"
 
 
-@pytest.mark.parametrize("name,t,bs", [("q8_0", TYPE_Q8_0, 32), ("q4_k", TYPE_Q4_K, 256)])
+@pytest.mark.parametrize("name,t,bs", [("q8_0", TYPE_Q8_0, 32), ("q4_k", TYPE_Q4_K, 256), ("q6_k", TYPE_Q6_K, 256)])
 def test_dequant_golden(oracle, golden, name, t, bs):
     src = golden[f"dequant_{name}_src"]
     exp = golden[f"dequant_{name}_out"]
@@ -58,7 +58,7 @@ def test_dequant_golden(oracle, golden, name, t, bs):
     assert np.array_equal(bits(got), bits(exp))
 
 
-@pytest.mark.parametrize("name,t", [("q8_0", TYPE_Q8_0), ("q4_k", TYPE_Q4_K)])
+@pytest.mark.parametrize("name,t", [("q8_0", TYPE_Q8_0), ("q4_k", TYPE_Q4_K), ("q6_k", TYPE_Q6_K)])
 def test_gemv_fused_scalar_golden(oracle, golden, name, t):
     o, i, T = golden["gemv_shape"]
     y = oracle.gemv_fused_scalar(t, golden[f"gemv_{name}_w"], golden[f"gemv_{name}_x"], o, i)
