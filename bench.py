@@ -729,6 +729,71 @@ def run_gemv_shapes(args):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_layer(args):
+    """--impl reference --config deepseek|qwen3|mixtral: the reference's own
+    per-token expert loop (gemv_quant + silu, compiled from source into
+    oracle/_ref) on the host cores, over a bounded sample of the config's tokens."""
+    world, rank, local = dist_setup(args)
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle.oracle import Oracle, Reference, reference_available
+
+    cfg = dict(LAYERS[args.config])
+    E, k, d, ffn, t = cfg["E"], cfg["k"], cfg["d"], cfg["ffn"], cfg["t"]
+    T = args.tokens if args.tokens_set else cfg["T"]
+    gb = ffn * row_bytes(t, d)
+    slots = None
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            from freemoe_b200 import hotpath
+
+            hotpath.init(0)
+            slots = [torch.cat([hotpath.synth_weights(t, rows, cols, 1000 + 3 * e + j)
+                                for j, (rows, cols) in enumerate(((ffn, d), (ffn, d), (d, ffn)))]).cpu().numpy()
+                     for e in range(E)]
+    except Exception:  # noqa: BLE001 - no usable GPU: encode on the host
+        slots = None
+    if slots is None:
+        orc = Oracle()
+        rng = np.random.default_rng(1)
+        slots = [np.concatenate([orc.quantize(t, rng.normal(0, 0.02, n).astype(np.float32))
+                                 for n in (ffn * d, ffn * d, d * ffn)]) for _ in range(E)]
+    x, lg = layer_inputs(cfg, T, seed=1)
+    threads = os.cpu_count() or 1
+    kind = "reference" if reference_available() else "port"
+    ref = Reference() if kind == "reference" else None
+    orc = Oracle()
+    n_s = min(T, max(1, int(args.sample)))
+
+    def step():
+        if ref is not None:
+            rc, ids, w, _ = ref.route(lg[:n_s], k)
+            return ref.moe_block(t, slots, gb, 2 * gb, x[:n_s], ids, w, d, ffn, threads=threads)
+        rc, ids, w, _ = orc.route(lg[:n_s], k)
+        return orc.moe_block(x[:n_s], ids, w, slots, d, ffn, t)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = n_s / dt
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": {8: "q8_0", 12: "q4_k"}[t], "data": "synthetic",
+            "config": {"workload": f"{args.config}: {E} experts d {d} ffn {ffn} top-{k} (routed experts), "
+                                   f"{n_s} of T={T} tokens per step", "tokens": n_s},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                             "sample": f"{n_s} tokens of the {T}-token batch per step"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_layer_ep(args):
     """The Qwen3-shaped layer expert-parallel over the torchrun ranks (NCCL):
     experts 128/G per rank, tokens 8192/G per rank (strong scaling), token rows
@@ -840,11 +905,16 @@ def main():
     ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sample", type=int, default=32,
+                    help="tokens per step of the reference arm on a layer configuration")
     ap.add_argument("--config", default="stack", choices=["stack", *LAYERS, "gemv"],
                     help="stack (default, the headline) or a layer configuration")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     args.tokens_set = any(a.startswith("--tokens") for a in sys.argv[1:])
+    if args.config in LAYERS and args.impl == "reference":
+        run_reference_layer(args)
+        return
     if args.config == "gemv" and args.impl == "ours":
         run_gemv_shapes(args)
         return
