@@ -254,6 +254,18 @@ int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what) {
     return FM_STATUS_OK;
 }
 
+// Quantised rows are read with loads as wide as the type allows: Q4_K with
+// 16-byte loads (144-byte blocks keep every row 16-byte aligned), Q8_0 and
+// Q6_K with 2- and 4-byte loads (34- and 210-byte blocks).  A matrix whose first
+// byte breaks that alignment is refused instead of read misaligned.
+int check_quant_alignment(uint32_t type_id, uint64_t byte_offset, const char *what) {
+    const uint64_t need = type_id == FM_TYPE_Q4_K ? 16 : (type_id == FM_TYPE_F32 ? 4 : 2);
+    if (byte_offset % need)
+        return set_error(FM_STATUS_INVALID_ARGUMENT, std::string(what) + ": quantised matrix must start on a " +
+                                                          std::to_string(need) + "-byte boundary");
+    return FM_STATUS_OK;
+}
+
 // The TMA-staged kernel takes rows of whole 256-value K steps whose byte
 // length keeps every row 16-byte aligned (bulk copies need 16-byte aligned
 // sources); everything on the BASELINE shapes qualifies.
@@ -350,6 +362,7 @@ extern "C" int fmcuda_gemv(uint32_t type_id, const void *w, const void *x, int32
         return set_error(FM_STATUS_INVALID_ARGUMENT, "unknown activation dtype");
     int rc = check_quant_shape(type_id, in_dim, "gemv");
     if (rc) return rc;
+    if ((rc = check_quant_alignment(type_id, reinterpret_cast<uintptr_t>(w), "gemv"))) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (type_id == FM_TYPE_F32) {
         const unsigned grid = min(65535u, (out_dim + 7) / 8);

@@ -89,6 +89,120 @@ struct StageGeom {
 
 constexpr int kMaxGroupExperts = 1024;
 
+// x operands of one 256-value K step b for one warp: the B fragments of the
+// token planes (lane (g, c) holds column g) and the sub-block sums (Q4_K: the
+// pair of sub-blocks 2c, 2c+1 of column g; Q8_0: the 8 sums of columns 2c and
+// 2c + 1).  Lanes of columns past the tile's tokens load a valid row (the
+// caller points them at x row 0): their MMA columns are never written out.
+template <int TYPE, int PLANES>
+struct ItemX {
+    uint32_t xb[PLANES][32];
+    float2 X;
+    float Xa[8], Xb[8];
+};
+
+template <int TYPE, int PLANES>
+__device__ __forceinline__ void load_item_x(ItemX<TYPE, PLANES> &ix, const uint8_t *xh_row, const uint8_t *xl_row,
+                                            const float *xs_row, const float *xs_a, const float *xs_b,
+                                            bool ok_a, bool ok_b, uint32_t b, int c) {
+#pragma unroll
+    for (int pl = 0; pl < PLANES; ++pl) {
+        const uint8_t *row = (pl ? xl_row : xh_row) + static_cast<uint64_t>(b) * 512;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(row + (4 * q + c) * 16));
+            ix.xb[pl][4 * q + 0] = v.x;
+            ix.xb[pl][4 * q + 1] = v.y;
+            ix.xb[pl][4 * q + 2] = v.z;
+            ix.xb[pl][4 * q + 3] = v.w;
+        }
+    }
+    ix.X = make_float2(0.f, 0.f);
+    if (TYPE == FM_TYPE_Q4_K) {
+        ix.X = __ldg(reinterpret_cast<const float2 *>(xs_row + b * 8 + 2 * c));
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            ix.Xa[q] = ok_a ? __ldg(xs_a + b * 8 + q) : 0.0f;
+            ix.Xb[q] = ok_b ? __ldg(xs_b + b * 8 + q) : 0.0f;
+        }
+    }
+}
+
+// One K step of one tile from its staged ring slot `st` (the tile's NMAT x
+// 16*MT rows back to back, RB bytes each): tot[m][mt] += this step's partial
+// dot products of rows (g, g + 8) of m-tile mt with columns (2c, 2c + 1).
+template <int TYPE, int MT, int NMAT, int PLANES, int RB>
+__device__ __forceinline__ void qgemv_item(const uint8_t *st, const ItemX<TYPE, PLANES> &ix, int g, int c,
+                                           float (&tot)[NMAT][MT][4]) {
+    constexpr int TILE = 16 * MT;
+    if (TYPE == FM_TYPE_Q4_K) {
+        uint32_t xm[2];
+        xm[0] = pack_half2(ix.X.x, ix.X.y);
+        xm[1] = pack_half2(ix.X.x - half_lo_f(xm[0]), ix.X.y - half_hi_f(xm[0]));
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint8_t *r0 = st + (m * TILE + 16 * mt + g) * RB;
+                const uint8_t *r1 = r0 + 8 * RB;
+                const uint4 h0 = *reinterpret_cast<const uint4 *>(r0);
+                const uint4 h1 = *reinterpret_cast<const uint4 *>(r1);
+                uint4 q0[2], q1[2];
+                q0[0] = *reinterpret_cast<const uint4 *>(r0 + 16 + 32 * c);
+                q0[1] = *reinterpret_cast<const uint4 *>(r0 + 32 + 32 * c);
+                q1[0] = *reinterpret_cast<const uint4 *>(r1 + 16 + 32 * c);
+                q1[1] = *reinterpret_cast<const uint4 *>(r1 + 32 + 32 * c);
+                q4k_mtile_block<PLANES>(h0, h1, q0, q1, c, ix.xb, xm, tot[m][mt]);
+            }
+    } else { // Q8_0: 8 blocks of 32 per K step; block sb uses registers 4sb..4sb+3
+#pragma unroll
+        for (int sb = 0; sb < 8; ++sb) {
+            const uint32_t off = 34 * sb;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    uint32_t wa[2], wb[2], dr[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint8_t *r = st + (m * TILE + 16 * mt + g + 8 * h) * RB + off;
+                        dr[h] = *reinterpret_cast<const uint16_t *>(r);
+                        if ((sb & 1) == 0) { // codes start 2 bytes into an aligned word
+                            const uint32_t *wp = reinterpret_cast<const uint32_t *>(r + 4 * c);
+                            const uint32_t *wq = reinterpret_cast<const uint32_t *>(r + 16 + 4 * c);
+                            wa[h] = __funnelshift_r(wp[0], wp[1], 16);
+                            wb[h] = __funnelshift_r(wq[0], wq[1], 16);
+                        } else {
+                            wa[h] = *reinterpret_cast<const uint32_t *>(r + 2 + 4 * c);
+                            wb[h] = *reinterpret_cast<const uint32_t *>(r + 18 + 4 * c);
+                        }
+                    }
+                    const uint32_t va0 = wa[0] ^ 0x80808080u, vb0 = wb[0] ^ 0x80808080u;
+                    const uint32_t va1 = wa[1] ^ 0x80808080u, vb1 = wb[1] ^ 0x80808080u;
+                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int pl = 0; pl < PLANES; ++pl) {
+                        mma_f16(acc, prmt(va0, 0u, 0x4240u), prmt(va1, 0u, 0x4240u),
+                                prmt(va0, 0u, 0x4341u), prmt(va1, 0u, 0x4341u),
+                                ix.xb[pl][4 * sb + 0], ix.xb[pl][4 * sb + 1]);
+                        mma_f16(acc, prmt(vb0, 0u, 0x4240u), prmt(vb1, 0u, 0x4240u),
+                                prmt(vb0, 0u, 0x4341u), prmt(vb1, 0u, 0x4341u),
+                                ix.xb[pl][4 * sb + 2], ix.xb[pl][4 * sb + 3]);
+                    }
+                    const float d0 = fp16_bits_to_f32(static_cast<uint16_t>(dr[0]));
+                    const float d1 = fp16_bits_to_f32(static_cast<uint16_t>(dr[1]));
+                    const float d0s = d0 * 16777216.0f, d1s = d1 * 16777216.0f; // codes carry 2^-24
+                    float *tt = tot[m][mt];
+                    tt[0] = fmaf(d0s, acc[0], fmaf(-128.0f * d0, ix.Xa[sb], tt[0]));
+                    tt[1] = fmaf(d0s, acc[1], fmaf(-128.0f * d0, ix.Xb[sb], tt[1]));
+                    tt[2] = fmaf(d1s, acc[2], fmaf(-128.0f * d1, ix.Xa[sb], tt[2]));
+                    tt[3] = fmaf(d1s, acc[3], fmaf(-128.0f * d1, ix.Xb[sb], tt[3]));
+                }
+        }
+    }
+}
+
 #ifndef FMB_GEMV_MINB
 #define FMB_GEMV_MINB 1
 #endif
@@ -190,6 +304,7 @@ __global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
     const uint8_t *cur_base = nullptr; // first row of the current tile (matrix 0)
     uint32_t cur_tile = 0xFFFFFFFFu, cur_jj = 0, issued = 0;
     const uint32_t my_items = my_tiles * nw;
+
     auto issue = [&]() {
         if (issued < my_items) {
             if (cur_jj == 0) {
@@ -245,99 +360,12 @@ __global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
         for (uint32_t jj = 0; jj < nw; ++jj) {
             const uint32_t j = i * nw + jj;
             const uint32_t b = warp + NW * jj;
-            // x fragments for this K step, loaded before the ring wait
-            uint32_t xb[PLANES][32];
-#pragma unroll
-            for (int pl = 0; pl < PLANES; ++pl) {
-                const uint8_t *row = (pl ? xl_row : xh_row) + static_cast<uint64_t>(b) * 512;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    if (col_ok) v = __ldg(reinterpret_cast<const uint4 *>(row + (4 * q + c) * 16));
-                    xb[pl][4 * q + 0] = v.x;
-                    xb[pl][4 * q + 1] = v.y;
-                    xb[pl][4 * q + 2] = v.z;
-                    xb[pl][4 * q + 3] = v.w;
-                }
-            }
-            float2 X = make_float2(0.f, 0.f);
-            float Xa[8], Xb[8];
-            if (TYPE == FM_TYPE_Q4_K) {
-                if (col_ok) X = __ldg(reinterpret_cast<const float2 *>(xs_row + b * 8 + 2 * c));
-            } else {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    Xa[q] = ok_a ? __ldg(xs_a + b * 8 + q) : 0.0f;
-                    Xb[q] = ok_b ? __ldg(xs_b + b * 8 + q) : 0.0f;
-                }
-            }
+            // x operands for this K step, loaded before the ring wait
+            ItemX<TYPE, PLANES> ix;
+            load_item_x<TYPE, PLANES>(ix, xh_row, xl_row, xs_row, xs_a, xs_b, ok_a, ok_b, b, c);
             cp_async_wait<P - 1>(); // item j landed (this lane's copies)
             __syncwarp();           // ... and every other lane's
-            const uint8_t *st = ring + (j % P) * G::BYTES;
-            if (tile_ok && TYPE == FM_TYPE_Q4_K) {
-                uint32_t xm[2];
-                xm[0] = pack_half2(X.x, X.y);
-                xm[1] = pack_half2(X.x - half_lo_f(xm[0]), X.y - half_hi_f(xm[0]));
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        const uint8_t *r0 = st + (m * TILE + 16 * mt + g) * G::RB;
-                        const uint8_t *r1 = r0 + 8 * G::RB;
-                        const uint4 h0 = *reinterpret_cast<const uint4 *>(r0);
-                        const uint4 h1 = *reinterpret_cast<const uint4 *>(r1);
-                        uint4 q0[2], q1[2];
-                        q0[0] = *reinterpret_cast<const uint4 *>(r0 + 16 + 32 * c);
-                        q0[1] = *reinterpret_cast<const uint4 *>(r0 + 32 + 32 * c);
-                        q1[0] = *reinterpret_cast<const uint4 *>(r1 + 16 + 32 * c);
-                        q1[1] = *reinterpret_cast<const uint4 *>(r1 + 32 + 32 * c);
-                        q4k_mtile_block<PLANES>(h0, h1, q0, q1, c, xb, xm, tot[m][mt]);
-                    }
-            } else if (tile_ok) { // Q8_0: 8 blocks of 32 per K step; block sb uses registers 4sb..4sb+3
-#pragma unroll
-                for (int sb = 0; sb < 8; ++sb) {
-                    const uint32_t off = 34 * sb;
-#pragma unroll
-                    for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt) {
-                            uint32_t wa[2], wb[2], dr[2];
-#pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                const uint8_t *r = st + (m * TILE + 16 * mt + g + 8 * h) * G::RB + off;
-                                dr[h] = *reinterpret_cast<const uint16_t *>(r);
-                                if ((sb & 1) == 0) { // codes start 2 bytes into an aligned word
-                                    const uint32_t *wp = reinterpret_cast<const uint32_t *>(r + 4 * c);
-                                    const uint32_t *wq = reinterpret_cast<const uint32_t *>(r + 16 + 4 * c);
-                                    wa[h] = __funnelshift_r(wp[0], wp[1], 16);
-                                    wb[h] = __funnelshift_r(wq[0], wq[1], 16);
-                                } else {
-                                    wa[h] = *reinterpret_cast<const uint32_t *>(r + 2 + 4 * c);
-                                    wb[h] = *reinterpret_cast<const uint32_t *>(r + 18 + 4 * c);
-                                }
-                            }
-                            const uint32_t va0 = wa[0] ^ 0x80808080u, vb0 = wb[0] ^ 0x80808080u;
-                            const uint32_t va1 = wa[1] ^ 0x80808080u, vb1 = wb[1] ^ 0x80808080u;
-                            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                            for (int pl = 0; pl < PLANES; ++pl) {
-                                mma_f16(acc, prmt(va0, 0x64646464u, 0x4240u), prmt(va1, 0x64646464u, 0x4240u),
-                                        prmt(va0, 0x64646464u, 0x4341u), prmt(va1, 0x64646464u, 0x4341u),
-                                        xb[pl][4 * sb + 0], xb[pl][4 * sb + 1]);
-                                mma_f16(acc, prmt(vb0, 0x64646464u, 0x4240u), prmt(vb1, 0x64646464u, 0x4240u),
-                                        prmt(vb0, 0x64646464u, 0x4341u), prmt(vb1, 0x64646464u, 0x4341u),
-                                        xb[pl][4 * sb + 2], xb[pl][4 * sb + 3]);
-                            }
-                            const float d0 = fp16_bits_to_f32(static_cast<uint16_t>(dr[0]));
-                            const float d1 = fp16_bits_to_f32(static_cast<uint16_t>(dr[1]));
-                            float *tt = tot[m][mt];
-                            tt[0] = fmaf(d0, acc[0], fmaf(-1152.0f * d0, Xa[sb], tt[0]));
-                            tt[1] = fmaf(d0, acc[1], fmaf(-1152.0f * d0, Xb[sb], tt[1]));
-                            tt[2] = fmaf(d1, acc[2], fmaf(-1152.0f * d1, Xa[sb], tt[2]));
-                            tt[3] = fmaf(d1, acc[3], fmaf(-1152.0f * d1, Xb[sb], tt[3]));
-                        }
-                }
-            }
+            if (tile_ok) qgemv_item<TYPE, MT, NMAT, PLANES, G::RB>(ring + (j % P) * G::BYTES, ix, g, c, tot);
             __syncwarp(); // every lane is done with the slot before it is refilled
             issue();
         }

@@ -15,17 +15,21 @@
 //   xl   fp16 residual x - xh (only for f32 inputs: x = xh + xl to 2^-22);
 //   xs   f32 sums of x over each 32-value sub-block.
 //
-// Exactness of the unpacking:
-//   Q4_K  (0x6400 | q) is the fp16 value 1024 + q.  One HFMA2 with
-//         (sc, -1024 sc) turns it into sc*q exactly (sc*q <= 945), so the
-//         sub-block scale is applied before the MMA and one accumulator spans
-//         the whole 256-value block; high nibbles are masked in place
-//         (1024 + 16 q) and use (sc/16, -64 sc).  The mins enter through one
-//         more MMA of the 6-bit mins against the sub-block sums (split into
-//         two fp16 planes).  Per block: y += d * acc - dmin * acc_min, the
-//         same algebra as row_dot_q4_k_avx2 (src/kernels.cpp:759-762).
-//   Q8_0  (q ^ 0x80) gives 1152 + q in fp16 via PRMT with 0x64; per block
-//         y += d * acc - 1152 d * X.
+// Exactness of the unpacking.  A code q masked in place is read as the fp16
+// bit pattern q, i.e. the subnormal q * 2^-24: exact, and one AND with a single
+// immediate mask per pair of codes (no magic-exponent OR, so no second constant
+// has to live in a register).  The tensor cores take subnormal fp16 operands
+// exactly.
+//   Q4_K  one HMUL2 by (sc, sc) gives sc*q * 2^-24 exactly (sc*q <= 945 stays
+//         on the subnormal grid), so the sub-block scale is applied before the
+//         MMA and one accumulator spans the whole 256-value block; high
+//         nibbles are masked in place (16 q * 2^-24) and use (sc/16, sc/16).
+//         The mins enter through one more MMA of the 6-bit mins against the
+//         sub-block sums (split into two fp16 planes).  Per block:
+//         y += (2^24 d) * acc - dmin * acc_min, the same algebra as
+//         row_dot_q4_k_avx2 (src/kernels.cpp:759-762).
+//   Q8_0  (q ^ 0x80) is 128 + q; PRMT with zero bytes makes it the subnormal
+//         (128 + q) * 2^-24; per block y += (2^24 d) * acc - 128 d * X.
 // All products are exact in the tensor core's fp32 accumulation; the result
 // differs from the reference only by summation order.
 #pragma once
@@ -172,14 +176,14 @@ struct QTile {
 // ---- Q4_K -----------------------------------------------------------------
 
 struct Q4kRowConsts {
-    uint32_t hs_lo, hb_lo, hs_hi, hb_hi; // half2 (sc, -1024 sc), (sc/16, -64 sc)
-    uint32_t mins;                       // half2 (m_2c, m_2c+1)
-    float d, dmin;
+    uint32_t hs_lo, hs_hi; // half2 (sc, sc) and (sc/16, sc/16)
+    uint32_t mins;         // half2 (m_2c, m_2c+1)
+    float d, dmin;         // d carries the 2^24 of the subnormal codes
 };
 
 __device__ __forceinline__ Q4kRowConsts q4k_row_consts(const uint4 &h, int c) {
     Q4kRowConsts r;
-    r.d = half_lo_f(h.x);
+    r.d = half_lo_f(h.x) * 16777216.0f;
     r.dmin = half_hi_f(h.x);
     const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
     // All sixteen 6-bit values, one per byte (src/quant.cpp:63-71).
@@ -195,9 +199,7 @@ __device__ __forceinline__ Q4kRowConsts q4k_row_consts(const uint4 &h, int c) {
     const uint32_t sc_lo2 = prmt(sc_pair, 0, 0x1010u);         // (sc_lo, sc_lo)
     const uint32_t sc_hi2 = prmt(sc_pair, 0, 0x3232u);         // (sc_hi, sc_hi)
     r.hs_lo = sc_lo2;
-    r.hb_lo = hmul2_u32(sc_lo2, 0xE400E400u);                  // * -1024
     r.hs_hi = hmul2_u32(sc_hi2, 0x2C002C00u);                  // * 1/16
-    r.hb_hi = hmul2_u32(sc_hi2, 0xD400D400u);                  // * -64
     return r;
 }
 
@@ -218,17 +220,17 @@ __device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1
     for (int i = 0; i < 8; ++i) {
         const uint32_t s0 = w0[i] >> 8, s1 = w1[i] >> 8;
         // low nibbles: sub-block 2c
-        const uint32_t a0 = hfma2_u32(lop_and_or(w0[i], 0x000F000Fu, 0x64006400u), r0.hs_lo, r0.hb_lo);
-        const uint32_t a1 = hfma2_u32(lop_and_or(w1[i], 0x000F000Fu, 0x64006400u), r1.hs_lo, r1.hb_lo);
-        const uint32_t a2 = hfma2_u32(lop_and_or(s0, 0x000F000Fu, 0x64006400u), r0.hs_lo, r0.hb_lo);
-        const uint32_t a3 = hfma2_u32(lop_and_or(s1, 0x000F000Fu, 0x64006400u), r1.hs_lo, r1.hb_lo);
+        const uint32_t a0 = hmul2_u32(w0[i] & 0x000F000Fu, r0.hs_lo);
+        const uint32_t a1 = hmul2_u32(w1[i] & 0x000F000Fu, r1.hs_lo);
+        const uint32_t a2 = hmul2_u32(s0 & 0x000F000Fu, r0.hs_lo);
+        const uint32_t a3 = hmul2_u32(s1 & 0x000F000Fu, r1.hs_lo);
 #pragma unroll
         for (int p = 0; p < PLANES; ++p) mma_f16(acc[i & 1], a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
         // high nibbles: sub-block 2c+1
-        const uint32_t e0 = hfma2_u32(lop_and_or(w0[i], 0x00F000F0u, 0x64006400u), r0.hs_hi, r0.hb_hi);
-        const uint32_t e1 = hfma2_u32(lop_and_or(w1[i], 0x00F000F0u, 0x64006400u), r1.hs_hi, r1.hb_hi);
-        const uint32_t e2 = hfma2_u32(lop_and_or(s0, 0x00F000F0u, 0x64006400u), r0.hs_hi, r0.hb_hi);
-        const uint32_t e3 = hfma2_u32(lop_and_or(s1, 0x00F000F0u, 0x64006400u), r1.hs_hi, r1.hb_hi);
+        const uint32_t e0 = hmul2_u32(w0[i] & 0x00F000F0u, r0.hs_hi);
+        const uint32_t e1 = hmul2_u32(w1[i] & 0x00F000F0u, r1.hs_hi);
+        const uint32_t e2 = hmul2_u32(s0 & 0x00F000F0u, r0.hs_hi);
+        const uint32_t e3 = hmul2_u32(s1 & 0x00F000F0u, r1.hs_hi);
 #pragma unroll
         for (int p = 0; p < PLANES; ++p)
             mma_f16(acc[2 + (i & 1)], e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);

@@ -162,9 +162,9 @@ __global__ void __launch_bounds__(NW * 32)
         // Q6_K (src/quant.cpp:347-372): one MMA per 16-value scale group j of a
         // block; lane (g, c) takes values 16j + 4c .. 16j + 4c + 3 of rows g and
         // g+8, so x is read in its natural order (4 consecutive fp16 per lane).
-        // The 6-bit code c6 becomes fp16 1024 + c6 (0x6400 | c6) and 1056 is
-        // subtracted exactly: A holds q = c6 - 32 exactly; the accumulator of
-        // each group is scaled by d * scale (exact product) in f32.
+        // The 6-bit code c6 placed in a zero fp16 is the subnormal c6 * 2^-24;
+        // subtracting 32 * 2^-24 is exact, so A holds (c6 - 32) * 2^-24; the
+        // accumulator of each group is scaled by 2^24 d * scale in f32.
         const uint32_t nblk = p.in_dim / 256;
         for (uint32_t b = warp; b < nblk; b += NW) {
 #pragma unroll 2
@@ -197,11 +197,11 @@ __global__ void __launch_bounds__(NW * 32)
                             const uint32_t ql = ldg_nc_u16(bp + ql_off) | (ldg_nc_u16(bp + ql_off + 2) << 16);
                             const uint32_t qh = ldg_nc_u16(bp + qh_off) | (ldg_nc_u16(bp + qh_off + 2) << 16);
                             const uint32_t c6 = ((ql >> nib) & 0x0F0F0F0Fu) | (((qh >> qsh) & 0x03030303u) << 4);
-                            a[hr][0] = hsub2_u32(prmt(c6, 0x64646464u, 0x5140u), 0x64206420u);
-                            a[hr][1] = hsub2_u32(prmt(c6, 0x64646464u, 0x7362u), 0x64206420u);
+                            a[hr][0] = hsub2_u32(prmt(c6, 0u, 0x5140u), 0x00200020u);
+                            a[hr][1] = hsub2_u32(prmt(c6, 0u, 0x7362u), 0x00200020u);
                             const float d = fp16_bits_to_f32(static_cast<uint16_t>(ldg_nc_u16(bp + 208)));
                             const int8_t sc = static_cast<int8_t>(ldg_nc_u16(bp + 192 + (j & ~1u)) >> (8 * (j & 1)));
-                            ds[hr] = __fmul_rn(d, static_cast<float>(sc));
+                            ds[hr] = __fmul_rn(d, static_cast<float>(sc)) * 16777216.0f; // codes carry 2^-24
                         }
                         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -249,20 +249,21 @@ __global__ void __launch_bounds__(NW * 32)
                     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int pl = 0; pl < PLANES; ++pl) {
-                        mma_f16(acc, prmt(va0, 0x64646464u, 0x4240u), prmt(va1, 0x64646464u, 0x4240u),
-                                prmt(va0, 0x64646464u, 0x4341u), prmt(va1, 0x64646464u, 0x4341u),
+                        mma_f16(acc, prmt(va0, 0u, 0x4240u), prmt(va1, 0u, 0x4240u),
+                                prmt(va0, 0u, 0x4341u), prmt(va1, 0u, 0x4341u),
                                 xb[pl][0], xb[pl][1]);
-                        mma_f16(acc, prmt(vb0, 0x64646464u, 0x4240u), prmt(vb1, 0x64646464u, 0x4240u),
-                                prmt(vb0, 0x64646464u, 0x4341u), prmt(vb1, 0x64646464u, 0x4341u),
+                        mma_f16(acc, prmt(vb0, 0u, 0x4240u), prmt(vb1, 0u, 0x4240u),
+                                prmt(vb0, 0u, 0x4341u), prmt(vb1, 0u, 0x4341u),
                                 xb[pl][2], xb[pl][3]);
                     }
                     const float dr0 = fp16_bits_to_f32(static_cast<uint16_t>(d0));
                     const float dr1 = fp16_bits_to_f32(static_cast<uint16_t>(d1));
+                    const float dr0s = dr0 * 16777216.0f, dr1s = dr1 * 16777216.0f; // codes carry 2^-24
                     float *t = tot[m][mt];
-                    t[0] = fmaf(dr0, acc[0], fmaf(-1152.0f * dr0, Xa, t[0]));
-                    t[1] = fmaf(dr0, acc[1], fmaf(-1152.0f * dr0, Xb, t[1]));
-                    t[2] = fmaf(dr1, acc[2], fmaf(-1152.0f * dr1, Xa, t[2]));
-                    t[3] = fmaf(dr1, acc[3], fmaf(-1152.0f * dr1, Xb, t[3]));
+                    t[0] = fmaf(dr0s, acc[0], fmaf(-128.0f * dr0, Xa, t[0]));
+                    t[1] = fmaf(dr0s, acc[1], fmaf(-128.0f * dr0, Xb, t[1]));
+                    t[2] = fmaf(dr1s, acc[2], fmaf(-128.0f * dr1, Xa, t[2]));
+                    t[3] = fmaf(dr1s, acc[3], fmaf(-128.0f * dr1, Xb, t[3]));
                 }
         }
     }

@@ -28,6 +28,7 @@ template <int MODE>
 int launch_qgemv(const QGemvParams &prm, int planes, uint32_t grid_y, uint32_t grid_z,
                  cudaStream_t s);
 int check_quant_shape(uint32_t type_id, uint32_t in_dim, const char *what);
+int check_quant_alignment(uint32_t type_id, uint64_t byte_offset, const char *what);
 bool staged_shape(uint32_t type_id, uint32_t in_dim);
 int xplane_layout(uint32_t type_id);
 int launch_xplanes_staged(const void *x, int32_t x_dtype, uint32_t rows, uint32_t k_dim, int layout,
@@ -145,6 +146,9 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     if ((rc = check_quant_shape(a->gate_type, a->d_model, "expert gate"))) return rc;
     if ((rc = check_quant_shape(a->up_type, a->d_model, "expert up"))) return rc;
     if ((rc = check_quant_shape(a->down_type, a->ffn, "expert down"))) return rc;
+    // slot bases are device-checked; the offsets inside a slot are checked here
+    if ((rc = check_quant_alignment(a->up_type, a->up_offset, "expert up offset"))) return rc;
+    if ((rc = check_quant_alignment(a->down_type, a->down_offset, "expert down offset"))) return rc;
     if (a->gate_type != a->up_type)
         return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION,
                          "fused gate/up needs one block type for both projections");
@@ -189,8 +193,8 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     const int xplanes = a->x_dtype == FM_X_F32 ? 2 : 1;
     // Expert slots come from cudaMalloc-class allocations (256-byte aligned);
     // the staged kernels also re-check each slot base on the device.
-    const bool gu_staged = staged_shape(a->gate_type, a->d_model);
-    const bool dn_staged = staged_shape(a->down_type, a->ffn);
+    const bool gu_staged = staged_shape(a->gate_type, a->d_model) && a->up_offset % 16 == 0;
+    const bool dn_staged = staged_shape(a->down_type, a->ffn) && a->down_offset % 16 == 0;
     rc = gu_staged ? launch_xplanes_staged(a->x, a->x_dtype, a->tokens, a->d_model,
                                            xplane_layout(a->gate_type), xh, xplanes > 1 ? xl : nullptr, xs, s)
                    : launch_xplanes_for(a->gate_type, a->x, a->x_dtype, a->tokens, a->d_model, xh,

@@ -324,3 +324,36 @@ def test_moe_block_missing_expert_flags(cuda, oracle):
     dslots[3] = None
     cuda.moe_block(x, logits, dslots, top_k=k, ffn=ffn, gate_type=TYPE_Q4_K)
     assert cuda.device_status(clear=True) == 18  # EXPERT_EXECUTION_MISMATCH
+
+
+def test_misaligned_quantised_matrices_are_refused(cuda, oracle):
+    """A Q4_K matrix whose first byte is not 16-byte aligned (the loads the
+    kernels issue) is refused on the host with INVALID_ARGUMENT, not read."""
+    import ctypes as C
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200._lib import FmError, load
+
+    rng = np.random.default_rng(2)
+    E, k, d, ffn = 2, 1, 256, 256
+    slots = make_experts(oracle, rng, E, d, ffn, TYPE_Q4_K)
+    pad = [np.concatenate([s, np.zeros(16, np.uint8)]) for s in slots]
+    dslots = [dev(s) for s in pad]
+    table = hotpath.slot_table(dslots, torch.device("cuda"))
+    x = torch.randn(3, d, device="cuda")
+    logits = torch.randn(3, E, device="cuda")
+    y = torch.empty(3, d, device="cuda")
+    gb = ffn * (d // 256) * 144
+    ws = torch.empty(hotpath.moe_workspace_bytes(3, E, k, d, ffn), dtype=torch.uint8, device="cuda")
+    lib = load()
+    for up, down in ((gb + 8, 2 * gb), (gb, 2 * gb + 2)):
+        a = hotpath.moe_args(x, logits, table, experts=E, top_k=k, d_model=d, ffn=ffn, gate_type=TYPE_Q4_K,
+                             up_type=TYPE_Q4_K, down_type=TYPE_Q4_K, up_offset=up, down_offset=down, y=y)
+        rc = lib.fmcuda_moe_block(C.byref(a), C.c_void_p(ws.data_ptr()), ws.numel(), None)
+        assert rc == 26, rc  # INVALID_ARGUMENT
+    w = dev(np.concatenate([np.zeros(4, np.uint8), slots[0][:gb]]))
+    with pytest.raises(FmError) as e:
+        cuda.gemv_quant(TYPE_Q4_K, w[4:], x, out_dim=ffn, in_dim=d)
+    assert e.value.code == 26
+    torch.cuda.synchronize()
+    assert cuda.device_status(clear=True) == 0
