@@ -308,14 +308,17 @@ int launch_async_inst(const QGemvParams &prm, uint32_t tok_tiles, uint32_t exper
     constexpr int MT = FMB_GEMV_MT, NW = FMB_GEMV_NW;
     constexpr int NMAT = MODE == GEMV_GATE_UP ? 2 : 1;
     using G = StageGeom<TYPE, MT, NMAT>;
-    constexpr size_t smem = static_cast<size_t>(NW) * P * G::BYTES;
+    // rings, then (MoE modes) the per-expert prefix of token tiles
+    constexpr size_t ring = static_cast<size_t>(NW) * P * G::BYTES;
+    constexpr size_t smem_max = ring + (kMaxGroupExperts + 4) * 4;
+    const size_t smem = ring + (MODE == GEMV_PLAIN ? 0 : (static_cast<size_t>(experts) + 4) / 4 * 16);
     auto kern = qgemv_async_kernel<TYPE, MT, NW, PL, MODE, P>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
         cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem));
+                                               static_cast<int>(smem_max));
         if (err != cudaSuccess) return cuda_status(err, "streamed GEMV shared-memory limit");
         configured[dev] = true;
     }

@@ -215,7 +215,8 @@ __global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
     constexpr int TILE = G::TILE;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[NW][NMAT][TILE][8];
-    __shared__ uint32_t s_prefix[kMaxGroupExperts + 1]; // token tiles before expert e
+    // token tiles before expert e, in the dynamic shared memory after the rings
+    uint32_t *s_prefix = reinterpret_cast<uint32_t *>(smem + static_cast<size_t>(NW) * P * G::BYTES);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, c = lane & 3;

@@ -51,6 +51,16 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A * B (accumulator starts from zero, no C registers to clear).
+__device__ __forceinline__ void mma_f16_zc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
     asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -109,11 +119,6 @@ __device__ __forceinline__ float half_lo_f(uint32_t v) {
 }
 __device__ __forceinline__ float half_hi_f(uint32_t v) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
-}
-
-// (1024 + v_lo, 1024 + v_hi) for the bytes 0 and 1 of `v` -> exact (v_lo, v_hi).
-__device__ __forceinline__ uint32_t bytes01_to_half2(uint32_t v) {
-    return hsub2_u32(prmt(v, 0x64646464u, 0x4140u), 0x64006400u);
 }
 
 // ---- x planes -------------------------------------------------------------
@@ -186,20 +191,21 @@ __device__ __forceinline__ Q4kRowConsts q4k_row_consts(const uint4 &h, int c) {
     r.d = half_lo_f(h.x) * 16777216.0f;
     r.dmin = half_hi_f(h.x);
     const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;
-    // All sixteen 6-bit values, one per byte (src/quant.cpp:63-71).
-    const uint32_t sc03 = s0 & 0x3F3F3F3Fu;
-    const uint32_t m03 = s1 & 0x3F3F3F3Fu;
-    const uint32_t sc47 = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
-    const uint32_t m47 = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
-    const uint32_t shift = 16u * (c & 1);
-    const uint32_t scw = ((c < 2) ? sc03 : sc47) >> shift; // bytes: sc_2c, sc_2c+1
-    const uint32_t mw = ((c < 2) ? m03 : m47) >> shift;
-    const uint32_t sc_pair = bytes01_to_half2(scw);            // (sc_lo, sc_hi)
-    r.mins = bytes01_to_half2(mw);                             // (m_lo, m_hi)
-    const uint32_t sc_lo2 = prmt(sc_pair, 0, 0x1010u);         // (sc_lo, sc_lo)
-    const uint32_t sc_hi2 = prmt(sc_pair, 0, 0x3232u);         // (sc_hi, sc_hi)
-    r.hs_lo = sc_lo2;
-    r.hs_hi = hmul2_u32(sc_hi2, 0x2C002C00u);                  // * 1/16
+    // The lane's two sub-blocks j = 2c, 2c + 1 (src/quant.cpp:63-71): bytes
+    // k = 2 (c & 1), k + 1 of each scale word.  R = (sc_2c, sc_2c+1, m_2c, m_2c+1).
+    const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;
+    const uint32_t y = prmt(s0, s1, sel);                              // low 6 bits (j < 4), top 2 (j >= 4)
+    uint32_t R;
+    if (c < 2) {
+        R = y & 0x3F3F3F3Fu;
+    } else {
+        const uint32_t x = prmt(s2, s2 >> 4, sel) & 0x0F0F0F0Fu;      // low 4 bits (j >= 4)
+        R = x | ((y >> 2) & 0x30303030u);
+    }
+    // bytes -> exact fp16 via 1024 + b
+    r.hs_lo = hsub2_u32(prmt(R, 0x64646464u, 0x4040u), 0x64006400u);  // (sc_2c, sc_2c)
+    r.hs_hi = hfma2_u32(prmt(R, 0x64646464u, 0x4141u), 0x2C002C00u, 0xD400D400u); // (sc_2c+1 / 16) x 2
+    r.mins = hsub2_u32(prmt(R, 0x64646464u, 0x4342u), 0x64006400u);   // (m_2c, m_2c+1)
     return r;
 }
 
@@ -213,7 +219,7 @@ __device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1
     const Q4kRowConsts r0 = q4k_row_consts(h0, c);
     const Q4kRowConsts r1 = q4k_row_consts(h1, c);
     // four independent accumulator chains (low / high nibbles x even / odd words)
-    float acc[4][4] = {};
+    float acc[4][4];
     const uint32_t w0[8] = {q0[0].x, q0[0].y, q0[0].z, q0[0].w, q0[1].x, q0[1].y, q0[1].z, q0[1].w};
     const uint32_t w1[8] = {q1[0].x, q1[0].y, q1[0].z, q1[0].w, q1[1].x, q1[1].y, q1[1].z, q1[1].w};
 #pragma unroll
@@ -225,18 +231,23 @@ __device__ __forceinline__ void q4k_mtile_block(const uint4 &h0, const uint4 &h1
         const uint32_t a2 = hmul2_u32(s0 & 0x000F000Fu, r0.hs_lo);
         const uint32_t a3 = hmul2_u32(s1 & 0x000F000Fu, r1.hs_lo);
 #pragma unroll
-        for (int p = 0; p < PLANES; ++p) mma_f16(acc[i & 1], a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
+        for (int p = 0; p < PLANES; ++p) {
+            if (i < 2 && p == 0) mma_f16_zc(acc[i & 1], a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
+            else mma_f16(acc[i & 1], a0, a1, a2, a3, xb[p][2 * i], xb[p][2 * i + 1]);
+        }
         // high nibbles: sub-block 2c+1
         const uint32_t e0 = hmul2_u32(w0[i] & 0x00F000F0u, r0.hs_hi);
         const uint32_t e1 = hmul2_u32(w1[i] & 0x00F000F0u, r1.hs_hi);
         const uint32_t e2 = hmul2_u32(s0 & 0x00F000F0u, r0.hs_hi);
         const uint32_t e3 = hmul2_u32(s1 & 0x00F000F0u, r1.hs_hi);
 #pragma unroll
-        for (int p = 0; p < PLANES; ++p)
-            mma_f16(acc[2 + (i & 1)], e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);
+        for (int p = 0; p < PLANES; ++p) {
+            if (i < 2 && p == 0) mma_f16_zc(acc[2 + (i & 1)], e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);
+            else mma_f16(acc[2 + (i & 1)], e0, e1, e2, e3, xb[p][16 + 2 * i], xb[p][16 + 2 * i + 1]);
+        }
     }
-    float accm[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_f16(accm, r0.mins, r1.mins, 0u, 0u, xm[0], 0u);
+    float accm[4];
+    mma_f16_zc(accm, r0.mins, r1.mins, 0u, 0u, xm[0], 0u);
     mma_f16(accm, r0.mins, r1.mins, 0u, 0u, xm[1], 0u);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
