@@ -168,9 +168,17 @@ __device__ __forceinline__ bool gg_wait(uint64_t *bar, uint32_t parity, volatile
 
 // ---- decoding one 64-value step of one row into 32 fp16x2 words (k order) ----
 
+// The fast paths below read a code placed in a zero fp16 as the subnormal
+// code * 2^-24 (exact; PRMT with zero bytes, no magic-exponent constant), and
+// fold the scale powers of two into the block factor; each produces the same
+// bits as the generic path, which stays for blocks whose scaled factor would
+// not fit fp16.
+
 // Q8_0: blocks 2*ST and 2*ST+1 of the chunk, bytes [68*ST, 68*ST + 68).
-// (q ^ 0x80) | 0x6400 is the fp16 1152 + q; subtracting 1152 is exact and the
-// multiply by d rounds once, giving RN(d * q).
+// Generic: (q ^ 0x80) | 0x6400 is the fp16 1152 + q; subtracting 1152 is exact
+// and the multiply by d rounds once, giving RN(d * q).  Fast (d < 2^-8): one
+// FMA of the subnormal (128 + q) * 2^-24 with 2^24 d and -128 d, the same
+// single rounding of d * q.
 template <int ST>
 __device__ __forceinline__ void gg_decode_q8_0(const uint8_t *row, uint32_t (&v)[32]) {
     constexpr int BASE = (68 * ST) / 16 * 16;
@@ -188,57 +196,90 @@ __device__ __forceinline__ void gg_decode_q8_0(const uint8_t *row, uint32_t (&v)
     for (int b = 0; b < 2; ++b) {
         const int o = M0 + 34 * b;
         const uint32_t dbits = (o % 4 == 0) ? (w[o / 4] & 0xFFFFu) : (w[o / 4] >> 16);
-        const uint32_t d2 = dbits | (dbits << 16);
         const int qo = o + 2;
         const int qi = qo / 4;
         const int sh = (qo % 4) * 8;
+        const float df = fp16_bits_to_f32(static_cast<uint16_t>(dbits));
+        if (fabsf(df) < 0.00390625f) {
+            const __half2 dd = __float2half2_rn(df * 16777216.0f), nb = __float2half2_rn(-128.0f * df);
+            const uint32_t udd = *reinterpret_cast<const uint32_t *>(&dd), unb = *reinterpret_cast<const uint32_t *>(&nb);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            uint32_t q = sh ? __funnelshift_r(w[qi + j], w[qi + j + 1], sh) : w[qi + j];
-            q ^= 0x80808080u;
-            const uint32_t lo = prmt(q, 0x64646464u, 0x5140u);
-            const uint32_t hi = prmt(q, 0x64646464u, 0x7362u);
-            v[16 * b + 2 * j] = hmul2_u32(hsub2_u32(lo, 0x64806480u), d2);
-            v[16 * b + 2 * j + 1] = hmul2_u32(hsub2_u32(hi, 0x64806480u), d2);
+            for (int j = 0; j < 8; ++j) {
+                uint32_t q = sh ? __funnelshift_r(w[qi + j], w[qi + j + 1], sh) : w[qi + j];
+                q ^= 0x80808080u;
+                v[16 * b + 2 * j] = hfma2_u32(prmt(q, 0u, 0x5140u), udd, unb);
+                v[16 * b + 2 * j + 1] = hfma2_u32(prmt(q, 0u, 0x7362u), udd, unb);
+            }
+        } else {
+            const uint32_t d2 = dbits | (dbits << 16);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t q = sh ? __funnelshift_r(w[qi + j], w[qi + j + 1], sh) : w[qi + j];
+                q ^= 0x80808080u;
+                const uint32_t lo = prmt(q, 0x64646464u, 0x5140u);
+                const uint32_t hi = prmt(q, 0x64646464u, 0x7362u);
+                v[16 * b + 2 * j] = hmul2_u32(hsub2_u32(lo, 0x64806480u), d2);
+                v[16 * b + 2 * j + 1] = hmul2_u32(hsub2_u32(hi, 0x64806480u), d2);
+            }
         }
     }
 }
 
 // Q4_K: group G4 (values 64*G4 .. 64*G4+63) of the 256-value block: low
 // nibbles of qs[32*G4 .. +32) are sub-block 2*G4, high nibbles 2*G4+1.
-// (1024 + q) * sc - 1024 * sc = sc * q exactly; then one rounding of
-// d * (sc * q) - RN(dmin * m).
+// Generic: (1024 + q) * sc - 1024 * sc = sc * q exactly; then one rounding of
+// d * (sc * q) - RN(dmin * m).  Fast (|d| < 4): the subnormal q * 2^-24 (high
+// nibbles masked in place: 16 q * 2^-24) times 2^10 sc (2^6 sc) is
+// sc * q * 2^-14 exactly, and one FMA with 2^14 d and -RN(dmin * m) rounds
+// d * (sc * q) - RN(dmin * m) once, as the generic path does.
 template <int G4>
 __device__ __forceinline__ void gg_decode_q4_k(const uint8_t *row, uint32_t (&v)[32]) {
     const uint4 h = *reinterpret_cast<const uint4 *>(row);
     const uint4 qa = *reinterpret_cast<const uint4 *>(row + 16 + 32 * G4);
     const uint4 qb = *reinterpret_cast<const uint4 *>(row + 32 + 32 * G4);
     const uint32_t dbits = h.x & 0xFFFFu;
+    const float df = fp16_bits_to_f32(static_cast<uint16_t>(dbits));
     const float dmin = fp16_bits_to_f32(static_cast<uint16_t>(h.x >> 16));
-    const uint32_t d2 = dbits | (dbits << 16);
     uint32_t sc0, mn0, sc1, mn1;
     q4k_scale_min_w(2 * G4, h.y, h.z, h.w, sc0, mn0);
     q4k_scale_min_w(2 * G4 + 1, h.y, h.z, h.w, sc1, mn1);
-    const __half2 s0 = __floats2half2_rn(static_cast<float>(sc0), static_cast<float>(sc0));
-    const __half2 n0 = __floats2half2_rn(-1024.0f * sc0, -1024.0f * sc0);
-    const __half2 s1 = __floats2half2_rn(static_cast<float>(sc1), static_cast<float>(sc1));
-    const __half2 n1 = __floats2half2_rn(-1024.0f * sc1, -1024.0f * sc1);
     const float m0f = -(dmin * static_cast<float>(mn0)), m1f = -(dmin * static_cast<float>(mn1));
     const __half2 mm0 = __floats2half2_rn(m0f, m0f), mm1 = __floats2half2_rn(m1f, m1f);
-    const uint32_t us0 = *reinterpret_cast<const uint32_t *>(&s0), un0 = *reinterpret_cast<const uint32_t *>(&n0);
-    const uint32_t us1 = *reinterpret_cast<const uint32_t *>(&s1), un1 = *reinterpret_cast<const uint32_t *>(&n1);
     const uint32_t um0 = *reinterpret_cast<const uint32_t *>(&mm0), um1 = *reinterpret_cast<const uint32_t *>(&mm1);
     const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    if (fabsf(df) < 4.0f) {
+        const __half2 s0 = __float2half2_rn(1024.0f * sc0), s1 = __float2half2_rn(64.0f * sc1);
+        const __half2 dd = __float2half2_rn(16384.0f * df);
+        const uint32_t us0 = *reinterpret_cast<const uint32_t *>(&s0), us1 = *reinterpret_cast<const uint32_t *>(&s1);
+        const uint32_t udd = *reinterpret_cast<const uint32_t *>(&dd);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const uint32_t lo = qw[j] & 0x0F0F0F0Fu;
-        const uint32_t hi = (qw[j] >> 4) & 0x0F0F0F0Fu;
-        const uint32_t l01 = prmt(lo, 0x64646464u, 0x5140u), l23 = prmt(lo, 0x64646464u, 0x7362u);
-        const uint32_t h01 = prmt(hi, 0x64646464u, 0x5140u), h23 = prmt(hi, 0x64646464u, 0x7362u);
-        v[2 * j] = hfma2_u32(hfma2_u32(l01, us0, un0), d2, um0);
-        v[2 * j + 1] = hfma2_u32(hfma2_u32(l23, us0, un0), d2, um0);
-        v[16 + 2 * j] = hfma2_u32(hfma2_u32(h01, us1, un1), d2, um1);
-        v[16 + 2 * j + 1] = hfma2_u32(hfma2_u32(h23, us1, un1), d2, um1);
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t lo = qw[j] & 0x0F0F0F0Fu;
+            const uint32_t hi = qw[j] & 0xF0F0F0F0u;
+            v[2 * j] = hfma2_u32(hmul2_u32(prmt(lo, 0u, 0x5140u), us0), udd, um0);
+            v[2 * j + 1] = hfma2_u32(hmul2_u32(prmt(lo, 0u, 0x7362u), us0), udd, um0);
+            v[16 + 2 * j] = hfma2_u32(hmul2_u32(prmt(hi, 0u, 0x5140u), us1), udd, um1);
+            v[16 + 2 * j + 1] = hfma2_u32(hmul2_u32(prmt(hi, 0u, 0x7362u), us1), udd, um1);
+        }
+    } else {
+        const uint32_t d2 = dbits | (dbits << 16);
+        const __half2 s0 = __floats2half2_rn(static_cast<float>(sc0), static_cast<float>(sc0));
+        const __half2 n0 = __floats2half2_rn(-1024.0f * sc0, -1024.0f * sc0);
+        const __half2 s1 = __floats2half2_rn(static_cast<float>(sc1), static_cast<float>(sc1));
+        const __half2 n1 = __floats2half2_rn(-1024.0f * sc1, -1024.0f * sc1);
+        const uint32_t us0 = *reinterpret_cast<const uint32_t *>(&s0), un0 = *reinterpret_cast<const uint32_t *>(&n0);
+        const uint32_t us1 = *reinterpret_cast<const uint32_t *>(&s1), un1 = *reinterpret_cast<const uint32_t *>(&n1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t lo = qw[j] & 0x0F0F0F0Fu;
+            const uint32_t hi = (qw[j] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t l01 = prmt(lo, 0x64646464u, 0x5140u), l23 = prmt(lo, 0x64646464u, 0x7362u);
+            const uint32_t h01 = prmt(hi, 0x64646464u, 0x5140u), h23 = prmt(hi, 0x64646464u, 0x7362u);
+            v[2 * j] = hfma2_u32(hfma2_u32(l01, us0, un0), d2, um0);
+            v[2 * j + 1] = hfma2_u32(hfma2_u32(l23, us0, un0), d2, um0);
+            v[16 + 2 * j] = hfma2_u32(hfma2_u32(h01, us1, un1), d2, um1);
+            v[16 + 2 * j + 1] = hfma2_u32(hfma2_u32(h23, us1, un1), d2, um1);
+        }
     }
 }
 
