@@ -102,6 +102,35 @@ def test_prefill_small_vs_oracle(cuda, oracle, t, T):
     assert rel_err(y.cpu().numpy(), y_o) < TOL
 
 
+@pytest.mark.parametrize("t,big,xs", [(TYPE_Q8_0, 1.0, 1.0), (TYPE_Q4_K, 2000.0, 1e-3)])
+def test_prefill_large_block_scales(cuda, oracle, t, big, xs):
+    """Experts whose block scales are too large for the converters' subnormal
+    fast path (Q8_0 d >= 2^-8, Q4_K d >= 4) take the generic path; both kinds
+    of block sit in one launch and must agree with the oracle.  x is scaled so
+    that the activations stay inside fp16 range."""
+    rng = np.random.default_rng(31 + t)
+    E, k, d, ffn, T = 4, 2, 256, 256, 64
+    slots = []
+    for e in range(E):
+        std = big if e % 2 else 0.02
+        slots.append(np.concatenate([oracle.quantize(t, rng.normal(0, std, size=n).astype(np.float32))
+                                     for n in (ffn * d, ffn * d, d * ffn)]))
+    x = bf16_round(rng.normal(0, xs, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    y, ids, w = cuda.moe_prefill(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                                 gate_type=t, return_routing=True)
+    assert cuda.device_status() == 0
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, t)
+    big_rows = np.isin(ids_o, [1, 3]).any(axis=1)
+    assert big_rows.any() and (~big_rows).any()
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
+    # the decode path reads the same records
+    y_dec = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                           gate_type=t)
+    assert rel_err(y_dec.cpu().numpy(), y_o) < TOL
+
+
 @pytest.mark.parametrize("xdt", ["bf16", "f32"])
 def test_prefill_ragged_groups_half_chunk(cuda, oracle, xdt):
     # Zipf routing: empty experts, experts with 3+ token tiles; down K = 384
