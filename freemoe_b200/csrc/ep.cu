@@ -264,12 +264,13 @@ extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_exp
     if (gate_type != up_type)
         return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "fused gate/up needs one block type for both projections");
     for (uint32_t t : {gate_type, down_type})
-        if (t != FM_TYPE_Q8_0 && t != FM_TYPE_Q4_K)
-            return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "the grouped GEMM takes Q8_0 or Q4_K weights");
-    const uint32_t kq = gate_type == FM_TYPE_Q4_K || down_type == FM_TYPE_Q4_K ? 256 : 64;
+        if (t != FM_TYPE_Q8_0 && t != FM_TYPE_Q4_K && t != FM_TYPE_Q6_K)
+            return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "the grouped GEMM takes Q8_0, Q4_K or Q6_K weights");
+    const uint32_t kq = gate_type != FM_TYPE_Q8_0 || down_type != FM_TYPE_Q8_0 ? 256 : 64;
     if (reinterpret_cast<uintptr_t>(x) % 16 || d_model % 128 || ffn % 128 || d_model % kq || ffn % kq)
         return set_error(FM_STATUS_SHAPE_MISMATCH,
-                         "expert rows must be 16-byte aligned fp16; d_model and ffn multiples of 128 (256 for Q4_K)");
+                         "expert rows must be 16-byte aligned fp16; d_model and ffn multiples of 128 (256 for "
+                         "Q4_K / Q6_K)");
     const uint64_t n64 = static_cast<uint64_t>(rows) * top_k;
     if (n64 > 0x7FFFFFFFull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
     const uint32_t n = static_cast<uint32_t>(n64);
@@ -373,12 +374,13 @@ extern "C" int fmcuda_moe_experts(const void *x, const uint32_t *expert_of_row, 
     if (gate_type != up_type)
         return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "fused gate/up needs one block type for both projections");
     for (uint32_t t : {gate_type, down_type})
-        if (t != FM_TYPE_Q8_0 && t != FM_TYPE_Q4_K)
-            return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "the grouped GEMM takes Q8_0 or Q4_K weights");
-    const uint32_t kq = gate_type == FM_TYPE_Q4_K || down_type == FM_TYPE_Q4_K ? 256 : 64;
+        if (t != FM_TYPE_Q8_0 && t != FM_TYPE_Q4_K && t != FM_TYPE_Q6_K)
+            return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION, "the grouped GEMM takes Q8_0, Q4_K or Q6_K weights");
+    const uint32_t kq = gate_type != FM_TYPE_Q8_0 || down_type != FM_TYPE_Q8_0 ? 256 : 64;
     if (reinterpret_cast<uintptr_t>(x) % 16 || d_model % 128 || ffn % 128 || d_model % kq || ffn % kq)
         return set_error(FM_STATUS_SHAPE_MISMATCH,
-                         "expert rows must be 16-byte aligned fp16; d_model and ffn multiples of 128 (256 for Q4_K)");
+                         "expert rows must be 16-byte aligned fp16; d_model and ffn multiples of 128 (256 for "
+                         "Q4_K / Q6_K)");
     const ExpertsLayout L = experts_layout(rows, experts, d_model, ffn);
     if (!workspace || workspace_bytes < L.total)
         return set_error(FM_STATUS_INVALID_ARGUMENT,

@@ -96,6 +96,18 @@ template <> struct GGeom<FM_TYPE_Q4_K> {
     static constexpr uint32_t CB = 144;
     static constexpr uint32_t RS = 3;
 };
+// Q6_K: one 210-byte block per chunk; block starts are only 2-byte aligned, so
+// the converter copies the 16-byte aligned window around the block (at most
+// 15 pieces = 240 bytes) and decodes from the block's offset in the window.
+template <> struct GGeom<FM_TYPE_Q6_K> {
+    static constexpr uint32_t CB = 210;
+    static constexpr uint32_t RS = 2;
+    static constexpr uint32_t WINDOW = 240;
+};
+template <int TYPE> constexpr uint32_t gg_pitch() {
+    if constexpr (TYPE == FM_TYPE_Q6_K) return GGeom<TYPE>::WINDOW;
+    else return GGeom<TYPE>::CB;
+}
 
 template <int TYPE, int NMAT> struct GGLayout {
     static constexpr uint32_t BN = NMAT == 2 ? GG_BN : GG_BN1;  // tokens per unit
@@ -103,7 +115,7 @@ template <int TYPE, int NMAT> struct GGLayout {
     static constexpr uint32_t SA = NMAT == 2 ? FMB_GG_SA2 : 8;          // A stages in TMEM
     static constexpr uint32_t A_COL0 = NMAT * BN;               // accumulators first
     static constexpr uint32_t A_STAGE_COLS = NMAT * (GG_BK / 2); // fp16 pairs per column
-    static constexpr uint32_t PITCH = GGeom<TYPE>::CB;         // raw row pitch (odd multiple of 16)
+    static constexpr uint32_t PITCH = gg_pitch<TYPE>();         // raw row pitch (odd multiple of 16)
     static constexpr uint32_t RS = GGeom<TYPE>::RS;
     static constexpr uint32_t B_STAGE = BN * GG_BK * 2;
     static constexpr uint32_t RAW_SLOT = 32 * PITCH;
@@ -283,10 +295,57 @@ __device__ __forceinline__ void gg_decode_q4_k(const uint8_t *row, uint32_t (&v)
     }
 }
 
+// Q6_K (src/quant.cpp:347-372): step ST covers values 64*ST .. 64*ST+63 of
+// the block, i.e. half h = ST/2 and the two 32-value groups 2*(ST&1) and
+// 2*(ST&1)+1: low bits from the nibble (ST&1) of ql[64h + l] and ql[64h + 32
+// + l], high bits from qh[32h + l] >> 2*group, scale group 4*ST + k/16.  `o`
+// is the block's (even) byte offset inside its copied window; words are read
+// aligned and shifted.  Each value is RN_f32(RN_f32(d * sc) * (c6 - 32)), the
+// reference's dequantised value bit for bit (one FMA: c6 * ds - 32 * ds),
+// then rounded once to fp16.
+template <int ST>
+__device__ __forceinline__ void gg_decode_q6_k(const uint8_t *win, uint32_t o, uint32_t (&v)[32]) {
+    constexpr uint32_t H = ST >> 1, NIB = 4 * (ST & 1), G0 = 2 * (ST & 1);
+    const uint32_t sh = (o & 3u) * 8u;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(win + (o & ~3u));
+    auto word = [&](uint32_t byte_off) -> uint32_t { // 4 bytes at o + byte_off (byte_off % 4 == 0)
+        const uint32_t i = byte_off >> 2;
+        return sh ? __funnelshift_r(w[i], w[i + 1], sh) : w[i];
+    };
+    const float d = fp16_bits_to_f32(*reinterpret_cast<const uint16_t *>(win + o + 208));
+    const uint32_t scw = word(192 + 4 * ST);
+    float ds[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ds[q] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(scw >> (8 * q))));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t qh = word(128 + 32 * H + 4 * i);
+        const uint32_t lo = word(64 * H + 4 * i), hi = word(64 * H + 32 + 4 * i);
+        const uint32_t c0 = ((lo >> NIB) & 0x0F0F0F0Fu) | (((qh >> (2 * G0)) & 0x03030303u) << 4);
+        const uint32_t c1 = ((hi >> NIB) & 0x0F0F0F0Fu) | (((qh >> (2 * G0 + 2)) & 0x03030303u) << 4);
+        float y0[4], y1[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const float f0 = static_cast<float>((c0 >> (8 * b)) & 0xFFu);
+            const float f1 = static_cast<float>((c1 >> (8 * b)) & 0xFFu);
+            const float s0 = ds[(4 * i + b) >> 4], s1 = ds[2 + ((4 * i + b) >> 4)];
+            y0[b] = fmaf(f0, s0, -32.0f * s0);
+            y1[b] = fmaf(f1, s1, -32.0f * s1);
+        }
+        const __half2 a0 = __floats2half2_rn(y0[0], y0[1]), a1 = __floats2half2_rn(y0[2], y0[3]);
+        const __half2 b0 = __floats2half2_rn(y1[0], y1[1]), b1 = __floats2half2_rn(y1[2], y1[3]);
+        v[2 * i] = *reinterpret_cast<const uint32_t *>(&a0);
+        v[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&a1);
+        v[16 + 2 * i] = *reinterpret_cast<const uint32_t *>(&b0);
+        v[16 + 2 * i + 1] = *reinterpret_cast<const uint32_t *>(&b1);
+    }
+}
+
 template <int TYPE, int ST>
-__device__ __forceinline__ void gg_decode(const uint8_t *row, uint32_t (&v)[32]) {
+__device__ __forceinline__ void gg_decode(const uint8_t *row, uint32_t o, uint32_t (&v)[32]) {
     if constexpr (TYPE == FM_TYPE_Q8_0) gg_decode_q8_0<ST>(row, v);
-    else gg_decode_q4_k<ST>(row, v);
+    else if constexpr (TYPE == FM_TYPE_Q4_K) gg_decode_q4_k<ST>(row, v);
+    else gg_decode_q6_k<ST>(row, o, v);
 }
 
 template <int TYPE, int NMAT, int EPI, int G>
@@ -450,19 +509,33 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
         // in row-major order, so each copy instruction covers ~512 contiguous
         // bytes of two or three rows instead of 32 scattered rows.
         uint32_t iss_nord = 0xFFFFFFFFu;
-        const uint8_t *iss_row0 = nullptr;
+        const uint8_t *iss_row0 = nullptr, *iss_end = nullptr;
         auto issue = [&](uint32_t j) {
             if (j < njobs) {
                 const uint32_t n_ord = j / J, ch = c0 + (j - n_ord * J) * cstep;
                 if (n_ord != iss_nord) {
                     const GUnit g = gg_unit<BN>(s_units, E, blockIdx.x + n_ord * gridDim.x, p.counts, p.offsets);
                     iss_row0 = p.slots[g.e] + w_off + static_cast<uint64_t>(g.rt * GG_BM + wq * 32u) * p.row_bytes;
+                    iss_end = p.slots[g.e] + w_off + static_cast<uint64_t>(p.out_dim) * p.row_bytes;
                     iss_nord = n_ord;
                 }
                 const uint8_t *src = iss_row0 + static_cast<uint64_t>(ch) * CB;
                 uint8_t *dst = ring + (j % RS) * L::RAW_SLOT;
                 const uint32_t bytes = min(CB, p.row_bytes - ch * CB);
-                if (bytes == CB) {
+                if constexpr (TYPE == FM_TYPE_Q6_K) {
+                    // 14 aligned 16-byte pieces hold the block: the window starts at
+                    // the block rounded down to 16 bytes and the block ends at most
+                    // 14 + 210 = 224 bytes in; a piece is clipped at the matrix end.
+#pragma unroll
+                    for (uint32_t u = 0; u < 14; ++u) {
+                        const uint32_t q = lane + 32u * u, r = q / 14, k = q - r * 14;
+                        const uint8_t *a = src + static_cast<uint64_t>(r) * p.row_bytes;
+                        const uint8_t *piece =
+                            reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(a) & ~uintptr_t(15)) + 16 * k;
+                        const uint64_t left = static_cast<uint64_t>(iss_end - piece);
+                        cp_async16_zfill(dst + r * L::PITCH + 16 * k, piece, left < 16 ? static_cast<uint32_t>(left) : 16u);
+                    }
+                } else if (bytes == CB) {
                     constexpr uint32_t PPR = CB / G; // pieces per row
 #pragma unroll
                     for (uint32_t u = 0; u < PPR; ++u) {
@@ -490,6 +563,12 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
                 __syncwarp();
                 const uint8_t *row = ring + (j % RS) * L::RAW_SLOT + lane * L::PITCH;
                 const uint32_t steps = min(GG_CHUNK / GG_BK, ksteps - ch * (GG_CHUNK / GG_BK));
+                // Q6_K: the block's byte offset inside its 16-byte aligned window
+                // (slot bases and matrix offsets are 16-byte aligned)
+                const uint32_t win_off =
+                    TYPE == FM_TYPE_Q6_K ? static_cast<uint32_t>((static_cast<uint64_t>(g.rt * GG_BM + row_in_tile) *
+                                                                      p.row_bytes + static_cast<uint64_t>(ch) * CB) & 15u)
+                                         : 0u;
 #pragma unroll
                 for (uint32_t st = 0; st < GG_CHUNK / GG_BK; ++st) {
                     if (st < steps) {
@@ -498,10 +577,10 @@ __global__ void __launch_bounds__(GG_THREADS, 1)
                         if (!gg_wait(&a_empty[ast], ((gs / SA) & 1u) ^ 1u, abort_flag, p.status)) goto conv_done;
                         tc_fence_after();
                         uint32_t v[32];
-                        if (st == 0) gg_decode<TYPE, 0>(row, v);
-                        else if (st == 1) gg_decode<TYPE, 1>(row, v);
-                        else if (st == 2) gg_decode<TYPE, 2>(row, v);
-                        else gg_decode<TYPE, 3>(row, v);
+                        if (st == 0) gg_decode<TYPE, 0>(row, win_off, v);
+                        else if (st == 1) gg_decode<TYPE, 1>(row, win_off, v);
+                        else if (st == 2) gg_decode<TYPE, 2>(row, win_off, v);
+                        else gg_decode<TYPE, 3>(row, win_off, v);
                         tmem_st32(tmem + lane_addr + L::A_COL0 + ast * L::A_STAGE_COLS + m * 32u, v);
                         tmem_wait_st();
                         tc_fence_before();

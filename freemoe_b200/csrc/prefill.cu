@@ -211,6 +211,8 @@ int launch_gg_inst(const GGemmParams &p, const CUtensorMap &map, uint32_t max_un
 
 // Widest async-copy size that every row start and chunk start is aligned to.
 int copy_granule(uint32_t type_id, uint64_t row_bytes, uint64_t off0, uint64_t off1) {
+    // Q6_K blocks are copied as 16-byte aligned windows: only the matrix starts matter
+    if (type_id == FM_TYPE_Q6_K) return (off0 % 16 == 0 && off1 % 16 == 0) ? 16 : 0;
     const uint64_t chunk = type_id == FM_TYPE_Q8_0 ? 272 : 144;
     const uint64_t tail = row_bytes % chunk;
     for (int g = 16; g >= 4; g /= 2)
@@ -225,6 +227,10 @@ int launch_gg(uint32_t type_id, const GGemmParams &p, const CUtensorMap &map, ui
         if (g != 16) return set_error(FM_STATUS_INVALID_ARGUMENT, "Q4_K rows must be 16-byte aligned");
         return launch_gg_inst<FM_TYPE_Q4_K, NMAT, EPI, 16>(p, map, max_units, s);
     }
+    if (type_id == FM_TYPE_Q6_K) {
+        if (g != 16) return set_error(FM_STATUS_INVALID_ARGUMENT, "Q6_K matrices must start 16-byte aligned");
+        return launch_gg_inst<FM_TYPE_Q6_K, NMAT, EPI, 16>(p, map, max_units, s);
+    }
     switch (g) {
     case 16: return launch_gg_inst<FM_TYPE_Q8_0, NMAT, EPI, 16>(p, map, max_units, s);
     case 8: return launch_gg_inst<FM_TYPE_Q8_0, NMAT, EPI, 8>(p, map, max_units, s);
@@ -234,10 +240,10 @@ int launch_gg(uint32_t type_id, const GGemmParams &p, const CUtensorMap &map, ui
 }
 
 int check_prefill_shape(uint32_t type_id, uint32_t in_dim, uint32_t out_dim, const char *what) {
-    if (type_id != FM_TYPE_Q8_0 && type_id != FM_TYPE_Q4_K)
+    if (type_id != FM_TYPE_Q8_0 && type_id != FM_TYPE_Q4_K && type_id != FM_TYPE_Q6_K)
         return set_error(FM_STATUS_UNSUPPORTED_QUANTISATION,
-                         std::string(what) + ": the grouped GEMM takes Q8_0 or Q4_K weights");
-    const uint32_t kq = type_id == FM_TYPE_Q4_K ? 256 : 64;
+                         std::string(what) + ": the grouped GEMM takes Q8_0, Q4_K or Q6_K weights");
+    const uint32_t kq = type_id == FM_TYPE_Q8_0 ? 64 : 256;
     if (in_dim == 0 || in_dim % kq || out_dim == 0 || out_dim % GG_BM)
         return set_error(FM_STATUS_SHAPE_MISMATCH,
                          std::string(what) + ": the grouped GEMM needs K a multiple of " + std::to_string(kq) +

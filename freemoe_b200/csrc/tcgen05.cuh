@@ -141,4 +141,11 @@ __device__ __forceinline__ void cp_async_g(void *dst, const void *src) {
                      : "memory");
 }
 
+// 16-byte async copy of which only the first `src_bytes` (0..16) are read;
+// the rest of the 16 destination bytes are zero-filled.
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
 } // namespace fmb

@@ -18,7 +18,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle.oracle import TYPE_F32, TYPE_Q4_K, TYPE_Q8_0, bf16_round
+from oracle.oracle import TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0, bf16_round
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
@@ -100,6 +100,47 @@ def test_prefill_small_vs_oracle(cuda, oracle, t, T):
     assert np.array_equal(bits(w.cpu().numpy()), bits(w_o))
     y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, t)
     assert rel_err(y.cpu().numpy(), y_o) < TOL
+
+
+@pytest.mark.parametrize("T", [37, 300])
+def test_prefill_q6_k_vs_oracle(cuda, oracle, T):
+    """Q6_K throughout: 210-byte blocks, rows of 210 (gate/up) and 420 (down)
+    bytes, so no block start is 4-byte aligned in general."""
+    rng = np.random.default_rng(500 + T)
+    E, k, d, ffn, t = 8, 2, 256, 512, TYPE_Q6_K
+    slots = host_experts(oracle, rng, E, d, ffn, t)
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    y = cuda.moe_prefill(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn, gate_type=t)
+    assert cuda.device_status() == 0
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, t)
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
+
+
+def test_prefill_mixed_record(cuda, oracle):
+    """Q4_K gate/up with a Q6_K down projection (the usual Q4_K_M mix), down rows
+    of 1260 bytes; prefill and decode paths both against the oracle."""
+    rng = np.random.default_rng(77)
+    E, k, d, ffn, T = 8, 2, 512, 1536, 300
+    slots = []
+    for _ in range(E):
+        parts = [oracle.quantize(TYPE_Q4_K, rng.normal(0, 0.02, size=ffn * d).astype(np.float32)),
+                 oracle.quantize(TYPE_Q4_K, rng.normal(0, 0.02, size=ffn * d).astype(np.float32)),
+                 oracle.quantize(TYPE_Q6_K, rng.normal(0, 0.02, size=d * ffn).astype(np.float32))]
+        slots.append(np.concatenate(parts))
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, TYPE_Q4_K, TYPE_Q4_K, TYPE_Q6_K)
+    dslots = [dev(s) for s in slots]
+    y = cuda.moe_prefill(dev(x, torch.bfloat16), dev(logits), dslots, top_k=k, ffn=ffn, gate_type=TYPE_Q4_K,
+                         down_type=TYPE_Q6_K)
+    assert cuda.device_status() == 0
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
+    y_dec = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), dslots, top_k=k, ffn=ffn, gate_type=TYPE_Q4_K,
+                           down_type=TYPE_Q6_K)
+    assert rel_err(y_dec.cpu().numpy(), y_o) < TOL
 
 
 @pytest.mark.parametrize("t,big,xs", [(TYPE_Q8_0, 1.0, 1.0), (TYPE_Q4_K, 2000.0, 1e-3)])
