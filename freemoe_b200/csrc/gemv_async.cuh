@@ -215,6 +215,7 @@ __global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
     constexpr int TILE = G::TILE;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[NW][NMAT][TILE][8];
+    __shared__ float s_act[MODE == GEMV_GATE_UP ? TILE : 1][8]; // SwiGLU outputs of a tile (planes epilogue)
     // token tiles before expert e, in the dynamic shared memory after the rings
     uint32_t *s_prefix = reinterpret_cast<uint32_t *>(smem + static_cast<size_t>(NW) * P * G::BYTES);
 
@@ -394,7 +395,29 @@ __global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
                 v[m] = sum;
             }
             const float out = (MODE == GEMV_GATE_UP) ? swiglu_ref(v[0], v[NMAT - 1]) : v[0];
-            p.y[static_cast<uint64_t>(tl.start + col) * p.out_dim + row] = out;
+            if (MODE == GEMV_GATE_UP && p.act_h) {
+                // the down projection's x planes, as xplanes_staged_kernel writes them
+                const uint64_t at = static_cast<uint64_t>(tl.start + col) * p.out_dim + staged_pos(row, p.act_layout);
+                const __half h = __float2half_rn(out);
+                p.act_h[at] = h;
+                p.act_l[at] = __float2half_rn(out - __half2float(h));
+                s_act[MODE == GEMV_GATE_UP ? r : 0][col] = out;
+            } else {
+                p.y[static_cast<uint64_t>(tl.start + col) * p.out_dim + row] = out;
+            }
+        }
+        if (MODE == GEMV_GATE_UP && p.act_h) {
+            // sums over each 32-value sub-block, in ascending order (tile rows are
+            // whole sub-blocks: the fused epilogue needs out_dim % 32 == 0)
+            __syncthreads();
+            for (int t = threadIdx.x; t < 8 * (TILE / 32); t += NW * 32) {
+                const int col = t & 7, sb = t >> 3;
+                if (!tile_ok || static_cast<uint32_t>(col) >= tl.ncol) continue;
+                float sum = 0.0f;
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) sum += s_act[MODE == GEMV_GATE_UP ? 32 * sb + i : 0][col];
+                p.act_s[static_cast<uint64_t>(tl.start + col) * (p.out_dim / 32) + (tl.row0 / 32 + sb)] = sum;
+            }
         }
         __syncthreads();
     }

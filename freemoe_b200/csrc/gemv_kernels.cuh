@@ -32,6 +32,12 @@ struct QGemvParams {
     // output
     float *y;                         // [rows][out_dim]
     int *status;                      // device status word
+    // gate/up of the streamed kernel only: when act_h is set, the SwiGLU output
+    // goes straight into the down projection's x planes (hi, lo fp16 in the
+    // staged order `act_layout`, f32 sums per 32 values) instead of y
+    __half *act_h, *act_l;
+    float *act_s;
+    int act_layout;
 };
 
 // SwiGLU of include/fm/activation.hpp:62-84 (plain form): float(silu(double(g))) * u.

@@ -219,13 +219,23 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     gu.xs = xs;
     gu.y = act;
     gu.status = device_status_word();
+    // both GEMVs streamed: the gate/up epilogue writes the down projection's x
+    // planes directly (same values and order as the separate plane kernel)
+    const bool fused_planes = gu_staged && dn_staged && a->ffn % 32 == 0;
+    if (fused_planes) {
+        gu.act_h = ah;
+        gu.act_l = al;
+        gu.act_s = as;
+        gu.act_layout = xplane_layout(a->down_type);
+    }
     rc = gu_staged ? launch_qgemv_stream<GEMV_GATE_UP>(gu, xplanes, tok_tiles, a->experts, s)
                    : launch_qgemv<GEMV_GATE_UP>(gu, xplanes, tok_tiles, a->experts, s);
     if (rc) return rc;
     mark(4);
 
-    rc = dn_staged ? launch_xplanes_staged(act, FM_X_F32, P, a->ffn, xplane_layout(a->down_type), ah, al, as, s)
-                   : launch_xplanes_for(a->down_type, act, FM_X_F32, P, a->ffn, ah, al, as, s);
+    rc = fused_planes ? FM_STATUS_OK
+         : dn_staged  ? launch_xplanes_staged(act, FM_X_F32, P, a->ffn, xplane_layout(a->down_type), ah, al, as, s)
+                      : launch_xplanes_for(a->down_type, act, FM_X_F32, P, a->ffn, ah, al, as, s);
     if (rc) return rc;
     mark(5);
 
