@@ -417,7 +417,7 @@ def run_ours(args):
                      "down_achieved": (EXPERTS * D_MODEL * row_bytes(type_id, FFN)) / (dn_ms / 1e3) / 1e9},
         "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": ms_e2e},
-        "gpu_launches": 6 * args.steps,  # router, grouping, x planes, gate/up (+ down's x planes), down, combine
+        "gpu_launches": 4 * args.steps,  # router + grouping + x planes, gate/up (+ down's x planes), down, combine
         "clocks": clocks.summary(),
     }
 
@@ -652,7 +652,7 @@ def run_layer(args):
         line["roofline"] = {"bound": "hbm", "kernel": "MoE block (distinct experts' bytes)",
                             "achieved": line["hbm_gbs"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
                             "frac": line["hbm_gbs"] / peak, "traffic": None, "algorithmic_bytes": wbytes}
-        line["gpu_launches"] = 6 * args.steps
+        line["gpu_launches"] = 4 * args.steps
 
     if not args.no_cpu:
         # the reference's CPU code on a bounded sample of the same tokens

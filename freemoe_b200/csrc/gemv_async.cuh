@@ -54,6 +54,69 @@ __host__ __device__ __forceinline__ uint32_t staged_pos(uint32_t k, int layout) 
     return base + chunk * 8 + (j & 4u) + xplane_pos(j & 3u);
 }
 
+// One 32-value sub-block s of x row `row`: staged fp16 plane(s) and the sum.
+// Each group of 4 values lands on 4 consecutive positions (xplane_pos order),
+// so the planes are written 8 bytes at a time; x is read 16 bytes at a time
+// when the row is 16-byte aligned.
+template <typename XT>
+__device__ __forceinline__ void xplanes_staged_item(const XT *__restrict__ x, uint32_t row, uint32_t s,
+                                                    uint32_t k_dim, int layout, __half *__restrict__ xh,
+                                                    __half *__restrict__ xl, float *__restrict__ xs) {
+    const uint32_t subs = k_dim / 32;
+    const XT *src = x + static_cast<uint64_t>(row) * k_dim + 32 * s;
+    __half *dh = xh + static_cast<uint64_t>(row) * k_dim;
+    __half *dl = xl ? xl + static_cast<uint64_t>(row) * k_dim : nullptr;
+    float v[32];
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        if constexpr (sizeof(XT) == 2) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 w = __ldg(reinterpret_cast<const uint4 *>(src) + q);
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    v[8 * q + 2 * i] = __uint_as_float(u[i] << 16);
+                    v[8 * q + 2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 w = __ldg(reinterpret_cast<const float4 *>(src) + q);
+                v[4 * q] = w.x;
+                v[4 * q + 1] = w.y;
+                v[4 * q + 2] = w.z;
+                v[4 * q + 3] = w.w;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = load_x<XT>(src + i);
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sum += v[i];
+#pragma unroll
+    for (int g4 = 0; g4 < 8; ++g4) {
+        const uint32_t pos = staged_pos(32 * s + 4 * g4, layout); // the group's first position
+        __half h[4], l[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            h[i] = __float2half_rn(v[4 * g4 + i]);
+            l[i] = __float2half_rn(v[4 * g4 + i] - __half2float(h[i]));
+        }
+        const uint2 hv = make_uint2(__half_as_ushort(h[0]) | (static_cast<uint32_t>(__half_as_ushort(h[2])) << 16),
+                                    __half_as_ushort(h[1]) | (static_cast<uint32_t>(__half_as_ushort(h[3])) << 16));
+        *reinterpret_cast<uint2 *>(dh + pos) = hv;
+        if (dl) {
+            const uint2 lv = make_uint2(__half_as_ushort(l[0]) | (static_cast<uint32_t>(__half_as_ushort(l[2])) << 16),
+                                        __half_as_ushort(l[1]) | (static_cast<uint32_t>(__half_as_ushort(l[3])) << 16));
+            *reinterpret_cast<uint2 *>(dl + pos) = lv;
+        }
+    }
+    xs[static_cast<uint64_t>(row) * subs + s] = sum;
+}
+
 template <typename XT>
 __global__ void xplanes_staged_kernel(const XT *__restrict__ x, uint32_t rows, uint32_t k_dim,
                                       int layout, __half *__restrict__ xh, __half *__restrict__ xl,
@@ -61,22 +124,8 @@ __global__ void xplanes_staged_kernel(const XT *__restrict__ x, uint32_t rows, u
     const uint32_t subs = k_dim / 32;
     const uint64_t id = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
     if (id >= static_cast<uint64_t>(rows) * subs) return;
-    const uint32_t row = static_cast<uint32_t>(id / subs), s = static_cast<uint32_t>(id % subs);
-    const XT *src = x + static_cast<uint64_t>(row) * k_dim;
-    __half *dh = xh + static_cast<uint64_t>(row) * k_dim;
-    __half *dl = xl ? xl + static_cast<uint64_t>(row) * k_dim : nullptr;
-    float sum = 0.0f;
-#pragma unroll 8
-    for (uint32_t i = 0; i < 32; ++i) {
-        const uint32_t k = 32 * s + i;
-        const float v = load_x<XT>(src + k);
-        sum += v;
-        const __half h = __float2half_rn(v);
-        const uint32_t pos = staged_pos(k, layout);
-        dh[pos] = h;
-        if (dl) dl[pos] = __float2half_rn(v - __half2float(h));
-    }
-    xs[static_cast<uint64_t>(row) * subs + s] = sum;
+    xplanes_staged_item(x, static_cast<uint32_t>(id / subs), static_cast<uint32_t>(id % subs), k_dim, layout, xh, xl,
+                        xs);
 }
 
 template <int TYPE, int MT, int NMAT>

@@ -4,15 +4,19 @@
 //   1. router        logits -> ids, weights                (router.cu)
 //   2. grouping      ids -> counts, offsets, pairs, slot_of (router.cu)
 //   3. x planes      x -> fp16 plane(s) + sub-block sums    (gemv_core.cuh)
+//      (1-3 are one CTA-sized launch, moe_front_kernel, for short batches)
 //   4. gate/up       per expert, fused gate and up GEMV with SwiGLU -> act[slot]
-//   5. act planes    act -> fp16 planes + sums
+//   5. act planes    act -> fp16 planes + sums (written by the gate/up epilogue
+//                    when both GEMVs are the streamed kernel)
 //   6. down          per expert, down GEMV -> part[slot]
 //   7. combine       y[t] = sum over r of w[t,r] * part[slot_of(t,r)], in top-k
 //                    order, multiply then add (src/engine.cpp:1770)
 // Each expert's weight rows are read once per 8 of its tokens.
 #include <string>
 
+#include "gemv_async.cuh"
 #include "gemv_kernels.cuh"
+#include "router_core.cuh"
 
 namespace fmb {
 
@@ -40,6 +44,36 @@ int launch_qgemv_stream(const QGemvParams &prm, int planes, uint32_t tok_tiles, 
 namespace {
 
 inline uint64_t a256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+// Steps 1-3 for a short batch in one launch: CTA 0 runs the router (warp w
+// takes tokens w, w + 32, ...) and, once the ids are visible to the CTA, the
+// grouping (the whole CTA); CTAs 1.. write the x planes.  Same device code and
+// results as the three separate kernels, two launches fewer.
+constexpr uint32_t kFrontMaxTokens = 64, kFrontMaxExperts = 64;
+
+template <typename XT>
+__global__ void __launch_bounds__(1024)
+    moe_front_kernel(const float *__restrict__ logits, const XT *__restrict__ x, uint32_t tokens, uint32_t experts,
+                     uint32_t top_k, int normalise, double epsilon, double scale, uint32_t d, int layout,
+                     uint32_t *ids, float *weights, uint32_t *counts, uint32_t *offsets, uint32_t *pairs,
+                     uint32_t *slot_of, __half *xh, __half *xl, float *xs, int *status) {
+    __shared__ double s_ex[32][kFrontMaxExperts];
+    __shared__ float s_pr[32][kFrontMaxExperts];
+    __shared__ uint32_t s_count[kFrontMaxExperts], s_off[kFrontMaxExperts], s_warp_tot[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x > 0) {
+        const uint32_t subs = d / 32;
+        for (uint32_t i = (blockIdx.x - 1) * blockDim.x + threadIdx.x; i < tokens * subs;
+             i += (gridDim.x - 1) * blockDim.x)
+            xplanes_staged_item(x, i / subs, i % subs, d, layout, xh, xl, xs);
+        return;
+    }
+    for (uint32_t t = warp; t < tokens; t += 32)
+        route_token(logits, t, experts, top_k, normalise, epsilon, scale, ids, weights, nullptr, status, s_ex[warp],
+                    s_pr[warp], lane);
+    __syncthreads();
+    group_block(ids, tokens * top_k, experts, counts, offsets, pairs, slot_of, status, s_count, s_off, s_warp_tot);
+}
 
 // Byte layout of the MoE workspace.
 struct MoeLayout {
@@ -183,23 +217,47 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
         }
     };
 
-    mark(0);
-    if ((rc = launch_route_cfg(a->logits, a->tokens, a->experts, a->top_k, a->router, a->normalise, a->epsilon,
-                           a->scale, ids, weights, nullptr, s)))
-        return rc;
-    mark(1);
-    if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
-    mark(2);
     const int xplanes = a->x_dtype == FM_X_F32 ? 2 : 1;
     // Expert slots come from cudaMalloc-class allocations (256-byte aligned);
     // the staged kernels also re-check each slot base on the device.
     const bool gu_staged = staged_shape(a->gate_type, a->d_model) && a->up_offset % 16 == 0;
     const bool dn_staged = staged_shape(a->down_type, a->ffn) && a->down_offset % 16 == 0;
-    rc = gu_staged ? launch_xplanes_staged(a->x, a->x_dtype, a->tokens, a->d_model,
-                                           xplane_layout(a->gate_type), xh, xplanes > 1 ? xl : nullptr, xs, s)
-                   : launch_xplanes_for(a->gate_type, a->x, a->x_dtype, a->tokens, a->d_model, xh,
-                                        xplanes > 1 ? xl : nullptr, xs, s);
-    if (rc) return rc;
+    const fmcuda_router_config *cfg = a->router;
+    const bool plain_router = !cfg || (cfg->gating == FM_GATING_SOFTMAX && !cfg->logit_bias && !cfg->selection_bias &&
+                                       cfg->groups <= 1 && !cfg->epsilon_additive);
+    mark(0);
+    if (plain_router && gu_staged && a->tokens <= kFrontMaxTokens && a->experts <= kFrontMaxExperts) {
+        const int norm = cfg ? cfg->normalise : a->normalise;
+        const double eps = cfg ? cfg->epsilon : a->epsilon, scl = cfg ? cfg->scale : a->scale;
+        const int layout = xplane_layout(a->gate_type);
+        __half *xl_or_null = xplanes > 1 ? xl : nullptr;
+        const unsigned front_grid = 1 + (a->tokens * (a->d_model / 32) + 1023) / 1024;
+        if (a->x_dtype == FM_X_BF16)
+            moe_front_kernel<__nv_bfloat16><<<front_grid, 1024, 0, s>>>(
+                a->logits, static_cast<const __nv_bfloat16 *>(a->x), a->tokens, a->experts, a->top_k, norm, eps, scl,
+                a->d_model, layout, ids, weights, counts, offsets, pairs, slot_of, xh, xl_or_null, xs,
+                device_status_word());
+        else
+            moe_front_kernel<float><<<front_grid, 1024, 0, s>>>(
+                a->logits, static_cast<const float *>(a->x), a->tokens, a->experts, a->top_k, norm, eps, scl,
+                a->d_model, layout, ids, weights, counts, offsets, pairs, slot_of, xh, xl_or_null, xs,
+                device_status_word());
+        if ((rc = check_launch("MoE front launch"))) return rc;
+        mark(1);
+        mark(2);
+    } else {
+        if ((rc = launch_route_cfg(a->logits, a->tokens, a->experts, a->top_k, a->router, a->normalise, a->epsilon,
+                                   a->scale, ids, weights, nullptr, s)))
+            return rc;
+        mark(1);
+        if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
+        mark(2);
+        rc = gu_staged ? launch_xplanes_staged(a->x, a->x_dtype, a->tokens, a->d_model,
+                                               xplane_layout(a->gate_type), xh, xplanes > 1 ? xl : nullptr, xs, s)
+                       : launch_xplanes_for(a->gate_type, a->x, a->x_dtype, a->tokens, a->d_model, xh,
+                                            xplanes > 1 ? xl : nullptr, xs, s);
+        if (rc) return rc;
+    }
     mark(3);
 
     const uint32_t tok_tiles = (a->tokens + 7) / 8; // an expert holds at most `tokens` pairs
