@@ -871,7 +871,7 @@ def run_layer_ep(args):
     logits = torch.from_numpy(lg_np[sl]).cuda()
     ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
                     local_slots=slots, up_offset=gb, down_offset=2 * gb)
-    layer = EPLayer(ops, record_timing=True)
+    layer = EPLayer(ops, record_timing=True, mode=args.ep_mode)
     for _ in range(args.warmup):
         y = layer.forward(x, logits)
     torch.cuda.synchronize()
@@ -923,7 +923,11 @@ def run_layer_ep(args):
                 "vs_baseline": None, "dtype": {8: "q8_0", 12: "q4_k"}[t] + " -> fp16 tensor cores", "data": "synthetic",
                 "config": {"workload": f"{args.config} expert-parallel: {E} experts ({per}/rank) d {d} ffn {ffn} "
                                        f"top-{k}, T={T} bf16 tokens ({tp}/rank), {cfg['logits']} router logits",
-                           "tokens": T, "parallelism": f"ep{world}", "exchange": "NCCL all-to-all (torch.distributed)"},
+                           "tokens": T, "parallelism": f"ep{world}",
+                           "exchange": {"p2p": "peer-memory stores fused into the dispatch and partial-sum kernels "
+                                                "(CUDA IPC mailboxes, no collective in the data path)",
+                                        "rows": "NCCL all-to-all (torch.distributed), one row per token and rank",
+                                        "pairs": "NCCL all-to-all (torch.distributed), one row per pair"}[args.ep_mode]},
                 "phase_ms_max_over_ranks": phases,
                 "e2e": {"value": T / (float(ms_e.item()) / 1e3), "unit": "tokens/s",
                         "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4,
@@ -934,6 +938,7 @@ def run_layer_ep(args):
                              "frac": routed / (ms / 1e3) / 1e12 / (peak * world), "traffic": None},
                 "gpu_launches": None, "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
+    layer.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -943,6 +948,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "rows", "pairs"],
+                    help="expert-parallel exchange of the layer configurations under torchrun")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))
     ap.add_argument("--tokens", type=int, default=8)

@@ -172,6 +172,18 @@ SIGNATURES = [
     ("fmcuda_moe_experts_partial", C.c_int, [_P, _P, _P, _U32, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32, _U32,
                                              _U32, _P, _P, _U64, _P]),
     ("fmcuda_ep_combine_rows", C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P]),
+    ("fmcuda_ep_mailbox_bytes", _U64, [_U32, _U32, _U32, _U32]),
+    ("fmcuda_ep_mailbox_alloc", C.c_int, [_U64, C.POINTER(C.c_void_p), _P]),
+    ("fmcuda_ep_mailbox_open", C.c_int, [_P, C.POINTER(C.c_void_p)]),
+    ("fmcuda_ep_mailbox_close", C.c_int, [_P]),
+    ("fmcuda_ep_mailbox_free", C.c_int, [_P]),
+    ("fmcuda_ep_p2p_dispatch_scratch_bytes", _U64, [_U32, _U32]),
+    ("fmcuda_ep_p2p_dispatch", C.c_int, [_P, _P, _U32, _U32, _U32, _U32, _U32, _P, C.c_int32, _U32, _P, _P, _U32,
+                                         _U32, _P, _P, _U32, _P]),
+    ("fmcuda_ep_p2p_experts_workspace_bytes", _U64, [_U32, _U32, _U32, _U32, _U32]),
+    ("fmcuda_ep_p2p_experts", C.c_int, [_P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32,
+                                        _U32, _U32, _P, _U64, _U32, _P]),
+    ("fmcuda_ep_p2p_combine", C.c_int, [_P, _U32, _U32, _U32, _U32, _U32, _P, _U32, _U32, _P, _U32, _P]),
     ("fmcuda_synth_weights", C.c_int, [_U32, _P, _U64, _U32, _U64, _F, _P]),
 ]
 

@@ -183,9 +183,14 @@ PartialLayout partial_layout(uint32_t rows, uint32_t top_k, uint32_t experts, ui
     return L;
 }
 
-__global__ void ep_meta_keys_kernel(const int32_t *__restrict__ meta_e, uint64_t n, uint32_t *__restrict__ keys) {
+// key of pair slot i = local expert, or absent for other ranks' slots and for
+// rows at or past *rows_dev (when the row count lives on the device)
+__global__ void ep_meta_keys_kernel(const int32_t *__restrict__ meta_e, uint64_t n, uint32_t top_k,
+                                    const uint32_t *__restrict__ rows_dev, uint32_t *__restrict__ keys) {
     const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
-    if (i < n) keys[i] = meta_e[i] >= 0 ? static_cast<uint32_t>(meta_e[i]) : 0xFFFFFFFFu;
+    if (i >= n) return;
+    const bool live = !rows_dev || i / top_k < *rows_dev;
+    keys[i] = live && meta_e[i] >= 0 ? static_cast<uint32_t>(meta_e[i]) : 0xFFFFFFFFu;
 }
 
 // xg[g] = x[pairs[g] / k]
@@ -251,14 +256,16 @@ extern "C" uint64_t fmcuda_moe_experts_partial_workspace_bytes(uint32_t rows, ui
     return partial_layout(rows, top_k, experts, d_model, ffn).total;
 }
 
-extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_expert, const float *meta_weight,
-                                          uint32_t rows, uint32_t top_k, uint32_t experts,
-                                          const void *const *expert_slots, uint64_t up_offset,
-                                          uint64_t down_offset, uint32_t gate_type, uint32_t up_type,
-                                          uint32_t down_type, uint32_t d_model, uint32_t ffn, float *partial,
-                                          void *workspace, uint64_t workspace_bytes, void *stream) {
+namespace fmb {
+// The expert GEMMs of fmcuda_moe_experts_partial up to the per-pair outputs
+// out_pairs[row * k + r] (rows = capacity when rows_dev holds the live count).
+int experts_partial_run(const void *x, const int32_t *meta_expert, const float *meta_weight, uint32_t rows,
+                        const uint32_t *rows_dev, uint32_t top_k, uint32_t experts, const void *const *expert_slots,
+                        uint64_t up_offset, uint64_t down_offset, uint32_t gate_type, uint32_t up_type,
+                        uint32_t down_type, uint32_t d_model, uint32_t ffn, float *out_pairs, void *workspace,
+                        uint64_t workspace_bytes, cudaStream_t s) {
     if (rows == 0) return FM_STATUS_OK;
-    if (!x || !meta_expert || !meta_weight || !expert_slots || !partial)
+    if (!x || !meta_expert || !meta_weight || !expert_slots || !out_pairs)
         return set_error(FM_STATUS_INVALID_ARGUMENT, "null expert-compute pointer");
     if (experts == 0 || experts > 1024) return set_error(FM_STATUS_INVALID_ARGUMENT, "1..1024 local experts");
     if (gate_type != up_type)
@@ -275,10 +282,9 @@ extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_exp
     if (n64 > 0x7FFFFFFFull) return set_error(FM_STATUS_INVALID_ARGUMENT, "too many pairs");
     const uint32_t n = static_cast<uint32_t>(n64);
     const PartialLayout L = partial_layout(rows, top_k, experts, d_model, ffn);
-    if (!workspace || workspace_bytes < L.total)
+    if (!workspace || workspace_bytes < L.out)
         return set_error(FM_STATUS_INVALID_ARGUMENT,
-                         "expert workspace too small: need " + std::to_string(L.total) + " bytes");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
+                         "expert workspace too small: need " + std::to_string(L.out) + " bytes");
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     uint32_t *keys = reinterpret_cast<uint32_t *>(ws + L.keys);
     uint32_t *counts = reinterpret_cast<uint32_t *>(ws + L.counts);
@@ -286,8 +292,8 @@ extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_exp
     uint32_t *pairs = reinterpret_cast<uint32_t *>(ws + L.pairs);
     __half *xg = reinterpret_cast<__half *>(ws + L.xg);
     __half *act = reinterpret_cast<__half *>(ws + L.act);
-    float *out = reinterpret_cast<float *>(ws + L.out);
-    ep_meta_keys_kernel<<<static_cast<unsigned>((n64 + 255) / 256), 256, 0, s>>>(meta_expert, n64, keys);
+    ep_meta_keys_kernel<<<static_cast<unsigned>((n64 + 255) / 256), 256, 0, s>>>(meta_expert, n64, top_k, rows_dev,
+                                                                                 keys);
     int rc = check_launch("expert keys launch");
     if (rc) return rc;
     if ((rc = launch_group_large(keys, n, experts, counts, offsets, pairs, nullptr,
@@ -297,12 +303,37 @@ extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_exp
                                               d_model, xg);
     if ((rc = check_launch("expert gather launch"))) return rc;
     // GEMM2 writes the output of grouped pair g to slot pairs[g] = row * k + r
-    if ((rc = run_expert_gemms(experts, expert_slots, up_offset, down_offset, gate_type, down_type, d_model, ffn,
-                               counts, offsets, n, xg, act, out, pairs, nullptr, s)))
-        return rc;
+    return run_expert_gemms(experts, expert_slots, up_offset, down_offset, gate_type, down_type, d_model, ffn, counts,
+                            offsets, n, xg, act, out_pairs, pairs, nullptr, s);
+}
+
+// workspace of experts_partial_run: everything but the per-pair outputs
+uint64_t experts_pairs_workspace_bytes(uint32_t rows, uint32_t top_k, uint32_t experts, uint32_t d, uint32_t ffn) {
+    return partial_layout(rows, top_k, experts, d, ffn).out;
+}
+} // namespace fmb
+
+extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_expert, const float *meta_weight,
+                                          uint32_t rows, uint32_t top_k, uint32_t experts,
+                                          const void *const *expert_slots, uint64_t up_offset,
+                                          uint64_t down_offset, uint32_t gate_type, uint32_t up_type,
+                                          uint32_t down_type, uint32_t d_model, uint32_t ffn, float *partial,
+                                          void *workspace, uint64_t workspace_bytes, void *stream) {
+    if (rows == 0) return FM_STATUS_OK;
+    if (!partial) return set_error(FM_STATUS_INVALID_ARGUMENT, "null expert-compute pointer");
+    const PartialLayout L = partial_layout(rows, top_k, experts, d_model, ffn);
+    if (!workspace || workspace_bytes < L.total)
+        return set_error(FM_STATUS_INVALID_ARGUMENT,
+                         "expert workspace too small: need " + std::to_string(L.total) + " bytes");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float *out = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + L.out);
+    int rc = experts_partial_run(x, meta_expert, meta_weight, rows, nullptr, top_k, experts, expert_slots, up_offset,
+                                 down_offset, gate_type, up_type, down_type, d_model, ffn, out, workspace,
+                                 workspace_bytes, s);
+    if (rc) return rc;
     const uint64_t m = static_cast<uint64_t>(rows) * d_model;
     ep_partial_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, s>>>(out, meta_expert, meta_weight, rows,
-                                                                             top_k, d_model, partial);
+                                                                              top_k, d_model, partial);
     return check_launch("expert partial-sum launch");
 }
 

@@ -19,9 +19,14 @@ and gets back one f32 partial sum per (token, rank) (fmcuda_moe_experts_partial,
 fmcuda_ep_combine_rows): less traffic, the same terms summed grouped by rank.
 
 The exchange uses ``torch.distributed.all_to_all_single`` on the group (NCCL
-over NVLink on GPUs).  The arithmetic is pluggable (``ops``): :class:`DeviceOps`
-calls the sm_100a library; the CPU tests plug in a host implementation to check
-the exchange and ordering logic with gloo ranks.
+over NVLink on GPUs).  ``mode="p2p"`` (one node, CUDA devices) does the
+de-duplicated exchange with no collective call in the data path: every rank
+owns a mailbox shared over CUDA IPC, the dispatch kernel writes the token rows
+straight into the destinations' mailboxes and the partial-sum kernel writes its
+results straight back (fmcuda_ep_p2p_*); the result is that of ``mode="rows"``
+bit for bit.  The arithmetic is pluggable (``ops``): :class:`DeviceOps` calls
+the sm_100a library; the CPU tests plug in a host implementation to check the
+exchange and ordering logic with gloo ranks.
 """
 from __future__ import annotations
 
@@ -162,6 +167,72 @@ class DeviceOps:
                                                    tokens, world, self.d, C.c_void_p(y.data_ptr()), self._stream()))
         return y
 
+    # ---- exchange over peer memory (mode "p2p") ------------------------------
+
+    def p2p_setup(self, world: int, rank: int, capacity: int, group=None, timeout_ms: int = 0):
+        """Allocates this rank's mailbox, swaps IPC handles with the group and
+        opens the peers' mailboxes (collective over `group`)."""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.world, self.rank, self.capacity, self.timeout_ms = world, rank, capacity, timeout_ms
+        nbytes = self.lib.fmcuda_ep_mailbox_bytes(world, capacity, self.k, self.d)
+        mine, handle = C.c_void_p(), (C.c_ubyte * 64)()
+        self.check(self.lib.fmcuda_ep_mailbox_alloc(nbytes, C.byref(mine), handle))
+        self.mailbox = mine.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened, ptrs = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                ptrs.append(self.mailbox)
+                continue
+            buf, p = (C.c_ubyte * 64).from_buffer_copy(h), C.c_void_p()
+            self.check(self.lib.fmcuda_ep_mailbox_open(buf, C.byref(p)))
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        dist.barrier(group=group)  # every mailbox is open before any rank writes
+
+    def p2p_close(self, group=None):
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # nobody writes into a mailbox that is going away
+        for p in getattr(self, "opened", []):
+            self.lib.fmcuda_ep_mailbox_close(C.c_void_p(p))
+        if getattr(self, "mailbox", None):
+            self.lib.fmcuda_ep_mailbox_free(C.c_void_p(self.mailbox))
+        self.opened, self.mailbox = [], None
+
+    def p2p_dispatch(self, ids, w, x, epoch: int) -> torch.Tensor:
+        T, k = ids.shape
+        dev, world = ids.device, self.world
+        row_of = torch.empty(max(T * world, 1), dtype=torch.int32, device=dev)
+        scratch = self._buf("p2p_dispatch", self.lib.fmcuda_ep_p2p_dispatch_scratch_bytes(T, world), dev)
+        xdt = self.X_BF16 if x.dtype == torch.bfloat16 else self.X_F32
+        P = C.c_void_p
+        self.check(self.lib.fmcuda_ep_p2p_dispatch(
+            P(ids.data_ptr()), P(w.data_ptr()), T, k, self.E // world, world, self.rank, P(x.data_ptr()), xdt, self.d,
+            P(self.mailbox), P(self.peers.data_ptr()), self.capacity, epoch, P(row_of.data_ptr()), P(scratch.data_ptr()),
+            self.timeout_ms, self._stream()))
+        return row_of
+
+    def p2p_experts(self, epoch: int):
+        dev = self.peers.device
+        per_rank = len(self.slots)
+        ws = self._buf("p2p_experts", self.lib.fmcuda_ep_p2p_experts_workspace_bytes(
+            self.capacity, self.k, per_rank, self.d, self.ffn), dev)
+        g, u, dn = self.types
+        P = C.c_void_p
+        self.check(self.lib.fmcuda_ep_p2p_experts(
+            P(self.mailbox), P(self.peers.data_ptr()), self.world, self.rank, self.capacity, epoch, self.k, per_rank,
+            P(self.table.data_ptr()), self.up_offset, self.down_offset, g, u, dn, self.d, self.ffn, P(ws.data_ptr()),
+            ws.numel(), self.timeout_ms, self._stream()))
+
+    def p2p_combine(self, row_of, tokens: int, epoch: int) -> torch.Tensor:
+        y = torch.empty(tokens, self.d, dtype=torch.float32, device=row_of.device)
+        self.check(self.lib.fmcuda_ep_p2p_combine(
+            C.c_void_p(self.mailbox), self.world, self.rank, self.capacity, epoch, self.k, C.c_void_p(row_of.data_ptr()),
+            tokens, self.d, C.c_void_p(y.data_ptr()), self.timeout_ms, self._stream()))
+        return y
+
     def combine(self, back: torch.Tensor, w: torch.Tensor, slot_of: torch.Tensor) -> torch.Tensor:
         T = w.shape[0]
         y = torch.empty(T, self.d, dtype=torch.float32, device=w.device)
@@ -176,8 +247,9 @@ class EPLayer:
 
     PHASES = ("route", "dispatch", "counts", "rows_out", "experts", "rows_back", "combine")
 
-    def __init__(self, ops, group=None, record_timing: bool = False, mode: str = "rows"):
-        if mode not in ("rows", "pairs"):
+    def __init__(self, ops, group=None, record_timing: bool = False, mode: str = "rows", capacity: int = 0,
+                 timeout_ms: int = 0):
+        if mode not in ("rows", "pairs", "p2p"):
             raise ValueError(f"unknown exchange mode {mode!r}")
         self.ops, self.group, self.mode = ops, group, mode
         self.record_timing = record_timing and torch.cuda.is_available()
@@ -187,6 +259,38 @@ class EPLayer:
         if ops.E % self.world:
             raise ValueError(f"{ops.E} experts do not shard evenly over {self.world} ranks")
         self.timing = {}
+        # mode "p2p": mailboxes are set up on the first call (capacity = the
+        # largest tokens per rank of that call x world unless given)
+        self.capacity, self.timeout_ms, self.epoch = capacity, timeout_ms, 0
+
+    def close(self):
+        """Releases the peer mailboxes (mode "p2p"); collective over the group."""
+        if self.mode == "p2p" and self.epoch:
+            self.ops.p2p_close(self.group)
+            self.epoch = 0
+
+    def _forward_p2p(self, x, logits):
+        ops = self.ops
+        if self.epoch == 0:
+            if not self.capacity:
+                t = torch.tensor([x.shape[0]], dtype=torch.int64, device=x.device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+                self.capacity = int(t.item()) * self.world
+            ops.p2p_setup(self.world, self.rank, self.capacity, self.group, self.timeout_ms)
+        self.epoch += 1
+        self._mark()
+        ids, w = ops.route(logits)
+        self._mark()
+        row_of = ops.p2p_dispatch(ids, w, x, self.epoch)
+        self._mark()
+        self._mark()  # counts: inside the dispatch kernels
+        self._mark()  # rows out: written by the dispatch kernel
+        ops.p2p_experts(self.epoch)
+        self._mark()  # the partial sums go back from the experts call
+        self._mark()
+        y = ops.p2p_combine(row_of, x.shape[0], self.epoch)
+        self._mark()
+        return y
 
     def _mark(self):
         if self.record_timing:
@@ -216,6 +320,8 @@ class EPLayer:
         dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits, group=self.group)
 
     def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        if self.mode == "p2p":
+            return self._forward_p2p(x, logits)
         ops = self.ops
         self._mark()
         ids, w = ops.route(logits)

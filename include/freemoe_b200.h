@@ -374,6 +374,48 @@ int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_expert, const 
 int fmcuda_ep_combine_rows(const float *back, const uint32_t *row_of, uint32_t tokens, uint32_t world,
                            uint32_t d_model, float *y, void *stream);
 
+/* ============ expert parallelism over peer memory (one node) ============ *
+ * The same de-duplicated exchange with no collective library call and no host
+ * read of the split sizes: each rank owns a mailbox (device memory shared with
+ * the other processes of the node by CUDA IPC); the dispatch kernel writes
+ * every token row straight into its destination's mailbox over NVLink, and
+ * the kernel that sums a received row's expert outputs writes the partial sum
+ * straight back into the source's mailbox.  Per layer call and rank:
+ *   fmcuda_ep_p2p_dispatch   route already done: group this rank's tokens by
+ *                            destination, publish the counts, send the rows
+ *   fmcuda_ep_p2p_experts    wait for the rows, run the local experts, return
+ *                            one f32 partial sum per received row
+ *   fmcuda_ep_p2p_combine    wait for the partial sums, y[t] = their sum over
+ *                            ranks (ascending): the result of mode "rows"
+ * `epoch` numbers the calls 1, 2, ... (the same on every rank).  `capacity`
+ * (the same on every rank) bounds the rows a mailbox receives: at least the
+ * largest tokens-per-rank times world.  `peers` is a device array of the
+ * world mailbox addresses as this process sees them (its own included);
+ * `mailbox` is this rank's own.  Waits give up after `timeout_ms` (0 = 2000)
+ * with FENCE_TIMEOUT in the device status word; a row that would land past a
+ * mailbox's capacity is dropped with INVALID_ARGUMENT there. */
+uint64_t fmcuda_ep_mailbox_bytes(uint32_t world, uint32_t capacity, uint32_t top_k, uint32_t d_model);
+/* allocates (zeroed) and returns the 64-byte cudaIpcMemHandle_t in ipc_handle */
+int fmcuda_ep_mailbox_alloc(uint64_t bytes, void **mailbox, void *ipc_handle);
+int fmcuda_ep_mailbox_open(const void *ipc_handle, void **mailbox);
+int fmcuda_ep_mailbox_close(void *mailbox);
+int fmcuda_ep_mailbox_free(void *mailbox);
+uint64_t fmcuda_ep_p2p_dispatch_scratch_bytes(uint32_t tokens, uint32_t world);
+int fmcuda_ep_p2p_dispatch(const uint32_t *ids, const float *weights, uint32_t tokens, uint32_t top_k,
+                           uint32_t experts_per_rank, uint32_t world, uint32_t rank, const void *x, int32_t x_dtype,
+                           uint32_t d_model, void *mailbox, void *const *peers, uint32_t capacity, uint32_t epoch,
+                           uint32_t *row_of, void *scratch, uint32_t timeout_ms, void *stream);
+uint64_t fmcuda_ep_p2p_experts_workspace_bytes(uint32_t capacity, uint32_t top_k, uint32_t experts,
+                                               uint32_t d_model, uint32_t ffn);
+int fmcuda_ep_p2p_experts(void *mailbox, void *const *peers, uint32_t world, uint32_t rank, uint32_t capacity,
+                          uint32_t epoch, uint32_t top_k, uint32_t experts, const void *const *expert_slots,
+                          uint64_t up_offset, uint64_t down_offset, uint32_t gate_type, uint32_t up_type,
+                          uint32_t down_type, uint32_t d_model, uint32_t ffn, void *workspace,
+                          uint64_t workspace_bytes, uint32_t timeout_ms, void *stream);
+int fmcuda_ep_p2p_combine(void *mailbox, uint32_t world, uint32_t rank, uint32_t capacity, uint32_t epoch,
+                          uint32_t top_k, const uint32_t *row_of, uint32_t tokens, uint32_t d_model, float *y,
+                          uint32_t timeout_ms, void *stream);
+
 /* Size of the scratch built into the library for fmcuda_moe_block_noalloc. */
 #define FM_MOE_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 

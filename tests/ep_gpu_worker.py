@@ -4,7 +4,8 @@ and token batch from seeds, keeps its expert shard and its token shard, runs
 EPLayer, and rank 0 compares the gathered output with fmcuda_moe_prefill over
 all experts on one GPU: identical bits in the per-pair exchange ("pairs"); in
 the de-duplicated exchange ("rows") the terms are summed grouped by rank, so
-the bar is 1e-5 of max |y|."""
+the bar is 1e-5 of max |y|; the peer-memory exchange ("p2p") must equal "rows"
+bit for bit on three successive calls."""
 from __future__ import annotations
 
 import datetime
@@ -41,8 +42,20 @@ def main():
     per, tp = E // world, T // world
     ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
                     local_slots=slots[rank * per:(rank + 1) * per], up_offset=gb, down_offset=2 * gb)
-    layer = EPLayer(ops, mode=mode)
-    y = layer.forward(x[rank * tp:(rank + 1) * tp].contiguous(), logits[rank * tp:(rank + 1) * tp].contiguous())
+    xs, ls = x[rank * tp:(rank + 1) * tp].contiguous(), logits[rank * tp:(rank + 1) * tp].contiguous()
+    if mode == "p2p":
+        # the peer-memory exchange must reproduce mode "rows" bit for bit, call after call
+        y_rows = EPLayer(ops, mode="rows").forward(xs, ls)
+        layer = EPLayer(ops, mode="p2p")
+        for call in range(3):
+            y = layer.forward(xs, ls)
+            torch.cuda.synchronize()
+            assert hotpath.device_status() == 0
+            assert torch.equal(y.view(torch.int32), y_rows.view(torch.int32)), f"call {call} differs from mode rows"
+        layer.close()
+    else:
+        layer = EPLayer(ops, mode=mode)
+        y = layer.forward(xs, ls)
     torch.cuda.synchronize()
     assert hotpath.device_status() == 0
     parts = [torch.empty_like(y) for _ in range(world)]

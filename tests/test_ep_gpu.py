@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("shape", [(16, 4, 256, 256, 512, 12), (128, 8, 4096, 1536, 1024, 12), (64, 6, 2048, 1408, 512, 8)])
-@pytest.mark.parametrize("mode", ["pairs", "rows"])
+@pytest.mark.parametrize("mode", ["pairs", "rows", "p2p"])
 def test_ep_matches_single_gpu(shape, mode):
     n = min(torch.cuda.device_count(), 8)
     n = 2 if shape[0] % n else n
@@ -29,3 +29,54 @@ def test_ep_matches_single_gpu(shape, mode):
                        "NCCL_NVLS_ENABLE": "0"})
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
     assert ("identical=True" if mode == "pairs" else "max_rel=") in p.stdout
+
+
+def test_p2p_exchange_single_rank_and_timeout(cuda):
+    """One rank (world 1) through the peer-memory exchange: mailbox, IPC handle,
+    the count/plan/send/return/combine kernels writing to its own mailbox,
+    three calls in a row, each equal bit for bit to fmcuda_moe_prefill.  Then a
+    wait whose flag nothing raises gives up after its limit with FENCE_TIMEOUT
+    in the device status word (the wait is bounded, the context stays usable)."""
+    import ctypes as C
+    import socket
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200._lib import load
+    from freemoe_b200.ep import DeviceOps, EPLayer
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        E, k, d, ffn, T, t = 16, 4, 256, 256, 64, 12
+        rb = hotpath.row_bytes
+        slots = [torch.cat([hotpath.synth_weights(t, ffn, d, 7000 + 3 * e), hotpath.synth_weights(t, ffn, d, 7001 + 3 * e),
+                            hotpath.synth_weights(t, d, ffn, 7002 + 3 * e)]) for e in range(E)]
+        gb = rb(t, d) * ffn
+        rng = np.random.default_rng(3)
+        x = torch.from_numpy(rng.normal(0, 1, size=(T, d)).astype(np.float32)).cuda().to(torch.bfloat16)
+        logits = torch.from_numpy(rng.uniform(-1, 1, size=(T, E)).astype(np.float32)).cuda()
+        ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
+                        local_slots=slots, up_offset=gb, down_offset=2 * gb)
+        y_one = hotpath.moe_prefill(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
+        layer = EPLayer(ops, mode="p2p")
+        for _ in range(3):
+            y = layer.forward(x, logits)
+            torch.cuda.synchronize()
+            assert cuda.device_status() == 0
+            assert torch.equal(y.view(torch.int32), y_one.view(torch.int32))
+        # a combine for an epoch nobody announced: bounded wait, FENCE_TIMEOUT
+        row_of = torch.zeros(T, dtype=torch.int32, device="cuda")
+        y_bad = torch.empty(T, d, device="cuda")
+        rc = load().fmcuda_ep_p2p_combine(C.c_void_p(ops.mailbox), 1, 0, ops.capacity, layer.epoch + 5, k,
+                                          C.c_void_p(row_of.data_ptr()), T, d, C.c_void_p(y_bad.data_ptr()), 50, None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert cuda.device_status(clear=True) == 22  # FENCE_TIMEOUT
+        layer.close()
+    finally:
+        dist.destroy_process_group()
