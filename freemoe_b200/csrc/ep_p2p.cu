@@ -173,10 +173,21 @@ __global__ void p2p_pack_send_kernel(const XT *__restrict__ x, const uint32_t *_
         uint8_t *peer = peers[dest];
         const XT *src = x + static_cast<uint64_t>(t) * d;
         uint4 *dst = reinterpret_cast<uint4 *>(at<__half>(peer, L.recv_x) + static_cast<uint64_t>(pos) * d);
+        const bool vec = sizeof(XT) == 2 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
         for (uint32_t c = threadIdx.x; c < d / 8; c += blockDim.x) {
             __align__(16) __half h[8];
+            if (vec) { // eight bf16 in one 16-byte load
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src) + c);
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) h[i] = __float2half_rn(load_x(src + 8 * c + i));
+                for (int i = 0; i < 4; ++i) {
+                    h[2 * i] = __float2half_rn(__uint_as_float(u[i] << 16));
+                    h[2 * i + 1] = __float2half_rn(__uint_as_float(u[i] & 0xFFFF0000u));
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) h[i] = __float2half_rn(load_x(src + 8 * c + i));
+            }
             dst[c] = *reinterpret_cast<const uint4 *>(h);
         }
         int32_t *me = at<int32_t>(peer, L.recv_e) + static_cast<uint64_t>(pos) * top_k;

@@ -431,27 +431,53 @@ __global__ void __launch_bounds__(NW * 32, FMB_GEMV_MINB)
                 s_red[warp][m][16 * mt + g + 8][2 * c + 1] = tot[m][mt][3];
             }
         __syncthreads();
-        for (int idx = threadIdx.x; idx < TILE * 8; idx += NW * 32) {
-            const int r = idx >> 3, col = idx & 7;
-            const uint32_t row = tl.row0 + r;
-            if (!tile_ok || static_cast<uint32_t>(col) >= tl.ncol || row >= p.out_dim) continue;
-            float v[NMAT];
+        if (MODE == GEMV_GATE_UP && p.act_h) {
+            // The down projection's x planes, as xplanes_staged_kernel writes them:
+            // four consecutive rows of one column land on four consecutive staged
+            // positions in (0, 2, 1, 3) order, one 8-byte store per plane.
+            for (int idx = threadIdx.x; idx < (TILE / 4) * 8; idx += NW * 32) {
+                const int g4 = idx >> 3, col = idx & 7;
+                if (!tile_ok || static_cast<uint32_t>(col) >= tl.ncol) continue;
+                __half h[4], l[4];
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                float sum = 0.0f;
+                for (int i = 0; i < 4; ++i) {
+                    const int r = 4 * g4 + i;
+                    float v[NMAT];
 #pragma unroll
-                for (int w = 0; w < NW; ++w) sum += s_red[w][m][r][col];
-                v[m] = sum;
+                    for (int m = 0; m < NMAT; ++m) {
+                        float sum = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < NW; ++w) sum += s_red[w][m][r][col];
+                        v[m] = sum;
+                    }
+                    const float out = swiglu_ref(v[0], v[NMAT - 1]);
+                    h[i] = __float2half_rn(out);
+                    l[i] = __float2half_rn(out - __half2float(h[i]));
+                    s_act[MODE == GEMV_GATE_UP ? r : 0][col] = out;
+                }
+                const uint64_t at =
+                    static_cast<uint64_t>(tl.start + col) * p.out_dim + staged_pos(tl.row0 + 4 * g4, p.act_layout);
+                *reinterpret_cast<uint2 *>(p.act_h + at) =
+                    make_uint2(__half_as_ushort(h[0]) | (static_cast<uint32_t>(__half_as_ushort(h[2])) << 16),
+                               __half_as_ushort(h[1]) | (static_cast<uint32_t>(__half_as_ushort(h[3])) << 16));
+                *reinterpret_cast<uint2 *>(p.act_l + at) =
+                    make_uint2(__half_as_ushort(l[0]) | (static_cast<uint32_t>(__half_as_ushort(l[2])) << 16),
+                               __half_as_ushort(l[1]) | (static_cast<uint32_t>(__half_as_ushort(l[3])) << 16));
             }
-            const float out = (MODE == GEMV_GATE_UP) ? swiglu_ref(v[0], v[NMAT - 1]) : v[0];
-            if (MODE == GEMV_GATE_UP && p.act_h) {
-                // the down projection's x planes, as xplanes_staged_kernel writes them
-                const uint64_t at = static_cast<uint64_t>(tl.start + col) * p.out_dim + staged_pos(row, p.act_layout);
-                const __half h = __float2half_rn(out);
-                p.act_h[at] = h;
-                p.act_l[at] = __float2half_rn(out - __half2float(h));
-                s_act[MODE == GEMV_GATE_UP ? r : 0][col] = out;
-            } else {
+        } else {
+            for (int idx = threadIdx.x; idx < TILE * 8; idx += NW * 32) {
+                const int r = idx >> 3, col = idx & 7;
+                const uint32_t row = tl.row0 + r;
+                if (!tile_ok || static_cast<uint32_t>(col) >= tl.ncol || row >= p.out_dim) continue;
+                float v[NMAT];
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    float sum = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) sum += s_red[w][m][r][col];
+                    v[m] = sum;
+                }
+                const float out = (MODE == GEMV_GATE_UP) ? swiglu_ref(v[0], v[NMAT - 1]) : v[0];
                 p.y[static_cast<uint64_t>(tl.start + col) * p.out_dim + row] = out;
             }
         }
