@@ -115,6 +115,23 @@ class SharedExpert(C.Structure):
     ]
 
 
+class Extent(C.Structure):
+    _fields_ = [("offset", C.c_uint64), ("size", C.c_uint64)]
+
+
+class FileIdentity(C.Structure):
+    _fields_ = [("size", C.c_uint64), ("dev", C.c_uint64), ("ino", C.c_uint64), ("mtime_ns", C.c_int64),
+                ("ctime_ns", C.c_int64), ("content_probe", C.c_uint64)]
+
+
+class RecordLoadStats(C.Structure):
+    _fields_ = [("payload_bytes", C.c_uint64), ("physical_bytes", C.c_uint64), ("read_requests", C.c_uint64),
+                ("coalesced_requests", C.c_uint64), ("direct_fallbacks", C.c_uint64), ("checksum", C.c_uint64),
+                ("elapsed_ms", C.c_double)]
+
+
+READER_BUFFERED, READER_DIRECT = 1, 3  # fm::ReaderMode ordinals
+
 MOE_STAGES = ("router", "grouping", "x_planes", "gate_up", "act_planes", "down", "combine")
 # the prefill path's stages under the same eight events (stage 5 is empty there)
 PREFILL_STAGES = ("router", "grouping", "gather", "gate_up", "none", "down", "combine")
@@ -184,6 +201,16 @@ SIGNATURES = [
     ("fmcuda_ep_p2p_experts", C.c_int, [_P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32,
                                         _U32, _U32, _P, _U64, _U32, _P]),
     ("fmcuda_ep_p2p_combine", C.c_int, [_P, _U32, _U32, _U32, _U32, _U32, _P, _U32, _U32, _P, _U32, _P]),
+    ("fmcuda_fnv1a64_workspace_bytes", _U64, [_U64]),
+    ("fmcuda_fnv1a64", C.c_int, [_P, _U64, _P, _P, _U64, _P]),
+    ("fmcuda_file_identity_get", C.c_int, [C.c_char_p, C.POINTER(FileIdentity)]),
+    ("fmcuda_coalesce_extents", C.c_int, [C.POINTER(Extent), _U32, _U64, _P, _P, _P, C.POINTER(C.c_uint32)]),
+    ("fmcuda_record_loader_create", C.c_int, [C.c_char_p, C.c_int, _U64, _U64, _U32, C.c_int,
+                                              C.POINTER(FileIdentity), C.POINTER(C.c_void_p)]),
+    ("fmcuda_record_loader_destroy", C.c_int, [_P]),
+    ("fmcuda_record_load_workspace_bytes", _U64, [_U64]),
+    ("fmcuda_record_load", C.c_int, [_P, C.POINTER(Extent), _U32, _P, _U64, C.c_int, _U64, _P, _U64, _P, _U32,
+                                     C.POINTER(RecordLoadStats)]),
     ("fmcuda_synth_weights", C.c_int, [_U32, _P, _U64, _U32, _U64, _F, _P]),
 ]
 

@@ -27,8 +27,12 @@ enum {
     FM_STATUS_OK = 0,
     FM_STATUS_UNSUPPORTED_QUANTISATION = 3,
     FM_STATUS_SHAPE_MISMATCH = 8,
+    FM_STATUS_SOURCE_CHANGED = 10,
+    FM_STATUS_IO_ERROR = 11,
+    FM_STATUS_SHORT_READ = 12,
     FM_STATUS_ALLOCATION_FAILED = 14,
     FM_STATUS_INVALID_EXPERT_ID = 16,
+    FM_STATUS_EXPERT_CHECKSUM_MISMATCH = 17,
     FM_STATUS_EXPERT_EXECUTION_MISMATCH = 18,
     FM_STATUS_TRANSFER_FAILED = 21,
     FM_STATUS_FENCE_TIMEOUT = 22,
@@ -434,6 +438,98 @@ int fmcuda_ep_p2p_combine(void *mailbox, uint32_t world, uint32_t rank, uint32_t
  * overwrites it, so calls that overlap on the GPU (other streams, other host
  * threads on the same device) race: keep them ordered on one stream. */
 int fmcuda_moe_block_noalloc(const fmcuda_moe_args *args, void *stream);
+
+/* ==================== cold -> warm expert loads (record_loader.cu) ==================== */
+
+/* FNV-1a 64 of `bytes` device bytes at `data` -- the reference's expert
+ * checksum fm::fnv1a64 (include/fm/common.hpp:73-81), bit for bit -- computed
+ * in parallel on the device and written to the device word *out (8-byte
+ * aligned) on `stream`.  `workspace` holds
+ * fmcuda_fnv1a64_workspace_bytes(bytes) device bytes.  Replaces the host-side
+ * fnv1a64 of a slot read-back (src/residency.cpp:700-720). */
+uint64_t fmcuda_fnv1a64_workspace_bytes(uint64_t bytes);
+int fmcuda_fnv1a64(const void *data, uint64_t bytes, uint64_t *out, void *workspace,
+                   uint64_t workspace_bytes, void *stream);
+
+/* fm::Extent (include/fm/io.hpp:24-27): one byte range of the model file. */
+typedef struct fmcuda_extent {
+    uint64_t offset;
+    uint64_t size;
+} fmcuda_extent;
+
+/* fm::FileIdentity (include/fm/common.hpp:144-160): stat fields plus a sparse
+ * FNV-1a content probe over the first, middle and last 64 bytes. */
+typedef struct fmcuda_file_identity {
+    uint64_t size;
+    uint64_t dev;
+    uint64_t ino;
+    int64_t mtime_ns;
+    int64_t ctime_ns;
+    uint64_t content_probe;
+} fmcuda_file_identity;
+int fmcuda_file_identity_get(const char *path, fmcuda_file_identity *id);
+
+/* coalesce_extents (src/io.cpp:46-78): extents sorted by (offset, size) merge
+ * into one read when they start at most `max_gap` bytes past the group's end.
+ * Writes *n_groups and, when the arrays are given, each group's
+ * [offset, end) and the group of every extent.  Host only; a zero-sized or
+ * overflowing extent is INVALID_ARGUMENT. */
+int fmcuda_coalesce_extents(const fmcuda_extent *extents, uint32_t n, uint64_t max_gap,
+                            uint64_t *group_offset, uint64_t *group_end, uint32_t *group_of,
+                            uint32_t *n_groups);
+
+/* fm::ReaderMode ordinals (include/fm/io.hpp:19): the loader reads with
+ * pread (Buffered) or O_DIRECT aligned spans (Direct). */
+enum { FM_READER_BUFFERED = 1, FM_READER_DIRECT = 3 };
+
+typedef struct fmcuda_record_loader fmcuda_record_loader;
+
+/* Opens `path` for expert loads: a ring of `ring_depth` pinned chunks of
+ * `chunk_bytes` (rounded up to the direct-I/O alignment), the reader mode, the
+ * coalescing gap and force_direct_fallback of fm::SchedulerConfig
+ * (include/fm/io.hpp:100-107).  `expected` is the identity the manifest was
+ * built against (NULL: the file as it is now); every load verifies it first
+ * and fails SOURCE_CHANGED (src/io.cpp:262-278) when the file differs.
+ * One loader serves one host thread at a time. */
+int fmcuda_record_loader_create(const char *path, int reader_mode, uint64_t coalesce_gap,
+                                uint64_t chunk_bytes, uint32_t ring_depth, int force_direct_fallback,
+                                const fmcuda_file_identity *expected, fmcuda_record_loader **out);
+int fmcuda_record_loader_destroy(fmcuda_record_loader *loader);
+
+typedef struct fmcuda_record_load_stats {
+    uint64_t payload_bytes;      /* bytes written to the slot (sum of the extents) */
+    uint64_t physical_bytes;     /* bytes read from the file (aligned spans in Direct mode) */
+    uint64_t read_requests;      /* coalesced groups read */
+    uint64_t coalesced_requests; /* extents merged into another extent's read */
+    uint64_t direct_fallbacks;   /* groups read buffered in Direct mode */
+    uint64_t checksum;           /* FNV-1a 64 of the slot bytes after the copy */
+    double elapsed_ms;           /* host wall time of the call */
+} fmcuda_record_load_stats;
+
+/* Device bytes of `workspace` for a record of `payload_bytes` (256-byte aligned). */
+uint64_t fmcuda_record_load_workspace_bytes(uint64_t payload_bytes);
+
+/* One expert record from the file into the HBM slot: the demand path of
+ * ResidencyManager::load_slot (src/residency.cpp:624-724) from
+ * ReadScheduler::read_record (src/io.cpp:392-400) through the upload and the
+ * slot checksum.  The extents are copied to the slot in record (role) order,
+ * as read_record concatenates them; each coalesced group is read in chunks
+ * straight into the pinned ring, each chunk copied with cudaMemcpyAsync on
+ * `stream` while the next is read.  Then FNV-1a 64 of the slot runs on the
+ * device; stats->checksum holds it.  With checksum_known, a value other than
+ * expected_checksum is EXPERT_CHECKSUM_MISMATCH -- one test covering the
+ * source check and the slot check of load_slot.  Without it (vendor files
+ * publish no checksum) the value is returned for the caller to keep.
+ * Errors: SOURCE_CHANGED, SHORT_READ (an extent past the end of the file,
+ * before any byte moves; or a short read), IO_ERROR, INVALID_ARGUMENT
+ * (zero-sized extent, payload larger than `slot_bytes`, small workspace),
+ * TRANSFER_FAILED / DEVICE_LOSS, FENCE_TIMEOUT (a copy not done within
+ * `timeout_ms`).  The call returns once the checksum is on the host; after an
+ * error, copies already issued may still be in flight on `stream`. */
+int fmcuda_record_load(fmcuda_record_loader *loader, const fmcuda_extent *extents, uint32_t n_extents,
+                       void *slot, uint64_t slot_bytes, int checksum_known, uint64_t expected_checksum,
+                       void *workspace, uint64_t workspace_bytes, void *stream, uint32_t timeout_ms,
+                       fmcuda_record_load_stats *stats);
 
 /* ====================== synthetic weights (bench/test) ====================== */
 

@@ -183,6 +183,26 @@ class Oracle:
         d = np.ascontiguousarray(data).view(np.uint8)
         return int(self.lib.fmo_fnv1a64(_ptr(d), d.size))
 
+    @staticmethod
+    def coalesce_extents(extents, max_gap: int):
+        """coalesce_extents (src/io.cpp:46-78): extents (offset, size) sorted by
+        offset then size; one starting at most max_gap bytes past the current
+        group's end joins it.  Returns [(offset, end, [extent indices])];
+        raises ValueError for a zero-sized or overflowing extent."""
+        order = sorted(range(len(extents)), key=lambda i: (extents[i][0], extents[i][1], i))
+        groups = []
+        for i in order:
+            off, size = extents[i]
+            if size == 0 or off > (1 << 64) - 1 - size:
+                raise ValueError("invalid extent")
+            end = off + size
+            if groups and max_gap <= (1 << 64) - 1 - groups[-1][1] and off <= groups[-1][1] + max_gap:
+                groups[-1][1] = max(groups[-1][1], end)
+                groups[-1][2].append(i)
+                continue
+            groups.append([off, end, [i]])
+        return [(g[0], g[1], g[2]) for g in groups]
+
 
 class Reference:
     """The reference's own code, compiled from source (oracle/_ref/libfmref.so)."""
@@ -201,6 +221,9 @@ class Reference:
             "fmr_route": (_i, [_P, _u32, _u32, _u32, _P, _P, _P]),
             "fmr_swiglu": (_f, [_f, _f]),
             "fmr_fnv1a64": (_u64, [_P, _u64]),
+            "fmr_coalesce_extents": (_i, [_P, _u32, _u64, _P, _P, _P, _P]),
+            "fmr_file_identity": (_i, [C.c_char_p, _P]),
+            "fmr_load_records_cpu": (C.c_int64, [C.c_char_p, _i, _u64, _P, _u32, _u32, _P, _P]),
             "fmr_moe_block": (_i, [_u32, _P, _u64, _u64, _P, _u32, _u32, _u32, _u32, _P, _P, _P, _u32]),
         }
         for name, (res, args) in sig.items():
@@ -211,6 +234,39 @@ class Reference:
 
     def isa(self) -> str:
         return self.lib.fmr_resolved_isa().decode()
+
+    def coalesce_extents(self, extents, max_gap: int):
+        """The reference's own coalesce_extents: [(offset, end, [extent indices])]."""
+        n = len(extents)
+        ext = np.array(extents, dtype=np.uint64).reshape(n, 2) if n else np.zeros((0, 2), np.uint64)
+        go, ge = np.zeros(max(n, 1), np.uint64), np.zeros(max(n, 1), np.uint64)
+        gof, ng = np.zeros(max(n, 1), np.uint32), np.zeros(1, np.uint32)
+        rc = self.lib.fmr_coalesce_extents(_ptr(ext), n, max_gap, _ptr(go), _ptr(ge), _ptr(gof), _ptr(ng))
+        if rc:
+            raise ValueError(self.lib.fmr_last_error().decode())
+        return [(int(go[j]), int(ge[j]), [i for i in range(n) if gof[i] == j]) for j in range(int(ng[0]))]
+
+    def file_identity(self, path) -> tuple:
+        """current_identity (src/common.cpp:79-119): (size, dev, ino, mtime_ns, ctime_ns, content_probe)."""
+        out = np.zeros(6, np.uint64)
+        rc = self.lib.fmr_file_identity(str(path).encode(), _ptr(out))
+        if rc:
+            raise RuntimeError(self.lib.fmr_last_error().decode())
+        v = [int(x) for x in out]
+        to_i64 = lambda u: u - (1 << 64) if u >= 1 << 63 else u
+        return (v[0], v[1], v[2], to_i64(v[3]), to_i64(v[4]), v[5])
+
+    def load_records_cpu(self, path, reader_mode: int, coalesce_gap: int, extents: np.ndarray,
+                         checksums: np.ndarray, slot: np.ndarray) -> int:
+        """load_slot's data path on the reference's CPU backend for records of
+        extents [n_records, n_ext, 2] (see fmr_load_records_cpu)."""
+        ext = np.ascontiguousarray(extents, dtype=np.uint64)
+        ck = np.ascontiguousarray(checksums, dtype=np.uint64)
+        rc = self.lib.fmr_load_records_cpu(str(path).encode(), reader_mode, coalesce_gap, _ptr(ext),
+                                           ext.shape[1], ext.shape[0], _ptr(ck), _ptr(slot))
+        if rc < 0:
+            raise RuntimeError(self.lib.fmr_last_error().decode())
+        return int(rc)
 
     def dequant(self, type_id, src, n_elems) -> np.ndarray:
         out = np.empty(n_elems, dtype=np.float32)

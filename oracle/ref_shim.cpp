@@ -19,6 +19,7 @@
 
 #include "fm/activation.hpp"
 #include "fm/common.hpp"
+#include "fm/io.hpp"
 #include "fm/kernels.hpp"
 #include "fm/quant.hpp"
 #define private public
@@ -234,6 +235,78 @@ int fmr_moe_block(uint32_t type_id, const uint8_t *const *slots, uint64_t up_off
         return 0;
     } catch (const fm::Error &e) {
         return code_of(e);
+    }
+}
+
+// coalesce_extents (src/io.cpp:46-78): group [offset, end) and the group of
+// every extent (extents are pairs offset, size).
+int fmr_coalesce_extents(const uint64_t *ext, uint32_t n, uint64_t max_gap, uint64_t *group_offset,
+                         uint64_t *group_end, uint32_t *group_of, uint32_t *n_groups) {
+    try {
+        std::vector<fm::Extent> v(n);
+        for (uint32_t i = 0; i < n; ++i) v[i] = {ext[2 * i], ext[2 * i + 1]};
+        std::vector<fm::CoalescedGroup> g = fm::coalesce_extents(v, max_gap);
+        *n_groups = static_cast<uint32_t>(g.size());
+        for (size_t j = 0; j < g.size(); ++j) {
+            group_offset[j] = g[j].offset;
+            group_end[j] = g[j].end;
+            for (size_t idx : g[j].request_indices) group_of[idx] = static_cast<uint32_t>(j);
+        }
+        return 0;
+    } catch (const fm::Error &e) {
+        return code_of(e);
+    }
+}
+
+// current_identity (src/common.cpp:79-119) as six words: size, dev, ino,
+// mtime_ns, ctime_ns, content_probe.
+int fmr_file_identity(const char *path, uint64_t *out) {
+    try {
+        fm::FileIdentity id = fm::current_identity(path);
+        out[0] = id.size;
+        out[1] = id.dev;
+        out[2] = id.ino;
+        out[3] = static_cast<uint64_t>(id.mtime_ns);
+        out[4] = static_cast<uint64_t>(id.ctime_ns);
+        out[5] = id.content_probe;
+        return 0;
+    } catch (const fm::Error &e) {
+        return code_of(e);
+    }
+}
+
+// The data path of ResidencyManager::load_slot (src/residency.cpp:637-720) on
+// the reference's CPU backend: ReadScheduler::read_record through the
+// reference's own reader, fnv1a64 of the payload against the record
+// checksum, the upload (CpuBackend::upload is a memcpy into the slot,
+// src/backend.cpp:262-283), then the slot read-back and its fnv1a64.  Records
+// are `n_records` x `n_ext` extents (offset, size pairs); slot receives each
+// record in turn.  Returns the number of records loaded, or -code.
+int64_t fmr_load_records_cpu(const char *path, int reader_mode, uint64_t coalesce_gap, const uint64_t *ext,
+                             uint32_t n_ext, uint32_t n_records, const uint64_t *checksums, uint8_t *slot) {
+    try {
+        fm::SchedulerConfig cfg;
+        cfg.mode = static_cast<fm::ReaderMode>(reader_mode);
+        cfg.path = path;
+        cfg.expected_identity = fm::current_identity(path);
+        cfg.coalesce_gap = coalesce_gap;
+        fm::ReadScheduler sched(cfg, fm::make_reader(cfg.mode, path, nullptr, false));
+        for (uint32_t r = 0; r < n_records; ++r) {
+            std::vector<fm::Extent> v(n_ext);
+            for (uint32_t i = 0; i < n_ext; ++i)
+                v[i] = {ext[2 * (r * n_ext + i)], ext[2 * (r * n_ext + i) + 1]};
+            std::vector<uint8_t> payload = sched.read_record(v, fm::ReadPriority::Demand);
+            if (fm::fnv1a64(payload) != checksums[r])
+                fm::fail(fm::ErrorCode::EXPERT_CHECKSUM_MISMATCH, "source expert checksum mismatch");
+            std::memcpy(slot, payload.data(), payload.size());
+            std::vector<uint8_t> slot_copy(payload.size());
+            std::memcpy(slot_copy.data(), slot, payload.size());
+            if (fm::fnv1a64(slot_copy) != checksums[r])
+                fm::fail(fm::ErrorCode::EXPERT_CHECKSUM_MISMATCH, "slot payload checksum mismatch");
+        }
+        return n_records;
+    } catch (const fm::Error &e) {
+        return -code_of(e);
     }
 }
 
