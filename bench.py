@@ -791,6 +791,192 @@ def run_gemv_shapes(args):
     print(json.dumps(line), flush=True)
 
 
+COLD_RECORDS = 8
+COLD_METRIC = "cold expert-record load GB/s (model file -> HBM slot, FNV-1a checked), Mixtral Q4_K records"
+
+
+def cold_model_file(records: int):
+    """A synthetic model file holding `records` Mixtral-shaped Q4_K expert records
+    in three stacked tensors (gate, up, down), like ffn_{gate,up,down}_exps; returns
+    (path, [[(offset, size)] * 3] per record, payload bytes, tmp dir).  Random bytes:
+    the path moves and checksums bytes, it does not decode them."""
+    import tempfile
+
+    import numpy as np
+
+    sizes = [FFN * row_bytes(TYPES["q4_k"], D_MODEL)] * 2 + [D_MODEL * row_bytes(TYPES["q4_k"], FFN)]
+    d = tempfile.mkdtemp(prefix="fm_cold_")
+    path = os.path.join(d, "experts.gguf")
+    header = 4096 + 123  # tensor data starts unaligned
+    starts = [header, header + records * sizes[0], header + records * (sizes[0] + sizes[1])]
+    total = starts[2] + records * sizes[2]
+    rng = np.random.default_rng(7)
+    with open(path, "wb") as f:
+        left = total
+        while left:
+            n = min(left, 64 << 20)
+            f.write(rng.integers(0, 256, n, dtype=np.uint8).tobytes())
+            left -= n
+    recs = [[(starts[j] + r * sizes[j], sizes[j]) for j in range(3)] for r in range(records)]
+    return path, recs, sum(sizes), d
+
+
+def cold_checksums(path, recs):
+    from oracle.oracle import Oracle
+
+    import numpy as np
+
+    orc = Oracle()
+    raw = np.memmap(path, dtype=np.uint8, mode="r")
+    return [orc.fnv1a64(np.concatenate([raw[o:o + s] for o, s in rec])) for rec in recs]
+
+
+def run_coldload(args):
+    """--config coldload: one step = one expert record from the model file into an
+    HBM slot through the C-ABI loader (pread by 8 reader threads into pinned
+    rings, cudaMemcpyAsync, FNV-1a 64 of the slot on the device, checked against
+    the record checksum), the demand load of ResidencyManager::load_slot
+    (src/residency.cpp:624-724).  Page cache warm: the file is written just
+    before; buffered reads."""
+    import shutil
+
+    import torch
+
+    from freemoe_b200 import _lib as FL
+    from freemoe_b200 import coldtier, hotpath
+
+    world, rank, local = dist_setup(args)
+    hotpath.init(local)
+    dev = torch.device("cuda", local)
+    path, recs, payload, tmp = cold_model_file(COLD_RECORDS)
+    try:
+        sums = cold_checksums(path, recs)
+        slot = torch.empty(payload, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        steps = args.steps if args.steps != 2000 else 200
+        with coldtier.RecordLoader(path, "buffered") as ld:
+            for i in range(args.warmup):
+                ld.read_record_into(recs[i % COLD_RECORDS], slot, checksum=sums[i % COLD_RECORDS])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clocks:
+                e0.record(stream)
+                for i in range(steps):
+                    ld.read_record_into(recs[i % COLD_RECORDS], slot, checksum=sums[i % COLD_RECORDS])
+                e1.record(stream)
+                torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+        # the device FNV alone (the loader's only kernels), CUDA events on its stream
+        lib = FL.load()
+        out = torch.empty(1, dtype=torch.int64, device=dev)
+        ws = torch.empty(int(lib.fmcuda_fnv1a64_workspace_bytes(payload)), dtype=torch.uint8, device=dev)
+        call = (C.c_void_p(slot.data_ptr()), payload, C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()),
+                ws.numel(), C.c_void_p(stream.cuda_stream))
+        for _ in range(3):
+            FL.check(lib.fmcuda_fnv1a64(*call))
+        reps = 50
+        e0.record(stream)
+        for _ in range(reps):
+            FL.check(lib.fmcuda_fnv1a64(*call))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        fnv_ms = e0.elapsed_time(e1) / reps
+        # the ceiling: a plain pinned host -> device copy of one record
+        h = torch.empty(payload, dtype=torch.uint8).pin_memory()
+        for _ in range(2):
+            slot.copy_(h, non_blocking=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(5):
+            slot.copy_(h, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        h2d = payload / (e0.elapsed_time(e1) / 5) / 1e6
+        del h
+        cpu = None
+        if not args.no_cpu and rank == 0:
+            from oracle.oracle import Reference, reference_available
+
+            if reference_available():
+                import numpy as np
+
+                ref = Reference()
+                hslot = np.empty(payload, dtype=np.uint8)
+                ext = np.array(recs, dtype=np.uint64)
+                t0 = time.perf_counter()
+                n = ref.load_records_cpu(path, 1, 4096, ext, np.array(sums, np.uint64), hslot)
+                dt = time.perf_counter() - t0
+                cpu = {"value": n * payload / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference",
+                       "sample": f"{n} records: ReadScheduler::read_record (buffered) + fnv1a64 + memcpy into the "
+                                 f"slot + fnv1a64 of the slot copy, the reference's own code"}
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    peak, peak_kind = load_peaks()
+    value = payload / ms / 1e6
+    fnv_gbs = payload / fnv_ms / 1e6
+    line = {"metric": COLD_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": f"{COLD_RECORDS} Mixtral Q4_K expert records of {payload / 1e6:.1f} MB "
+                                   f"(3 extents at unaligned offsets), cycled; buffered reads, page cache warm",
+                       "record_bytes": payload, "reader_threads": 8, "chunk_bytes": 4 << 20,
+                       "l2": "inputs larger than L2 (99 MB record per step, 8 records cycled)"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": payload, "d2h_bytes_per_step": 8},
+            "roofline": {"bound": "hbm", "kernel": "fnv_round_kernel x8 + fnv_final_kernel (per record)",
+                         "achieved": fnv_gbs, "peak": peak, "unit": "GB/s", "frac": fnv_gbs / peak,
+                         "peak_kind": peak_kind, "traffic": None},
+            "h2d_ceiling": {"pinned_copy_GBps": h2d, "frac": value / h2d},
+            "gpu_launches": steps * 10, "clocks": clocks.summary()}
+    if cpu:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference_coldload(args):
+    """--impl reference --config coldload: the reference's own demand-load data path
+    (fmr_load_records_cpu over ReadScheduler::read_record, fnv1a64, the CPU
+    backend's memcpy upload and the slot checksum), on the same records."""
+    import shutil
+
+    import numpy as np
+
+    world, rank, local = dist_setup(args)
+    if rank != 0:
+        return
+    from oracle.oracle import Reference
+
+    path, recs, payload, tmp = cold_model_file(COLD_RECORDS)
+    try:
+        sums = cold_checksums(path, recs)
+        ref = Reference()
+        hslot = np.empty(payload, dtype=np.uint8)
+        one = lambda i: ref.load_records_cpu(path, 1, 4096, np.array([recs[i % COLD_RECORDS]], np.uint64),
+                                             np.array([sums[i % COLD_RECORDS]], np.uint64), hslot)
+        t0 = time.perf_counter()
+        one(0)
+        t_one = time.perf_counter() - t0
+        steps = max(1, min(args.steps, int(REF_BUDGET_S / max(t_one, 1e-3))))
+        for i in range(min(args.warmup, 3)):
+            one(i)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            one(i)
+        dt = (time.perf_counter() - t0) / steps
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    value = payload / dt / 1e9
+    line = {"impl": "reference", "metric": COLD_METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": f"{COLD_RECORDS} Mixtral Q4_K expert records of {payload / 1e6:.1f} MB, cycled; "
+                                   f"buffered reads, page cache warm", "record_bytes": payload},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "reference",
+                             "sample": f"{steps} of the --steps records (the arm is bounded to ~{REF_BUDGET_S:.0f} s)"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference_layer(args):
     """--impl reference --config deepseek|qwen3|mixtral: the reference's own
     per-token expert loop (gemv_quant + silu, compiled from source into
@@ -976,11 +1162,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--sample", type=int, default=32,
                     help="tokens per step of the reference arm on a layer configuration")
-    ap.add_argument("--config", default="stack", choices=["stack", *LAYERS, "gemv"],
-                    help="stack (default, the headline) or a layer configuration")
+    ap.add_argument("--config", default="stack", choices=["stack", *LAYERS, "gemv", "coldload"],
+                    help="stack (default, the headline), a layer configuration, the GEMV shapes, "
+                         "or cold expert-record loads")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     args.tokens_set = any(a.startswith("--tokens") for a in sys.argv[1:])
+    if args.config == "coldload":
+        (run_reference_coldload if args.impl == "reference" else run_coldload)(args)
+        return
     if args.config in LAYERS and args.impl == "reference":
         run_reference_layer(args)
         return

@@ -205,7 +205,7 @@ SIGNATURES = [
     ("fmcuda_fnv1a64", C.c_int, [_P, _U64, _P, _P, _U64, _P]),
     ("fmcuda_file_identity_get", C.c_int, [C.c_char_p, C.POINTER(FileIdentity)]),
     ("fmcuda_coalesce_extents", C.c_int, [C.POINTER(Extent), _U32, _U64, _P, _P, _P, C.POINTER(C.c_uint32)]),
-    ("fmcuda_record_loader_create", C.c_int, [C.c_char_p, C.c_int, _U64, _U64, _U32, C.c_int,
+    ("fmcuda_record_loader_create", C.c_int, [C.c_char_p, C.c_int, _U64, _U64, _U32, _U32, C.c_int,
                                               C.POINTER(FileIdentity), C.POINTER(C.c_void_p)]),
     ("fmcuda_record_loader_destroy", C.c_int, [_P]),
     ("fmcuda_record_load_workspace_bytes", _U64, [_U64]),

@@ -77,12 +77,15 @@ class RecordLoader:
 
     mode: "buffered" (pread) or "direct" (O_DIRECT aligned spans, falling back
     to buffered reads per group when the file system refuses, counted in
-    ``direct_fallbacks``).  ``expected_identity`` is the identity the manifest
+    ``direct_fallbacks``).  ``reader_threads`` threads read chunks of
+    ``chunk_bytes`` in parallel, each into its own ring of ``ring_depth``
+    pinned chunks.  ``expected_identity`` is the identity the manifest
     was built against (None: the file as it is now); each load re-checks it.
     """
 
-    def __init__(self, path, mode: str = "buffered", coalesce_gap: int = 4096, chunk_bytes: int = 8 << 20,
-                 ring_depth: int = 4, force_direct_fallback: bool = False, expected_identity: tuple | None = None):
+    def __init__(self, path, mode: str = "buffered", coalesce_gap: int = 4096, chunk_bytes: int = 4 << 20,
+                 ring_depth: int = 3, reader_threads: int = 8, force_direct_fallback: bool = False,
+                 expected_identity: tuple | None = None):
         self._lib = L.load()
         modes = {"buffered": L.READER_BUFFERED, "direct": L.READER_DIRECT}
         if mode not in modes:
@@ -92,7 +95,7 @@ class RecordLoader:
             ident = L.FileIdentity(*expected_identity)
         h = C.c_void_p()
         L.check(self._lib.fmcuda_record_loader_create(str(path).encode(), modes[mode], coalesce_gap, chunk_bytes,
-                                                      ring_depth, 1 if force_direct_fallback else 0,
+                                                      ring_depth, reader_threads, 1 if force_direct_fallback else 0,
                                                       C.byref(ident) if ident is not None else None, C.byref(h)))
         self._h = h
         self._ws = None

@@ -1,7 +1,8 @@
 // record_loader.cu -- cold -> warm expert loads on the host side of the path:
-// file extents are read straight into a ring of pinned chunks and copied to the
-// HBM slot with cudaMemcpyAsync while the next chunk is read; the checksum is
-// FNV-1a 64 of the slot computed on the device (fnv.cu).
+// file extents are read straight into rings of pinned chunks by several reader
+// threads and copied to the HBM slot with cudaMemcpyAsync (one copy stream per
+// reader) while the next chunks are read; the checksum is FNV-1a 64 of the
+// slot computed on the device (fnv.cu).
 //
 // What it replaces in the reference's demand load (ResidencyManager::load_slot,
 // src/residency.cpp:624-724):
@@ -29,10 +30,12 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cerrno>
 #include <chrono>
 #include <cstring>
 #include <limits>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -138,6 +141,17 @@ ssize_t pread_full(int fd, void *buf, uint64_t n, uint64_t off) {
 
 } // namespace
 
+// One reader thread's share: a copy stream and a ring of pinned chunks.
+struct Reader {
+    cudaStream_t stream = nullptr;
+    std::vector<void *> raw;         // pinned allocations, chunk + alignment bytes
+    std::vector<uint8_t *> buf;      // the aligned chunk inside each
+    std::vector<cudaEvent_t> ev;     // last copy out of each chunk
+    std::vector<bool> busy;
+    cudaEvent_t tail = nullptr;      // end of this reader's copies of a record
+    size_t next = 0;
+};
+
 struct fmcuda_record_loader {
     std::string path;
     int fd = -1;
@@ -148,22 +162,24 @@ struct fmcuda_record_loader {
     uint64_t alignment = 4096;
     uint64_t chunk = 0;
     fmcuda_file_identity expected{};
-    std::vector<void *> ring_raw;     // pinned allocations, `chunk` + `alignment` bytes
-    std::vector<void *> ring;         // the aligned `chunk` bytes inside each
-    std::vector<cudaEvent_t> ring_ev; // last copy out of each chunk
-    std::vector<bool> ring_busy;
+    std::vector<Reader> readers;
+    cudaEvent_t entry = nullptr;      // the caller's stream at the start of a load
     uint64_t *host_word = nullptr;    // pinned: the checksum read back
     cudaEvent_t done = nullptr;
-    size_t next = 0;
 
     ~fmcuda_record_loader() {
-        for (size_t i = 0; i < ring.size(); ++i) {
-            if (ring_ev[i]) {
-                (void)cudaEventSynchronize(ring_ev[i]);
-                (void)cudaEventDestroy(ring_ev[i]);
+        for (Reader &r : readers) {
+            for (size_t i = 0; i < r.ev.size(); ++i) {
+                if (r.ev[i]) {
+                    (void)cudaEventSynchronize(r.ev[i]);
+                    (void)cudaEventDestroy(r.ev[i]);
+                }
+                if (r.raw[i]) (void)cudaFreeHost(r.raw[i]);
             }
-            if (ring_raw[i]) (void)cudaFreeHost(ring_raw[i]);
+            if (r.tail) (void)cudaEventDestroy(r.tail);
+            if (r.stream) (void)cudaStreamDestroy(r.stream);
         }
+        if (entry) (void)cudaEventDestroy(entry);
         if (done) {
             (void)cudaEventSynchronize(done);
             (void)cudaEventDestroy(done);
@@ -172,22 +188,34 @@ struct fmcuda_record_loader {
         if (fd >= 0) ::close(fd);
         if (direct_fd >= 0) ::close(direct_fd);
     }
-
-    // polled, bounded wait for one event (Backend::wait_fence semantics)
-    int wait(cudaEvent_t ev, uint32_t timeout_ms) {
-        const auto t0 = std::chrono::steady_clock::now();
-        for (uint32_t spin = 0;; ++spin) {
-            const cudaError_t err = cudaEventQuery(ev);
-            if (err == cudaSuccess) return FM_STATUS_OK;
-            if (err != cudaErrorNotReady) return fmb::cuda_status(err, "record load: copy");
-            (void)cudaGetLastError();
-            if (std::chrono::steady_clock::now() - t0 >= std::chrono::milliseconds(timeout_ms))
-                return set_error(FM_STATUS_FENCE_TIMEOUT, "record load: copy did not complete within " +
-                                                              std::to_string(timeout_ms) + " ms");
-            if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(5));
-        }
-    }
 };
+
+namespace {
+
+// polled, bounded wait for one event (Backend::wait_fence semantics)
+int wait_event(cudaEvent_t ev, uint32_t timeout_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t spin = 0;; ++spin) {
+        const cudaError_t err = cudaEventQuery(ev);
+        if (err == cudaSuccess) return FM_STATUS_OK;
+        if (err != cudaErrorNotReady) return fmb::cuda_status(err, "record load: copy");
+        (void)cudaGetLastError();
+        if (std::chrono::steady_clock::now() - t0 >= std::chrono::milliseconds(timeout_ms))
+            return set_error(FM_STATUS_FENCE_TIMEOUT, "record load: copy did not complete within " +
+                                                          std::to_string(timeout_ms) + " ms");
+        if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(5));
+    }
+}
+
+// One chunk-sized read: file bytes [lo, hi) of group g, read from `pos`
+// (Direct: an aligned span of n bytes; buffered: pos = lo, n = hi - lo).
+struct Job {
+    uint32_t group;
+    bool direct;
+    uint64_t pos, n, lo, hi;
+};
+
+} // namespace
 
 extern "C" int fmcuda_file_identity_get(const char *path, fmcuda_file_identity *id) {
     if (!path || !id) return set_error(FM_STATUS_INVALID_ARGUMENT, "file identity: null argument");
@@ -211,15 +239,17 @@ extern "C" int fmcuda_coalesce_extents(const fmcuda_extent *extents, uint32_t n,
 }
 
 extern "C" int fmcuda_record_loader_create(const char *path, int reader_mode, uint64_t coalesce_gap,
-                                           uint64_t chunk_bytes, uint32_t ring_depth,
+                                           uint64_t chunk_bytes, uint32_t ring_depth, uint32_t reader_threads,
                                            int force_direct_fallback, const fmcuda_file_identity *expected,
                                            fmcuda_record_loader **out) {
     if (!path || !out) return set_error(FM_STATUS_INVALID_ARGUMENT, "record loader: null argument");
     *out = nullptr;
     if (reader_mode != FM_READER_BUFFERED && reader_mode != FM_READER_DIRECT)
         return set_error(FM_STATUS_INVALID_ARGUMENT, "record loader: reader mode must be buffered or direct");
-    if (ring_depth < 2 || ring_depth > 64 || chunk_bytes < (1u << 16) || chunk_bytes > (1ull << 30))
-        return set_error(FM_STATUS_INVALID_ARGUMENT, "record loader: ring of 2..64 chunks of 64 KiB..1 GiB");
+    if (ring_depth < 2 || ring_depth > 64 || chunk_bytes < (1u << 16) || chunk_bytes > (1ull << 30) ||
+        reader_threads < 1 || reader_threads > 32)
+        return set_error(FM_STATUS_INVALID_ARGUMENT,
+                         "record loader: 1..32 readers, each a ring of 2..64 chunks of 64 KiB..1 GiB");
     auto *L = new fmcuda_record_loader();
     L->path = path;
     L->mode = reader_mode;
@@ -252,25 +282,29 @@ extern "C" int fmcuda_record_loader_create(const char *path, int reader_mode, ui
     // chunks are whole multiples of the direct-I/O alignment, so every chunk
     // of an aligned span starts aligned in the file and in memory
     L->chunk = (chunk_bytes + L->alignment - 1) / L->alignment * L->alignment;
-    L->ring_raw.assign(ring_depth, nullptr);
-    L->ring.assign(ring_depth, nullptr);
-    L->ring_ev.assign(ring_depth, nullptr);
-    L->ring_busy.assign(ring_depth, false);
-    for (uint32_t i = 0; i < ring_depth && !rc; ++i) {
-        cudaError_t err = cudaHostAlloc(&L->ring_raw[i], L->chunk + L->alignment, cudaHostAllocDefault);
-        if (err == cudaSuccess) {
-            const uintptr_t a = reinterpret_cast<uintptr_t>(L->ring_raw[i]);
-            L->ring[i] = reinterpret_cast<void *>((a + L->alignment - 1) & ~uintptr_t(L->alignment - 1));
+    L->readers.resize(reader_threads);
+    cudaError_t err = cudaSuccess;
+    for (Reader &r : L->readers) {
+        r.raw.assign(ring_depth, nullptr);
+        r.buf.assign(ring_depth, nullptr);
+        r.ev.assign(ring_depth, nullptr);
+        r.busy.assign(ring_depth, false);
+        if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking);
+        if (err == cudaSuccess) err = cudaEventCreateWithFlags(&r.tail, cudaEventDisableTiming);
+        for (uint32_t i = 0; i < ring_depth && err == cudaSuccess; ++i) {
+            err = cudaHostAlloc(&r.raw[i], L->chunk + L->alignment, cudaHostAllocDefault);
+            if (err == cudaSuccess) {
+                const uintptr_t a = reinterpret_cast<uintptr_t>(r.raw[i]);
+                r.buf[i] = reinterpret_cast<uint8_t *>((a + L->alignment - 1) & ~uintptr_t(L->alignment - 1));
+                err = cudaEventCreateWithFlags(&r.ev[i], cudaEventDisableTiming);
+            }
         }
-        if (err == cudaSuccess) err = cudaEventCreateWithFlags(&L->ring_ev[i], cudaEventDisableTiming);
-        if (err != cudaSuccess) rc = fmb::cuda_status(err, "record loader: pinned ring");
     }
-    if (!rc) {
-        cudaError_t err = cudaHostAlloc(reinterpret_cast<void **>(&L->host_word), 64, cudaHostAllocDefault);
-        if (err == cudaSuccess) err = cudaEventCreateWithFlags(&L->done, cudaEventDisableTiming);
-        if (err != cudaSuccess) rc = fmb::cuda_status(err, "record loader: checksum word");
-    }
-    if (rc) {
+    if (err == cudaSuccess) err = cudaEventCreateWithFlags(&L->entry, cudaEventDisableTiming);
+    if (err == cudaSuccess) err = cudaHostAlloc(reinterpret_cast<void **>(&L->host_word), 64, cudaHostAllocDefault);
+    if (err == cudaSuccess) err = cudaEventCreateWithFlags(&L->done, cudaEventDisableTiming);
+    if (err != cudaSuccess) {
+        rc = fmb::cuda_status(err, "record loader: pinned ring");
         (void)cudaGetLastError();
         delete L;
         return rc;
@@ -320,95 +354,116 @@ extern "C" int fmcuda_record_load(fmcuda_record_loader *L, const fmcuda_extent *
         if (g.end > now.size)
             return set_error(FM_STATUS_SHORT_READ, "read beyond EOF: " + L->path);
     stats->payload_bytes = payload;
-    uint8_t *dst = static_cast<uint8_t *>(slot);
+    stats->read_requests = groups.size();
+    for (const Group &g : groups) stats->coalesced_requests += g.members.size() - 1;
 
-    // copies of the file bytes [lo, hi), held in `buf` from file offset `base`
-    auto dispatch = [&](const Group &g, const uint8_t *buf, uint64_t base, uint64_t lo, uint64_t hi) -> int {
-        for (uint32_t i : g.members) {
-            const uint64_t a = std::max(lo, extents[i].offset);
-            const uint64_t b = std::min(hi, extents[i].offset + extents[i].size);
-            if (a >= b) continue;
-            const cudaError_t err = cudaMemcpyAsync(dst + out_off[i] + (a - extents[i].offset), buf + (a - base),
-                                                    b - a, cudaMemcpyHostToDevice, stream);
-            if (err != cudaSuccess) {
-                (void)cudaGetLastError();
-                const int code = fmb::cuda_status(err, "record load: host-to-device copy");
-                return code == FM_STATUS_DEVICE_LOSS ? code : set_error(FM_STATUS_TRANSFER_FAILED, fmcuda_last_error());
-            }
-        }
-        return FM_STATUS_OK;
-    };
-    // next ring chunk, once the copies out of it have finished
-    auto take = [&](uint8_t **buf, size_t *idx) -> int {
-        const size_t i = L->next;
-        L->next = (L->next + 1) % L->ring.size();
-        if (L->ring_busy[i]) {
-            if (int rc = L->wait(L->ring_ev[i], timeout_ms)) return rc;
-            L->ring_busy[i] = false;
-        }
-        *buf = static_cast<uint8_t *>(L->ring[i]);
-        *idx = i;
-        return FM_STATUS_OK;
-    };
-    auto release = [&](size_t i) -> int {
-        const cudaError_t err = cudaEventRecord(L->ring_ev[i], stream);
-        if (err != cudaSuccess) return fmb::cuda_status(err, "record load: chunk event");
-        L->ring_busy[i] = true;
-        return FM_STATUS_OK;
-    };
-    // buffered reads of [from, g.end)
-    auto read_buffered = [&](const Group &g, uint64_t from) -> int {
-        for (uint64_t pos = from; pos < g.end;) {
-            uint8_t *buf;
-            size_t idx;
-            if (int rc = take(&buf, &idx)) return rc;
-            const uint64_t n = std::min(L->chunk, g.end - pos);
-            const ssize_t r = pread_full(L->fd, buf, n, pos);
-            if (r < 0) return set_error(FM_STATUS_IO_ERROR, "pread failed for " + L->path + ": " + std::strerror(errno));
-            if (static_cast<uint64_t>(r) < n) return set_error(FM_STATUS_SHORT_READ, "short read from " + L->path);
-            stats->physical_bytes += n;
-            if (int rc = dispatch(g, buf, pos, pos, pos + n)) return rc;
-            if (int rc = release(idx)) return rc;
-            pos += n;
-        }
-        return FM_STATUS_OK;
-    };
-
-    for (const Group &g : groups) {
-        ++stats->read_requests;
-        stats->coalesced_requests += g.members.size() - 1;
-        const bool direct = L->mode == FM_READER_DIRECT && !L->force_fallback && L->direct_fd >= 0;
-        if (!direct) {
-            if (L->mode == FM_READER_DIRECT) ++stats->direct_fallbacks;
-            if (int rc = read_buffered(g, g.offset)) return rc;
-            continue;
-        }
-        // aligned span [a0, a1) in chunk-sized direct reads
+    // chunk-sized reads of every group, in file order
+    const bool direct = L->mode == FM_READER_DIRECT && !L->force_fallback && L->direct_fd >= 0;
+    if (L->mode == FM_READER_DIRECT && !direct) stats->direct_fallbacks = groups.size();
+    std::vector<Job> jobs;
+    for (uint32_t gi = 0; gi < groups.size(); ++gi) {
+        const Group &g = groups[gi];
         const uint64_t A = L->alignment;
-        const uint64_t a0 = g.offset & ~(A - 1);
-        const uint64_t a1 = (g.end + A - 1) & ~(A - 1);
-        uint64_t covered = g.offset; // file bytes of the group already dispatched
-        for (uint64_t pos = a0; pos < a1 && covered < g.end;) {
-            uint8_t *buf;
-            size_t idx;
-            if (int rc = take(&buf, &idx)) return rc;
-            const uint64_t n = std::min(L->chunk, a1 - pos);
-            const ssize_t r = pread_full(L->direct_fd, buf, n, pos);
-            const uint64_t want = std::min(pos + n, g.end) - covered; // bytes this chunk must supply
-            if (r < 0 || pos + static_cast<uint64_t>(r) < covered + want) {
-                // the file system refused or came up short: buffered reads for the rest
-                L->ring_busy[idx] = false;
-                ++stats->direct_fallbacks;
-                break;
-            }
-            stats->physical_bytes += static_cast<uint64_t>(r);
-            if (int rc = dispatch(g, buf, pos, covered, covered + want)) return rc;
-            if (int rc = release(idx)) return rc;
-            covered += want;
-            pos += n;
+        const uint64_t s0 = direct ? g.offset & ~(A - 1) : g.offset;
+        const uint64_t s1 = direct ? (g.end + A - 1) & ~(A - 1) : g.end;
+        for (uint64_t pos = s0; pos < s1; pos += L->chunk) {
+            const uint64_t n = std::min(L->chunk, s1 - pos);
+            jobs.push_back({gi, direct, pos, n, std::max(pos, g.offset), std::min(pos + n, g.end)});
         }
-        if (covered < g.end)
-            if (int rc = read_buffered(g, covered)) return rc;
+    }
+
+    int dev = 0;
+    cudaError_t cerr = cudaGetDevice(&dev);
+    if (cerr == cudaSuccess) cerr = cudaEventRecord(L->entry, stream);
+    if (cerr != cudaSuccess) return fmb::cuda_status(cerr, "record load: entry event");
+    uint8_t *dst = static_cast<uint8_t *>(slot);
+    std::atomic<size_t> next_job{0};
+    std::atomic<uint64_t> physical{0}, fallbacks{0};
+    std::vector<std::atomic<bool>> fell_back(groups.size());
+    for (auto &f : fell_back) f.store(false);
+    std::atomic<bool> failed{false};
+    std::mutex err_mutex;
+    int err_code = FM_STATUS_OK;
+    std::string err_msg;
+    const size_t n_readers = std::max<size_t>(1, std::min(L->readers.size(), jobs.size()));
+
+    auto reader = [&](size_t t) {
+        auto fail = [&](int code) {
+            std::lock_guard<std::mutex> lock(err_mutex);
+            if (err_code == FM_STATUS_OK) {
+                err_code = code;
+                err_msg = fmcuda_last_error();
+            }
+            failed.store(true);
+        };
+        auto cuda_fail = [&](cudaError_t e, const char *what) {
+            (void)cudaGetLastError();
+            const int code = fmb::cuda_status(e, what);
+            fail(code == FM_STATUS_DEVICE_LOSS || code == FM_STATUS_ALLOCATION_FAILED ? code
+                 : set_error(FM_STATUS_TRANSFER_FAILED, fmcuda_last_error()));
+        };
+        Reader &R = L->readers[t];
+        cudaError_t e = cudaSetDevice(dev);
+        // copies into the slot start after the caller's earlier work on it
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(R.stream, L->entry, 0);
+        if (e != cudaSuccess) return cuda_fail(e, "record load: reader stream");
+        for (;;) {
+            const size_t j = next_job.fetch_add(1);
+            if (j >= jobs.size() || failed.load()) break;
+            const Job &J = jobs[j];
+            const size_t i = R.next;
+            R.next = (R.next + 1) % R.buf.size();
+            if (R.busy[i]) {
+                if (int rc = wait_event(R.ev[i], timeout_ms)) return fail(rc);
+                R.busy[i] = false;
+            }
+            uint8_t *buf = R.buf[i];
+            uint64_t base = J.pos;
+            bool have = false;
+            if (J.direct && !fell_back[J.group].load()) {
+                const ssize_t r = pread_full(L->direct_fd, buf, J.n, J.pos);
+                if (r >= 0 && J.pos + static_cast<uint64_t>(r) >= J.hi) {
+                    physical += static_cast<uint64_t>(r);
+                    have = true;
+                } else if (!fell_back[J.group].exchange(true)) {
+                    ++fallbacks; // the file system refused: buffered reads for the rest of the group
+                }
+            }
+            if (!have) {
+                const uint64_t n = J.hi - J.lo;
+                const ssize_t r = pread_full(L->fd, buf, n, J.lo);
+                if (r < 0) return fail(set_error(FM_STATUS_IO_ERROR, "pread failed for " + L->path + ": " +
+                                                                         std::strerror(errno)));
+                if (static_cast<uint64_t>(r) < n) return fail(set_error(FM_STATUS_SHORT_READ, "short read from " + L->path));
+                physical += n;
+                base = J.lo;
+            }
+            for (uint32_t m : groups[J.group].members) {
+                const uint64_t a = std::max(J.lo, extents[m].offset);
+                const uint64_t b = std::min(J.hi, extents[m].offset + extents[m].size);
+                if (a >= b) continue;
+                e = cudaMemcpyAsync(dst + out_off[m] + (a - extents[m].offset), buf + (a - base), b - a,
+                                    cudaMemcpyHostToDevice, R.stream);
+                if (e != cudaSuccess) return cuda_fail(e, "record load: host-to-device copy");
+            }
+            if ((e = cudaEventRecord(R.ev[i], R.stream)) != cudaSuccess) return cuda_fail(e, "record load: chunk event");
+            R.busy[i] = true;
+        }
+        if ((e = cudaEventRecord(R.tail, R.stream)) != cudaSuccess) return cuda_fail(e, "record load: reader tail");
+    };
+    if (n_readers == 1) {
+        reader(0);
+    } else {
+        std::vector<std::thread> pool;
+        for (size_t t = 0; t < n_readers; ++t) pool.emplace_back(reader, t);
+        for (auto &th : pool) th.join();
+    }
+    stats->physical_bytes = physical.load();
+    stats->direct_fallbacks += fallbacks.load();
+    if (err_code != FM_STATUS_OK) return set_error(err_code, err_msg);
+    for (size_t t = 0; t < n_readers; ++t) {
+        cerr = cudaStreamWaitEvent(stream, L->readers[t].tail, 0);
+        if (cerr != cudaSuccess) return fmb::cuda_status(cerr, "record load: join");
     }
 
     // FNV-1a 64 of the slot bytes, on the device, then back to the host
@@ -416,11 +471,12 @@ extern "C" int fmcuda_record_load(fmcuda_record_loader *L, const fmcuda_extent *
     if (int rc = fmb::fnv1a64_launch(dst, payload, d_sum, static_cast<uint8_t *>(workspace) + 256,
                                      workspace_bytes - 256, stream))
         return rc;
-    cudaError_t err = cudaMemcpyAsync(L->host_word, d_sum, 8, cudaMemcpyDeviceToHost, stream);
-    if (err == cudaSuccess) err = cudaEventRecord(L->done, stream);
-    if (err != cudaSuccess) return fmb::cuda_status(err, "record load: checksum read-back");
-    if (int rc = L->wait(L->done, timeout_ms)) return rc;
-    for (size_t i = 0; i < L->ring.size(); ++i) L->ring_busy[i] = false; // all copies are behind `done`
+    cerr = cudaMemcpyAsync(L->host_word, d_sum, 8, cudaMemcpyDeviceToHost, stream);
+    if (cerr == cudaSuccess) cerr = cudaEventRecord(L->done, stream);
+    if (cerr != cudaSuccess) return fmb::cuda_status(cerr, "record load: checksum read-back");
+    if (int rc = wait_event(L->done, timeout_ms)) return rc;
+    // every reader's copies are behind `done`
+    for (size_t t = 0; t < n_readers; ++t) L->readers[t].busy.assign(L->readers[t].busy.size(), false);
     stats->checksum = *L->host_word;
     stats->elapsed_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     if (checksum_known && stats->checksum != expected_checksum)

@@ -484,16 +484,18 @@ enum { FM_READER_BUFFERED = 1, FM_READER_DIRECT = 3 };
 
 typedef struct fmcuda_record_loader fmcuda_record_loader;
 
-/* Opens `path` for expert loads: a ring of `ring_depth` pinned chunks of
- * `chunk_bytes` (rounded up to the direct-I/O alignment), the reader mode, the
- * coalescing gap and force_direct_fallback of fm::SchedulerConfig
- * (include/fm/io.hpp:100-107).  `expected` is the identity the manifest was
- * built against (NULL: the file as it is now); every load verifies it first
- * and fails SOURCE_CHANGED (src/io.cpp:262-278) when the file differs.
- * One loader serves one host thread at a time. */
+/* Opens `path` for expert loads by `reader_threads` reader threads, each with
+ * a copy stream and a ring of `ring_depth` pinned chunks of `chunk_bytes`
+ * (rounded up to the direct-I/O alignment); the reader mode, the coalescing
+ * gap and force_direct_fallback of fm::SchedulerConfig (include/fm/io.hpp:
+ * 100-107).  `expected` is the identity the manifest was built against (NULL:
+ * the file as it is now); every load verifies it first and fails
+ * SOURCE_CHANGED (src/io.cpp:262-278) when the file differs.  One loader
+ * serves one caller thread at a time. */
 int fmcuda_record_loader_create(const char *path, int reader_mode, uint64_t coalesce_gap,
-                                uint64_t chunk_bytes, uint32_t ring_depth, int force_direct_fallback,
-                                const fmcuda_file_identity *expected, fmcuda_record_loader **out);
+                                uint64_t chunk_bytes, uint32_t ring_depth, uint32_t reader_threads,
+                                int force_direct_fallback, const fmcuda_file_identity *expected,
+                                fmcuda_record_loader **out);
 int fmcuda_record_loader_destroy(fmcuda_record_loader *loader);
 
 typedef struct fmcuda_record_load_stats {
@@ -513,10 +515,11 @@ uint64_t fmcuda_record_load_workspace_bytes(uint64_t payload_bytes);
  * ResidencyManager::load_slot (src/residency.cpp:624-724) from
  * ReadScheduler::read_record (src/io.cpp:392-400) through the upload and the
  * slot checksum.  The extents are copied to the slot in record (role) order,
- * as read_record concatenates them; each coalesced group is read in chunks
- * straight into the pinned ring, each chunk copied with cudaMemcpyAsync on
- * `stream` while the next is read.  Then FNV-1a 64 of the slot runs on the
- * device; stats->checksum holds it.  With checksum_known, a value other than
+ * as read_record concatenates them; the coalesced groups are cut into chunks
+ * that the reader threads read straight into their pinned rings and copy to
+ * the slot with cudaMemcpyAsync on their own streams, which first wait for
+ * the work already queued on `stream`.  Then `stream` waits for every copy
+ * and FNV-1a 64 of the slot runs on the device; stats->checksum holds it.  With checksum_known, a value other than
  * expected_checksum is EXPERT_CHECKSUM_MISMATCH -- one test covering the
  * source check and the slot check of load_slot.  Without it (vendor files
  * publish no checksum) the value is returned for the caller to keep.

@@ -64,6 +64,19 @@ def test_device_fnv_constant_inputs(oracle):
         assert coldtier.fnv1a64(on_gpu(a)) == oracle.fnv1a64(a), v
 
 
+def test_device_fnv_ignores_stale_workspace(oracle):
+    # the workspace is scratch: whatever it holds from earlier use must not matter
+    lib = L.load()
+    a = seeded(71, 512 * 256 * 2 + 9)
+    src = on_gpu(a)
+    ws = torch.full((int(lib.fmcuda_fnv1a64_workspace_bytes(a.size)),), 0xFF, dtype=torch.uint8, device="cuda")
+    out = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+    for _ in range(2):
+        assert lib.fmcuda_fnv1a64(src.data_ptr(), a.size, out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                  torch.cuda.current_stream().cuda_stream) == 0
+        assert int(out.cpu().item()) & ((1 << 64) - 1) == oracle.fnv1a64(a)
+
+
 def test_device_fnv_rejects_bad_arguments():
     lib = L.load()
     out = torch.zeros(2, dtype=torch.int64, device="cuda")
@@ -120,20 +133,21 @@ def check_load(oracle, loader, data, extents, slot_bytes=None, **kw):
     return stats, groups
 
 
-@pytest.mark.parametrize("chunk,depth", [(1 << 16, 2), (1 << 16, 3), (1 << 20, 4), (8 << 20, 4)])
-def test_buffered_load(oracle, model_file, chunk, depth):
+@pytest.mark.parametrize("chunk,depth,threads", [(1 << 16, 2, 1), (1 << 16, 3, 4), (1 << 20, 4, 8), (8 << 20, 4, 4),
+                                                 (8 << 20, 2, 32)])
+def test_buffered_load(oracle, model_file, chunk, depth, threads):
     p, data = model_file
-    with coldtier.RecordLoader(p, "buffered", chunk_bytes=chunk, ring_depth=depth) as ld:
+    with coldtier.RecordLoader(p, "buffered", chunk_bytes=chunk, ring_depth=depth, reader_threads=threads) as ld:
         for seed in range(3):  # the ring carries over between records
             stats, groups = check_load(oracle, ld, data, record_extents(seed))
             assert stats.physical_bytes == sum(e - o for o, e, _ in groups)
             assert stats.direct_fallbacks == 0
 
 
-@pytest.mark.parametrize("chunk", [1 << 16, 4 << 20])
-def test_direct_load(oracle, model_file, chunk):
+@pytest.mark.parametrize("chunk,threads", [(1 << 16, 1), (1 << 16, 4), (4 << 20, 4)])
+def test_direct_load(oracle, model_file, chunk, threads):
     p, data = model_file
-    with coldtier.RecordLoader(p, "direct", chunk_bytes=chunk, ring_depth=3) as ld:
+    with coldtier.RecordLoader(p, "direct", chunk_bytes=chunk, ring_depth=3, reader_threads=threads) as ld:
         for seed in range(3):
             stats, groups = check_load(oracle, ld, data, record_extents(10 + seed))
             # O_DIRECT reads whole aligned blocks; a file system without it falls back per group
