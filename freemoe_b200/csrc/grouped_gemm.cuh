@@ -60,9 +60,6 @@ constexpr uint32_t GG_BM = 128;     // weight rows per tile (TMEM lanes)
 #ifndef FMB_GG_BN1
 #define FMB_GG_BN1 256
 #endif
-#ifndef FMB_GG_SB1
-#define FMB_GG_SB1 2
-#endif
 constexpr uint32_t GG_BN = FMB_GG_BN2;  // tokens per tile of the gate/up GEMM (two accumulators)
 constexpr uint32_t GG_BN1 = FMB_GG_BN1; // tokens per tile of the one-matrix GEMM (one accumulator)
 constexpr uint32_t GG_BK = 64;      // K values per MMA stage (one 128-byte fp16 row)
@@ -109,9 +106,19 @@ template <int TYPE> constexpr uint32_t gg_pitch() {
     else return GGeom<TYPE>::CB;
 }
 
+// Token (B) stages of the one-matrix GEMM: three where shared memory holds
+// them next to the raw rings (Q4_K, Q6_K; measured on the Qwen3 shape: down
+// -11% against two), else two (Q8_0's 272-byte chunks leave no room).
+template <int TYPE> constexpr uint32_t gg_sb1() {
+    constexpr uint32_t raw = 8 * GGeom<TYPE>::RS * 32 * gg_pitch<TYPE>();
+    constexpr uint32_t stage = GG_BN1 * GG_BK * 2;
+    constexpr uint32_t fixed = 1024 + 512 + 4 * (GG_MAX_EXPERTS + 1); // alignment, barriers, unit table
+    return raw + 3 * stage + fixed <= 227u * 1024u ? 3u : 2u;
+}
+
 template <int TYPE, int NMAT> struct GGLayout {
     static constexpr uint32_t BN = NMAT == 2 ? GG_BN : GG_BN1;  // tokens per unit
-    static constexpr uint32_t SB = NMAT == 2 ? FMB_GG_SB2 : FMB_GG_SB1; // B ring stages
+    static constexpr uint32_t SB = NMAT == 2 ? FMB_GG_SB2 : gg_sb1<TYPE>(); // B ring stages
     static constexpr uint32_t SA = NMAT == 2 ? FMB_GG_SA2 : 8;          // A stages in TMEM
     static constexpr uint32_t A_COL0 = NMAT * BN;               // accumulators first
     static constexpr uint32_t A_STAGE_COLS = NMAT * (GG_BK / 2); // fp16 pairs per column
@@ -130,6 +137,7 @@ template <int TYPE, int NMAT> struct GGLayout {
     static_assert((SB * B_STAGE) % 1024 == 0, "1024-byte aligned raw rings");
     static_assert(PITCH % 16 == 0 && (PITCH / 16) % 2 == 1, "conflict-free 16-byte row reads");
     static constexpr uint32_t smem_bytes(uint32_t experts) { return 1024 + OFF_UNITS + 4 * (experts + 1); }
+    static_assert(1024 + OFF_UNITS + 4 * (GG_MAX_EXPERTS + 1) <= 227u * 1024u, "shared memory per CTA");
 };
 
 struct GUnit {
