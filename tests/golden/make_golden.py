@@ -1,7 +1,7 @@
 """Generates the committed golden fixtures for the hot path.
 
-Run in a container that has the reference tree (default /root/reference, or
-$FM_REFERENCE) and the compiled reference shim (``make -C oracle``):
+Run where the reference source tree is present (its location comes from
+$FM_REFERENCE, with the checker's default otherwise) and the compiled reference shim (``make -C oracle``):
 
     python tests/golden/make_golden.py
 
