@@ -270,7 +270,7 @@ def make_experts(oracle, rng, E, d, ffn, t):
 
 
 @pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
-@pytest.mark.parametrize("T", [1, 4, 9, 33])
+@pytest.mark.parametrize("T", [1, 4, 9, 33, 70])
 @pytest.mark.parametrize("xdt", ["bf16", "f32"])
 def test_moe_block_vs_oracle(cuda, oracle, t, T, xdt):
     rng = np.random.default_rng(T * 7 + t)
@@ -288,6 +288,27 @@ def test_moe_block_vs_oracle(cuda, oracle, t, T, xdt):
     assert cuda.device_status() == 0
     assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
     assert np.array_equal(bits(w.cpu().numpy()), bits(w_o))
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
+
+
+@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
+def test_moe_block_skewed_routing(cuda, oracle, t):
+    # one expert takes every token (5 token tiles of the same rows), two take
+    # none, the rest share the second choices
+    rng = np.random.default_rng(500 + t)
+    E, k, d, ffn, T = 8, 2, 512, 768, 40
+    slots = make_experts(oracle, rng, E, d, ffn, t)
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    logits[:, 2] += 8.0
+    logits[:, [5, 6]] -= 8.0
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    assert (ids_o[:, 0] == 2).all()
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, t)
+    y, ids, w = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                               gate_type=t, return_routing=True)
+    assert cuda.device_status() == 0
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
     assert rel_err(y.cpu().numpy(), y_o) < TOL
 
 
