@@ -312,6 +312,24 @@ def test_moe_block_skewed_routing(cuda, oracle, t):
     assert rel_err(y.cpu().numpy(), y_o) < TOL
 
 
+@pytest.mark.parametrize("T", [3, 20])
+def test_moe_block_wide_model_short_ffn(cuda, oracle, T):
+    # 16 experts, d 2048, ffn 256: the down projection is a single 256-value K
+    # step (the second warp of each tile has no items), 15 experts active at T=20
+    rng = np.random.default_rng(700 + T)
+    E, k, d, ffn = 16, 2, 2048, 256
+    slots = make_experts(oracle, rng, E, d, ffn, TYPE_Q4_K)
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, TYPE_Q4_K)
+    y, ids, w = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                               gate_type=TYPE_Q4_K, return_routing=True)
+    assert cuda.device_status() == 0
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
+    assert rel_err(y.cpu().numpy(), y_o) < TOL
+
+
 @pytest.mark.parametrize("T", [1, 5, 40])
 def test_moe_block_mixed_record(cuda, oracle, T):
     # mixed-type expert records: Q4_K gate/up with a Q6_K down projection
