@@ -1102,21 +1102,15 @@ def run_layer_ep(args):
     dist.all_reduce(ph_t, op=dist.ReduceOp.MAX)
     phases = dict(zip(EPLayer.PHASES, ph_t.tolist()))
     layer.record_timing = False
-    # e2e: host token rows and logits in, y out, every step
+    # e2e: host token rows and logits in, y out, every step; the copies run on
+    # two copy streams beside the layer, as in the one-GPU configurations
     hx = torch.from_numpy(x_np[sl]).to(torch.bfloat16).pin_memory()
     hl = torch.from_numpy(lg_np[sl]).pin_memory()
-    hy = torch.empty(tp, d, dtype=torch.float32).pin_memory()
     dist.barrier()
     torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps):
-        dx = hx.cuda(non_blocking=True)
-        dl = hl.cuda(non_blocking=True)
-        y = layer.forward(dx, dl)
-        hy.copy_(y, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_e = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device="cuda")
+    ms_loc, hy = pipelined_e2e(lambda dx, dl, dy: dy.copy_(layer.forward(dx, dl)), hx, hl, x, logits,
+                               torch.empty(tp, d, dtype=torch.float32, device="cuda"), args.steps, stream)
+    ms_e = torch.tensor([ms_loc], dtype=torch.float64, device="cuda")
     dist.all_reduce(ms_e, op=dist.ReduceOp.MAX)
     assert np.isfinite(hy.numpy()).all()
     pairs = T * k
