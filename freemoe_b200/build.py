@@ -68,7 +68,10 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if failed:
         raise RuntimeError(f"nvcc failed for: {', '.join(failed)}")
     tmp = LIB.with_suffix(".so.tmp")
-    link = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp)]
+    # --no-undefined: a symbol missing from every object fails the build here,
+    # not the first dlopen on a GPU box
+    link = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-Xlinker", "--no-undefined", *map(str, objs),
+            "-o", str(tmp)]
     if verbose:
         print(" ".join(link), file=sys.stderr)
     subprocess.run(link, check=True)

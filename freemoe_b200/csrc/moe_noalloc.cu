@@ -9,6 +9,8 @@
 // cudaMalloc.  Both can still run the routed-expert block through this entry
 // point: its scratch is a fixed array in the library's device image, so the
 // call allocates nothing and frees nothing.
+#include <cuda.h>
+
 #include <mutex>
 #include <string>
 
@@ -27,10 +29,32 @@ namespace {
 static __device__ __align__(256) uint8_t g_noalloc_scratch[FM_MOE_NOALLOC_SCRATCH_BYTES];
 
 std::mutex g_scratch_mutex;
-void *g_scratch_addr[64] = {};
+struct ScratchEntry {
+    CUcontext ctx = nullptr; // the context the address belongs to
+    void *addr = nullptr;
+};
+ScratchEntry g_scratch_addr[64];
 
-// Device address of the scratch on the current device, looked up once per
-// device with that device current.
+// The current driver context (looked up through the runtime, so the library
+// needs no link against the driver library); NULL if none is current yet.
+CUcontext current_context() {
+    using GetCurrent = CUresult (*)(CUcontext *);
+    static GetCurrent fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<GetCurrent>(p);
+    }();
+    CUcontext ctx = nullptr;
+    if (!fn || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
+
+// Device address of the scratch on the current device, looked up with that
+// device current and cached per device and context: a context that was torn
+// down and created again (cudaDeviceReset) gets its own lookup.
 int scratch_address(void **out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
@@ -38,16 +62,19 @@ int scratch_address(void **out) {
     if (dev < 0 || dev >= 64)
         return set_error(FM_STATUS_INVALID_ARGUMENT, "device ordinal out of range for the scratch table");
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
+    ScratchEntry &e = g_scratch_addr[dev];
+    const CUcontext ctx = current_context();
+    if (!e.addr || !ctx || ctx != e.ctx) {
         void *p = nullptr;
         err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (err != cudaSuccess) {
             (void)cudaGetLastError();
             return cuda_status(err, "scratch symbol lookup");
         }
-        g_scratch_addr[dev] = p;
+        e.addr = p;
+        e.ctx = current_context(); // the lookup made the device's context current
     }
-    *out = g_scratch_addr[dev];
+    *out = e.addr;
     return FM_STATUS_OK;
 }
 

@@ -460,7 +460,22 @@ extern "C" int fmcuda_record_load(fmcuda_record_loader *L, const fmcuda_extent *
     }
     stats->physical_bytes = physical.load();
     stats->direct_fallbacks += fallbacks.load();
-    if (err_code != FM_STATUS_OK) return set_error(err_code, err_msg);
+    if (err_code != FM_STATUS_OK) {
+        // Copies the other readers issued before the failure may still be
+        // writing into the slot: order the caller's stream after every
+        // reader's last copy, and give them the timeout to finish, so a caller
+        // that reuses the slot after this error never sees late writes.
+        for (size_t t = 0; t < n_readers; ++t) {
+            Reader &R = L->readers[t];
+            if (cudaEventRecord(R.tail, R.stream) != cudaSuccess ||
+                cudaStreamWaitEvent(stream, R.tail, 0) != cudaSuccess) {
+                (void)cudaGetLastError();
+                continue;
+            }
+            if (wait_event(R.tail, timeout_ms) == FM_STATUS_OK) R.busy.assign(R.busy.size(), false);
+        }
+        return set_error(err_code, err_msg);
+    }
     for (size_t t = 0; t < n_readers; ++t) {
         cerr = cudaStreamWaitEvent(stream, L->readers[t].tail, 0);
         if (cerr != cudaSuccess) return fmb::cuda_status(cerr, "record load: join");

@@ -432,11 +432,16 @@ int fmcuda_ep_p2p_combine(void *mailbox, uint32_t world, uint32_t rank, uint32_t
  * FM_MOE_NOALLOC_SCRATCH_BYTES inside the library's device image, held by
  * every GPU that loads the library until the process exits.  A block whose
  * fmcuda_moe_workspace_bytes() exceeds that size is refused with
- * INVALID_ARGUMENT.  The first call on each device looks up the scratch's
- * device address with that device current; make that first call before
- * capturing the stream.  All calls share the one array and the next call
- * overwrites it, so calls that overlap on the GPU (other streams, other host
- * threads on the same device) race: keep them ordered on one stream. */
+ * INVALID_ARGUMENT.  The first call on each device (and the first after that
+ * device's context was destroyed and created again) looks up the scratch's
+ * device address with that device current.  With CUDA's lazy module loading
+ * that lookup is also when the device maps the scratch, so it can fail with
+ * ALLOCATION_FAILED once HBM is full: make the first call on each device --
+ * a call with tokens = 0 does the lookup and nothing else -- before the
+ * device memory is committed (to expert slots, say) and before capturing the
+ * stream.  All calls share the one array and the next call overwrites it, so
+ * calls that overlap on the GPU (other streams, other host threads on the
+ * same device) race: keep them ordered on one stream. */
 int fmcuda_moe_block_noalloc(const fmcuda_moe_args *args, void *stream);
 
 /* ==================== cold -> warm expert loads (record_loader.cu) ==================== */

@@ -352,6 +352,48 @@ def test_moe_block_mixed_record(cuda, oracle, T):
     assert rel_err(y.cpu().numpy(), y_o) < TOL
 
 
+@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
+@pytest.mark.parametrize("T,xdt", [(1, "bf16"), (9, "f32"), (37, "bf16"), (70, "f32")])
+def test_moe_block_ragged_tiles_d1024(cuda, oracle, t, T, xdt):
+    # the streamed GEMV on rows of four K steps: ragged token tiles, several
+    # token tiles of one expert (expert 1 takes most tokens), an expert with
+    # none; also checked element-wise where |y_ref| is not tiny
+    rng = np.random.default_rng(1300 + T + t)
+    E, k, d, ffn = 6, 2, 1024, 1024
+    slots = make_experts(oracle, rng, E, d, ffn, t)
+    x = rng.normal(0, 1, size=(T, d)).astype(np.float32)
+    if xdt == "bf16":
+        x = bf16_round(x)
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    logits[:, 1] += 2.0
+    logits[:, 4] -= 9.0
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, t)
+    xt = dev(x, torch.bfloat16) if xdt == "bf16" else dev(x)
+    y, ids, w = cuda.moe_block(xt, dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                               gate_type=t, return_routing=True)
+    assert cuda.device_status() == 0
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
+    got = y.cpu().numpy()
+    assert rel_err(got, y_o) < TOL
+    big = np.abs(y_o) > 1e-2 * np.abs(y_o).max()
+    assert float((np.abs(got - y_o)[big] / np.abs(y_o[big])).max()) < TOL
+
+
+def test_moe_block_streamed_missing_expert_flags(cuda, oracle):
+    rng = np.random.default_rng(3)
+    E, k, d, ffn = 4, 2, 1024, 1024
+    slots = make_experts(oracle, rng, E, d, ffn, TYPE_Q4_K)
+    x = torch.randn(6, d, device="cuda")
+    logits = torch.zeros(6, E, device="cuda")
+    logits[:, 3] = 5.0  # every token routes to expert 3
+    dslots = [dev(s) for s in slots]
+    dslots[3] = None
+    cuda.moe_block(x, logits, dslots, top_k=k, ffn=ffn, gate_type=TYPE_Q4_K)
+    torch.cuda.synchronize()
+    assert cuda.device_status(clear=True) == 18  # EXPERT_EXECUTION_MISMATCH
+
+
 def test_moe_block_missing_expert_flags(cuda, oracle):
     rng = np.random.default_rng(1)
     E, k, d, ffn = 4, 2, 256, 256

@@ -4,10 +4,14 @@ Some hosts cannot call cudaMalloc once decoding runs -- all of their HBM is
 already committed to expert slots, or the device allocator belongs to the host
 framework -- so the library offers a variant of the MoE block whose scratch is
 a fixed array inside the library image.  These tests call it through the C ABI
-and compare it with fmcuda_moe_block (which uses a caller workspace) on two
-calls in a row with different inputs, so a result that depended on what the
-previous call left in the shared scratch would show.  Collected last on
-purpose (file name), and independent of the other tests' state.
+and compare it with fmcuda_moe_block (which uses a caller workspace) bit for
+bit: both run the same kernels in the same order, so any difference would be
+a fault of the shared scratch.  Calls come in a row with different inputs, so
+a result that depended on what the previous call left in the scratch would
+show; they cover the single-launch front end (T <= 64, plain router), the
+separate router / grouping / x-plane kernels (T > 64, and a router variant),
+and free device memory must not move once the scratch is mapped.  Collected
+last on purpose (file name), and independent of the other tests' state.
 """
 from __future__ import annotations
 
@@ -20,7 +24,7 @@ import torch
 from freemoe_b200._lib import MOE_NOALLOC_SCRATCH_BYTES, MoeArgs
 from oracle.oracle import TYPE_Q4_K, TYPE_Q8_0, bf16_round
 
-TOL = 1e-3  # the MoE-block bar of the other GPU tests
+GATING_SIGMOID = 1  # FM_GATING_SIGMOID
 
 
 def make_block(oracle, seed, t, E=8, k=2, d=512, ffn=768, T=5):
@@ -32,36 +36,58 @@ def make_block(oracle, seed, t, E=8, k=2, d=512, ffn=768, T=5):
     return slots, x, logits, dict(E=E, k=k, d=d, ffn=ffn, T=T)
 
 
-def args_for(cuda, slots, x, logits, cfg, t, y):
+def args_for(cuda, slots, x, logits, cfg, t, y, router=None):
     gate_bytes = cuda.row_bytes(t, cfg["d"]) * cfg["ffn"]
     table = cuda.slot_table(slots, x.device)
     a = cuda.moe_args(x, logits, table, experts=cfg["E"], top_k=cfg["k"], d_model=cfg["d"], ffn=cfg["ffn"],
-                      gate_type=t, up_type=t, down_type=t, up_offset=gate_bytes, down_offset=2 * gate_bytes, y=y)
+                      gate_type=t, up_type=t, down_type=t, up_offset=gate_bytes, down_offset=2 * gate_bytes, y=y,
+                      router=router)
     return a, table
+
+
+def run_both(cuda, lib, slots, x, logits, cfg, t, router=None):
+    """The block through fmcuda_moe_block and through fmcuda_moe_block_noalloc."""
+    from freemoe_b200._lib import check
+
+    y_ref = torch.empty(cfg["T"], cfg["d"], device="cuda")
+    y_new = torch.full((cfg["T"], cfg["d"]), float("nan"), device="cuda")
+    a_ref, keep_ref = args_for(cuda, slots, x, logits, cfg, t, y_ref, router)
+    need = cuda.moe_workspace_bytes(cfg["T"], cfg["E"], cfg["k"], cfg["d"], cfg["ffn"])
+    assert need <= MOE_NOALLOC_SCRATCH_BYTES
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    check(lib.fmcuda_moe_block(C.byref(a_ref), C.c_void_p(ws.data_ptr()), need, None))
+    a_new, keep_new = args_for(cuda, slots, x, logits, cfg, t, y_new, router)
+    check(lib.fmcuda_moe_block_noalloc(C.byref(a_new), None))
+    torch.cuda.synchronize()
+    assert cuda.device_status() == 0
+    return y_ref.cpu().numpy(), y_new.cpu().numpy()
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("t", [TYPE_Q4_K, TYPE_Q8_0])
 def test_noalloc_matches_workspace_entry_point(cuda, oracle, t):
-    from freemoe_b200._lib import check, load
+    from freemoe_b200._lib import load
 
     lib = load()
-    for call, seed in enumerate((101, 202)):  # two calls in a row, different inputs
-        slots, x, logits, cfg = make_block(oracle, seed + t, t, T=5 + 4 * call)
-        y_ref = torch.empty(cfg["T"], cfg["d"], device="cuda")
-        y_new = torch.full((cfg["T"], cfg["d"]), float("nan"), device="cuda")
-        a_ref, keep_ref = args_for(cuda, slots, x, logits, cfg, t, y_ref)
-        need = cuda.moe_workspace_bytes(cfg["T"], cfg["E"], cfg["k"], cfg["d"], cfg["ffn"])
-        ws = torch.empty(need, dtype=torch.uint8, device="cuda")
-        check(lib.fmcuda_moe_block(C.byref(a_ref), C.c_void_p(ws.data_ptr()), need, None))
-        a_new, keep_new = args_for(cuda, slots, x, logits, cfg, t, y_new)
-        check(lib.fmcuda_moe_block_noalloc(C.byref(a_new), None))
+    # a tokens = 0 call looks the scratch up and does nothing else
+    empty = MoeArgs()
+    assert lib.fmcuda_moe_block_noalloc(C.byref(empty), None) == 0
+    free_before = None
+    # two calls in a row through the single-launch front end, then a call with
+    # more tokens than it takes and a call with a router variant (both through
+    # the separate router / grouping / x-plane kernels)
+    router = cuda.router_config(gating=GATING_SIGMOID, groups=4, groups_used=2)
+    for call, (seed, T, rt) in enumerate(((101, 5, None), (202, 9, None), (303, 70, None), (404, 12, router))):
+        slots, x, logits, cfg = make_block(oracle, seed + t, t, T=T)
         torch.cuda.synchronize()
-        assert cuda.device_status() == 0
-        ref, got = y_ref.cpu().numpy(), y_new.cpu().numpy()
+        if call == 1:
+            free_before = torch.cuda.mem_get_info()[0]
+        ref, got = run_both(cuda, lib, slots, x, logits, cfg, t, rt)
+        if call == 1:
+            # the scratch was mapped by the first call: this one moved no device memory
+            assert torch.cuda.mem_get_info()[0] == free_before
         assert np.isfinite(got).all()
-        err = float(np.max(np.abs(got - ref)) / np.max(np.abs(ref)))
-        assert err <= TOL, f"call {call}: {err}"
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"call {call} differs"
 
 
 @pytest.mark.gpu
