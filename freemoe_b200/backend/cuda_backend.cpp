@@ -2,6 +2,7 @@
 #include "cuda_backend.hpp"
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <thread>
@@ -25,6 +26,12 @@ bool device_tag(fm::AllocationTag tag) {
     return tag == fm::AllocationTag::Weights || tag == fm::AllocationTag::ExpertCache;
 }
 
+// Every live CudaBackend, for the link-time engine hooks that map a raw
+// pointer back to the backend that owns it.
+std::mutex g_registry_mutex;
+std::vector<CudaBackend *> g_registry;
+std::atomic<int> g_registry_size{0};
+
 } // namespace
 
 struct StagingSlot {
@@ -46,8 +53,12 @@ struct Runtime {
     void *dev_io = nullptr;
     uint64_t dev_io_bytes = 0;
     std::vector<void *> free_events;
-    std::mutex mutex;
-    std::map<uintptr_t, uint64_t> device_ranges;
+    mutable std::mutex mutex;
+    struct Range {
+        uint64_t bytes;
+        bool host_readable; // managed (Weights) vs plain HBM (ExpertCache)
+    };
+    std::map<uintptr_t, Range> device_ranges;
     fmcuda_device_info dev_info{};
 
     ~Runtime() {
@@ -114,10 +125,26 @@ CudaBackend::CudaBackend(fm::BackendConfig config, fm::TraceWriter *trace, int d
         fields.set("matvec_order", static_cast<int64_t>(matvec_order_));
         trace_->event("backend_init", std::move(fields));
     }
+    std::lock_guard<std::mutex> lock(g_registry_mutex);
+    g_registry.push_back(this);
+    g_registry_size.store(static_cast<int>(g_registry.size()));
 }
 
 CudaBackend::~CudaBackend() {
+    {
+        std::lock_guard<std::mutex> lock(g_registry_mutex);
+        g_registry.erase(std::remove(g_registry.begin(), g_registry.end(), this), g_registry.end());
+        g_registry_size.store(static_cast<int>(g_registry.size()));
+    }
     for (auto &kv : fence_events_) fmcuda_event_destroy(kv.second);
+}
+
+CudaBackend *CudaBackend::owner_of(const void *p, bool *host_readable) {
+    if (g_registry_size.load(std::memory_order_relaxed) == 0 || !p) return nullptr;
+    std::lock_guard<std::mutex> lock(g_registry_mutex);
+    for (CudaBackend *b : g_registry)
+        if (b->owns_device_pointer(p, host_readable)) return b;
+    return nullptr;
 }
 
 fm::DeviceInfo CudaBackend::info() const {
@@ -143,8 +170,10 @@ std::unique_ptr<fm::DeviceBuffer> CudaBackend::allocate(uint64_t bytes, fm::Allo
     if (bytes == 0) fm::fail(fm::ErrorCode::INVALID_ARGUMENT, "zero-byte allocation");
     void *ptr = nullptr;
     const bool on_device = device_tag(tag);
+    const bool host_readable = tag != fm::AllocationTag::ExpertCache;
     if (on_device) {
-        check(fmcuda_malloc_managed(bytes, &ptr), "HBM allocation");
+        if (host_readable) check(fmcuda_malloc_managed(bytes, &ptr), "HBM allocation");
+        else check(fmcuda_malloc(bytes, &ptr), "HBM expert slot allocation");
     } else {
         check(fmcuda_host_alloc(bytes, &ptr), "pinned host allocation");
         std::memset(ptr, 0, static_cast<size_t>(bytes));
@@ -158,7 +187,7 @@ std::unique_ptr<fm::DeviceBuffer> CudaBackend::allocate(uint64_t bytes, fm::Allo
     auto rt = rt_;
     if (on_device) {
         std::lock_guard<std::mutex> lock(rt->mutex);
-        rt->device_ranges[reinterpret_cast<uintptr_t>(ptr)] = bytes;
+        rt->device_ranges[reinterpret_cast<uintptr_t>(ptr)] = Runtime::Range{bytes, host_readable};
     }
     buffer->cleanup = [tracker, rt, id = buffer->allocation_id, ptr, on_device]() {
         // The runtime (streams, staging) outlives every buffer it served.
@@ -178,13 +207,15 @@ std::unique_ptr<fm::DeviceBuffer> CudaBackend::allocate(uint64_t bytes, fm::Allo
     return buffer;
 }
 
-bool CudaBackend::owns_device_pointer(const void *p) const {
+bool CudaBackend::owns_device_pointer(const void *p, bool *host_readable) const {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
     std::lock_guard<std::mutex> lock(rt_->mutex);
     auto it = rt_->device_ranges.upper_bound(a);
     if (it == rt_->device_ranges.begin()) return false;
     --it;
-    return a < it->first + it->second;
+    if (a >= it->first + it->second.bytes) return false;
+    if (host_readable) *host_readable = it->second.host_readable;
+    return true;
 }
 
 fm::Fence CudaBackend::upload(fm::DeviceBuffer &buffer, const void *src, uint64_t bytes) {
@@ -335,13 +366,26 @@ void CudaBackend::matvec_quant(uint32_t type_id, const uint8_t *weights, const f
                       out_dim, in_dim, s),
           "quantised matvec " + op_name);
     check(fmcuda_download(y, dio + yoff, yb, s), "quantised matvec output");
-    record_operation({op_name, name(), fmcuda_row_bytes(type_id, in_dim) * out_dim + xb, yb});
+    if (!op_name.empty()) record_operation({op_name, name(), fmcuda_row_bytes(type_id, in_dim) * out_dim + xb, yb});
 }
 
 void CudaBackend::download(const fm::DeviceBuffer &buffer, void *dst, uint64_t bytes) {
     if (bytes > buffer.bytes) fm::fail(fm::ErrorCode::INVALID_ARGUMENT, "download past the buffer");
+    download_range(dst, buffer.data, bytes);
+}
+
+void CudaBackend::download_range(void *dst, const void *src, uint64_t bytes) {
+    if (fault_ == fm::BackendFault::DeviceLoss) fm::fail(fm::ErrorCode::DEVICE_LOSS, "injected CUDA device loss");
     check(fmcuda_stream_sync(rt_->upload_stream), "upload drain");
-    check(fmcuda_download(dst, buffer.data, bytes, rt_->compute_stream), "slot read-back");
+    check(fmcuda_download(dst, src, bytes, rt_->compute_stream), "slot read-back");
+    record_control("slot_readback", bytes, bytes, name());
+}
+
+void CudaBackend::upload_range(void *dst, const void *src, uint64_t bytes) {
+    if (fault_ == fm::BackendFault::DeviceLoss) fm::fail(fm::ErrorCode::DEVICE_LOSS, "injected CUDA device loss");
+    check(fmcuda_stream_sync(rt_->upload_stream), "upload drain");
+    check(fmcuda_upload_async(dst, src, bytes, rt_->compute_stream, nullptr), "host-to-device copy");
+    check(fmcuda_stream_sync(rt_->compute_stream), "host-to-device copy");
 }
 
 std::unique_ptr<fm::Backend> make_cuda_backend(const fm::BackendConfig &config, fm::TraceWriter *trace) {

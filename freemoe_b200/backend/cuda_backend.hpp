@@ -8,10 +8,16 @@
 // and the CLI see the same typed errors as from the CPU backends.
 //
 // Memory placement:
-//   Weights, ExpertCache   HBM (managed, preferred location = the device):
+//   ExpertCache            plain HBM (cudaMalloc): the residency manager's
+//                          expert slots.  Only the device reads them; the
+//                          slot read-back for checksums goes through
+//                          download(), the quantised expert GEMVs through
+//                          matvec_quant() (engine_hooks.cpp routes the
+//                          unchanged engine's calls there).
+//   Weights                HBM (managed, preferred location = the device):
 //                          the GEMVs read them on the device; the unchanged
-//                          engine also reads them on the host (token embedding
-//                          rows, slot read-back for checksums).
+//                          engine also reads some on the host (token embedding
+//                          rows, norm scales).
 //   KV, Workspace, Staging,
 //   Other                  pinned host memory: the parts of forward_token that
 //                          stay on the CPU (attention, norms) use them.
@@ -53,14 +59,22 @@ public:
 
     // Quantised product on the device, the GEMV that Engine::matvec_view runs
     // on the CPU for block types (src/engine.cpp:360-367): W lives in a
-    // buffer of this backend, x and y are host vectors.
+    // buffer of this backend, x and y are host vectors.  An empty op_name
+    // records nothing (the caller records the operation itself).
     void matvec_quant(uint32_t type_id, const uint8_t *weights, const float *x, float *y,
                       uint32_t out_dim, uint32_t in_dim, const std::string &op_name);
     // Copies device bytes back to the host (the slot read-back of
     // src/residency.cpp:703-714 without touching managed pages on the host).
     void download(const fm::DeviceBuffer &buffer, void *dst, uint64_t bytes);
-    // True when `p` points into memory this backend allocated on the device.
-    bool owns_device_pointer(const void *p) const;
+    // The same for any range inside one of this backend's device buffers.
+    void download_range(void *dst, const void *src, uint64_t bytes);
+    // Synchronous host -> device copy into one of this backend's device buffers.
+    void upload_range(void *dst, const void *src, uint64_t bytes);
+    // True when `p` points into memory this backend allocated on the device;
+    // *host_readable says whether the host may also read it (managed memory).
+    bool owns_device_pointer(const void *p, bool *host_readable = nullptr) const;
+    // The live CUDA backend whose device memory holds `p` (NULL if none).
+    static CudaBackend *owner_of(const void *p, bool *host_readable = nullptr);
 
 private:
     std::shared_ptr<Runtime> rt_;

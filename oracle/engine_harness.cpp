@@ -17,12 +17,19 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <functional>
+#include <map>
+#include <memory>
 #include <random>
 #include <string>
 #include <vector>
 
+#include "fm/backend.hpp"
 #include "fm/common.hpp"
 #include "fm/engine.hpp"
+#include "fm/gguf.hpp"
+#include "fm/io.hpp"
+#include "fm/residency.hpp"
 
 namespace {
 
@@ -253,7 +260,7 @@ int fme_run(const char *path, int backend, int scalar_kernels, const uint8_t *pr
         cfg.backend.kind = backend == 2 ? fm::BackendKind::PhysicalGPU : fm::BackendKind::ScalarCPU;
         if (scalar_kernels) cfg.backend.kernel_isa = fm::KernelIsa::Scalar;
         cfg.backend.kernel_threads = 1;
-        cfg.budget.requested_slots = cache_slots;
+        cfg.cache_slots = cache_slots; // Engine copies it into budget.requested_slots (src/engine.cpp:146)
         cfg.t_wait_ms = 5000;
         fm::Engine engine(cfg);
         engine.initialize();
@@ -281,6 +288,256 @@ int fme_run(const char *path, int backend, int scalar_kernels, const uint8_t *pr
         g_error = e.what();
         return static_cast<int>(e.code);
     }
+}
+
+} // extern "C"
+
+namespace {
+
+fm::Json backend_ops_summary(const fm::Backend &backend) {
+    // operation count per executing backend label, and the quantised GEMV
+    // records (the engine labels CPU ones "cpu-quant")
+    std::map<std::string, int64_t> by_backend;
+    int64_t expert_ops = 0, expert_ops_device = 0;
+    for (const auto &op : backend.operations()) {
+        ++by_backend[op.backend];
+        if (op.name.rfind("expert_", 0) == 0 && op.name.rfind("expert_swiglu", 0) != 0 &&
+            op.name.rfind("expert_combine", 0) != 0 && op.name.rfind("expert_proj_bias", 0) != 0) {
+            ++expert_ops;
+            if (op.backend == backend.name()) ++expert_ops_device;
+        }
+    }
+    fm::Json j = fm::Json::object();
+    for (const auto &kv : by_backend) j.set(kv.first, kv.second);
+    fm::Json out = fm::Json::object();
+    out.set("by_backend", std::move(j));
+    out.set("expert_gemvs", expert_ops);
+    out.set("expert_gemvs_on_backend", expert_ops_device);
+    out.set("backend", backend.name());
+    return out;
+}
+
+} // namespace
+
+extern "C" {
+
+// Engine::compare_reference (src/engine.cpp:2490-2578) over `prompts` prompts
+// of `reference_root` with `tokens` greedy tokens each, on the CPU (backend 0)
+// or GPU (2) backend: the comparison as JSON plus the operation summary.
+int fme_compare(const char *path, int backend, const char *reference_root, uint32_t prompts, uint32_t tokens,
+                uint32_t cache_slots, char *json_out, uint32_t json_cap) {
+    try {
+        fm::RunConfig cfg;
+        cfg.model_path = path;
+        cfg.backend.kind = backend == 2 ? fm::BackendKind::PhysicalGPU : fm::BackendKind::ScalarCPU;
+        cfg.backend.kernel_threads = 1;
+        cfg.cache_slots = cache_slots;
+        cfg.t_wait_ms = 5000;
+        cfg.reference_root = reference_root;
+        fm::Engine engine(cfg);
+        engine.initialize();
+        const fm::ComparisonResult c = engine.compare_reference(reference_root, prompts, tokens);
+        fm::Json j = fm::Json::object();
+        j.set("comparison", c.to_json());
+        j.set("ops", backend_ops_summary(engine.backend()));
+        if (engine.residency()) j.set("residency", engine.residency()->metrics_json());
+        const std::string m = j.dump();
+        std::snprintf(json_out, json_cap, "%s", m.c_str());
+        engine.release_runtime();
+        return 0;
+    } catch (const fm::Error &e) {
+        g_error = e.what();
+        return static_cast<int>(e.code);
+    }
+}
+
+// The residency manager's slot and fault semantics (the reference's own unit
+// harness, tests/unit/tests.cpp:794-882) on the backend of `backend` (0 CPU,
+// 2 GPU), over the model at `path`.  Writes {"checks": [[name, ok], ...]}.
+int fme_residency_faults(const char *path, int backend, char *json_out, uint32_t json_cap) {
+    fm::Json checks = fm::Json::array();
+    auto check = [&](bool ok, const std::string &name) {
+        fm::Json row = fm::Json::array();
+        row.push(fm::Json::string(name));
+        row.push(fm::Json::boolean(ok));
+        checks.push(std::move(row));
+    };
+    auto throws_code = [](fm::ErrorCode code, const std::function<void()> &fn) {
+        try {
+            fn();
+        } catch (const fm::Error &e) {
+            return e.code == code;
+        }
+        return false;
+    };
+    struct Fixture {
+        std::string path;
+        std::unique_ptr<fm::MappedFile> file;
+        fm::GGUFDocument doc;
+        fm::ModelManifest manifest;
+        std::unique_ptr<fm::TraceWriter> trace;
+        std::unique_ptr<fm::Backend> backend;
+        std::unique_ptr<fm::ReadScheduler> scheduler;
+        fm::BudgetResult budget;
+        fm::ResidencyConfig residency_config;
+        std::unique_ptr<fm::ResidencyManager> manager;
+        Fixture(const std::string &p, int kind, uint32_t slots, fm::ReplacementPolicy policy, uint32_t t_wait_ms)
+            : path(p) {
+            file = std::make_unique<fm::MappedFile>(path);
+            doc = fm::parse_gguf(file->data(), file->size());
+            manifest = fm::build_manifest(doc, path);
+            trace = std::make_unique<fm::TraceWriter>("");
+            fm::BackendConfig backend_config;
+            backend_config.kind = kind == 2 ? fm::BackendKind::PhysicalGPU : fm::BackendKind::ScalarCPU;
+            backend = fm::Backend::create(backend_config);
+            fm::SchedulerConfig scheduler_config;
+            scheduler_config.mode = fm::ReaderMode::Buffered;
+            scheduler_config.path = path;
+            scheduler_config.expected_identity = file->identity();
+            scheduler_config.queue_depth = 2;
+            scheduler_config.coalesce_gap = 4096;
+            scheduler = std::make_unique<fm::ReadScheduler>(
+                scheduler_config, fm::make_reader(fm::ReaderMode::Buffered, path, nullptr, false), trace.get());
+            fm::BudgetConfig budget_config;
+            budget_config.requested_slots = slots;
+            budget = fm::compute_budget(manifest, budget_config, backend->info());
+            residency_config.replacement = policy;
+            residency_config.enable_prefetch = false;
+            residency_config.t_wait_ms = t_wait_ms;
+            manager = std::make_unique<fm::ResidencyManager>(manifest, *backend, *scheduler, *trace, budget,
+                                                             residency_config);
+            manager->initialize();
+        }
+    };
+    try {
+        using fm::SlotState;
+        {
+            Fixture f(path, backend, 1, fm::ReplacementPolicy::LRU, 1);
+            check(f.manager->slots().size() == 1, "one-slot pool allocated");
+            check(f.manager->inject_stale_completion(0, 999), "stale completion is detectable");
+            check(f.manager->metrics().stale_completions == 1, "stale completion counter increments");
+            check(f.manager->slots()[0].state == SlotState::ABSENT, "stale completion leaves slot unchanged");
+            fm::SlotHandle first = f.manager->acquire(0, 0, 0);
+            check(static_cast<bool>(first), "first expert acquisition returns slot data");
+            check(!f.manager->try_evict(0), "eviction of referenced slot is refused");
+            first.release();
+            check(f.manager->slots()[0].state == SlotState::GPU_READY, "release returns slot to GPU_READY");
+            fm::SlotHandle second = f.manager->acquire(0, 1, 1);
+            second.release();
+            check(f.manager->metrics().evictions == 1, "second expert evicts LRU victim");
+            check(f.manager->metrics().checksum_checks >= 4, "source and slot checksums are checked");
+            bool all = true;
+            for (uint32_t layer = 0; layer < f.manifest.config.layers; ++layer)
+                for (uint32_t expert = 0; expert < f.manifest.config.expert_count; ++expert) {
+                    fm::SlotHandle handle = f.manager->acquire(layer, expert, 10 + layer * 100 + expert);
+                    all = all && static_cast<bool>(handle);
+                }
+            check(all, "all experts cycle through one-slot pool");
+            check(f.manager->metrics().checksum_failures == 0, "no checksum failures during expert cycle");
+            check(f.manager->metrics().invalid_transitions == 0, "no invalid state transitions");
+            check(f.manager->metrics().cache_misses >= f.manifest.config.layers * f.manifest.config.expert_count,
+                  "every expert demand miss is counted");
+            if (backend == 2) {
+                bool on_device = false;
+                for (const auto &op : f.backend->operations())
+                    if (op.name == "upload" && op.backend == f.backend->name()) on_device = true;
+                check(on_device, "CUDA backend: slot uploads ran on the device");
+            }
+        }
+        {
+            Fixture f(path, backend, 1, fm::ReplacementPolicy::LRU, 1);
+            f.manager->pin_slot_for_test(0);
+            check(throws_code(fm::ErrorCode::SLOTS_BUSY, [&]() { (void)f.manager->acquire(0, 0, 0); }),
+                  "all-slots-busy returns SLOTS_BUSY after wait deadline");
+            check(f.manager->metrics().slots_busy_events == 1, "slots busy event recorded");
+            f.manager->unpin_slot_for_test(0);
+        }
+        {
+            Fixture f(path, backend, 2, fm::ReplacementPolicy::Clock, 1);
+            f.manager->unpin_slot_for_test(0);
+            f.manager->unpin_slot_for_test(1);
+            f.manager->slots()[0].key = fm::ModelManifest::expert_key(0, 0);
+            f.manager->slots()[1].key = fm::ModelManifest::expert_key(0, 1);
+            f.manager->slots()[0].last_used = 1;
+            f.manager->slots()[1].last_used = 2;
+            f.manager->set_clock_bits_for_test({1, 0});
+            fm::Slot *victim = f.manager->select_victim_for_test(10);
+            check(victim && victim->index == 1, "clock victim sequence matches test vector");
+            f.manager->set_clock_bits_for_test({0, 0});
+            victim = f.manager->select_victim_for_test(11);
+            check(victim && victim->index == 0, "clock hand advances to next victim");
+        }
+        {
+            Fixture f(path, backend, 1, fm::ReplacementPolicy::LRU, 1);
+            fm::Slot &slot = f.manager->slots()[0];
+            slot.state = SlotState::UPLOAD_QUEUED;
+            slot.generation = 7;
+            slot.fence = fm::Fence{1, fm::now_ms() + 3600000ull, true};
+            check(!f.manager->complete_upload(0, 7), "deferred fence keeps slot in UPLOAD_QUEUED");
+            check(slot.state == SlotState::UPLOAD_QUEUED, "deferred fence does not publish slot");
+            slot.fence.deferred = false;
+            slot.fence.ready_at_ms = 0;
+            check(f.manager->complete_upload(0, 7), "fence completion publishes GPU_READY");
+            check(slot.state == SlotState::GPU_READY, "published slot state is GPU_READY");
+            check(!f.manager->complete_upload(0, 8), "generation mismatch is rejected");
+        }
+        {
+            Fixture f(path, backend, 1, fm::ReplacementPolicy::LRU, 1);
+            f.backend->inject_fault(fm::BackendFault::TransferFailure);
+            check(throws_code(fm::ErrorCode::TRANSFER_FAILED, [&]() { (void)f.manager->acquire(0, 0, 0); }),
+                  "transfer failure is propagated with typed code");
+            check(f.manager->metrics().transfer_failures == 1, "transfer failure metric recorded");
+            f.manager->reset_errors_for_test();
+            f.backend->inject_fault(fm::BackendFault::FenceTimeout);
+            check(throws_code(fm::ErrorCode::FENCE_TIMEOUT, [&]() { (void)f.manager->acquire(0, 0, 1); }),
+                  "fence timeout is propagated with typed code");
+            check(f.manager->metrics().fence_timeouts == 1, "fence timeout metric recorded");
+            f.manager->reset_errors_for_test();
+            fm::SlotHandle handle = f.manager->acquire(0, 0, 2);
+            handle.release();
+            f.manager->inject_device_loss();
+            check(f.manager->slots()[0].state == SlotState::ERROR, "device loss invalidates live slot");
+            check(f.manager->metrics().device_loss_events >= 1, "device loss metric recorded");
+            // beyond the reference's checks: while the backend reports the
+            // device lost it refuses the next load with DEVICE_LOSS; once the
+            // faults are cleared the slot loads and verifies again
+            f.manager->reset_errors_for_test();
+            f.backend->inject_fault(fm::BackendFault::DeviceLoss);
+            check(throws_code(fm::ErrorCode::DEVICE_LOSS, [&]() { (void)f.manager->acquire(0, 1, 3); }),
+                  "a lost device refuses the next load with DEVICE_LOSS");
+            f.manager->reset_errors_for_test();
+            fm::SlotHandle again = f.manager->acquire(0, 1, 4);
+            check(static_cast<bool>(again), "after the faults are cleared the slot loads again");
+            again.release();
+            check(f.manager->metrics().checksum_failures == 0, "no checksum failures across the fault sequence");
+        }
+        if (backend == 2) {
+            // a deferred fence through the CUDA backend itself (the CPU
+            // backend ignores this fault): upload with the fault armed, then
+            // advance_fences() releases it
+            Fixture f(path, backend, 1, fm::ReplacementPolicy::LRU, 1);
+            auto buf = f.backend->allocate(4096, fm::AllocationTag::ExpertCache);
+            std::vector<uint8_t> bytes(4096, 7);
+            f.backend->inject_fault(fm::BackendFault::FenceDeferred);
+            fm::Fence fence = f.backend->upload(*buf, bytes.data(), bytes.size());
+            check(fence.deferred && !f.backend->fence_complete(fence),
+                  "CUDA backend: an injected deferral keeps the fence pending");
+            check(throws_code(fm::ErrorCode::FENCE_TIMEOUT, [&]() { f.backend->wait_fence(fence, 5); }),
+                  "CUDA backend: waiting on a deferred fence times out with FENCE_TIMEOUT");
+            f.backend->advance_fences();
+            check(f.backend->fence_complete(fence), "CUDA backend: advance_fences completes a deferred fence");
+            f.backend->wait_fence(fence, 1000);
+            check(true, "CUDA backend: the released fence waits without error");
+        }
+    } catch (const fm::Error &e) {
+        g_error = e.what();
+        check(false, std::string("unexpected error: ") + e.what());
+    }
+    fm::Json j = fm::Json::object();
+    j.set("checks", std::move(checks));
+    const std::string m = j.dump();
+    std::snprintf(json_out, json_cap, "%s", m.c_str());
+    return 0;
 }
 
 } // extern "C"

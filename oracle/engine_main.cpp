@@ -6,6 +6,8 @@
 //
 //   fm_engine write-tiny PATH [SEED]
 //   fm_engine run PATH cpu|gpu PROMPT_HEX N_GEN SLOTS SCALAR(0|1) OUT.bin
+//   fm_engine compare PATH cpu|gpu REFERENCE_ROOT PROMPTS TOKENS SLOTS   (JSON on stdout)
+//   fm_engine residency PATH cpu|gpu                                   (JSON on stdout)
 //
 // OUT.bin: u32 n_ids, i32 ids[n]; u32 n_logits, f32 logits[n];
 //          u32 n_routing, u32 routing[n]; u32 n_json, char json[n].
@@ -25,6 +27,9 @@ int fme_run(const char *path, int backend, int scalar_kernels, const uint8_t *pr
             uint32_t n_gen, uint32_t cache_slots, int32_t *ids_out, uint32_t ids_cap, uint32_t *n_ids,
             float *logits_out, uint32_t logits_cap, uint32_t *n_logits, uint32_t *routing_out,
             uint32_t routing_cap, uint32_t *n_routing, char *metrics_out, uint32_t metrics_cap);
+int fme_compare(const char *path, int backend, const char *reference_root, uint32_t prompts, uint32_t tokens,
+                uint32_t cache_slots, char *json_out, uint32_t json_cap);
+int fme_residency_faults(const char *path, int backend, char *json_out, uint32_t json_cap);
 }
 
 int main(int argc, char **argv) {
@@ -73,6 +78,31 @@ int main(int argc, char **argv) {
         std::fclose(f);
         return 0;
     }
-    std::fprintf(stderr, "usage: fm_engine write-tiny PATH [SEED] | run PATH cpu|gpu HEX N SLOTS SCALAR OUT\n");
+    if (argc == 8 && std::strcmp(argv[1], "compare") == 0) {
+        std::vector<char> json(1 << 22);
+        const int rc = fme_compare(argv[2], std::strcmp(argv[3], "gpu") == 0 ? 2 : 0, argv[4],
+                                   static_cast<uint32_t>(std::atoi(argv[5])), static_cast<uint32_t>(std::atoi(argv[6])),
+                                   static_cast<uint32_t>(std::atoi(argv[7])), json.data(),
+                                   static_cast<uint32_t>(json.size()));
+        if (rc) {
+            std::fprintf(stderr, "compare failed (%d): %s\n", rc, fme_last_error());
+            return rc;
+        }
+        std::printf("%s\n", json.data());
+        return 0;
+    }
+    if (argc == 4 && std::strcmp(argv[1], "residency") == 0) {
+        std::vector<char> json(1 << 20);
+        const int rc = fme_residency_faults(argv[2], std::strcmp(argv[3], "gpu") == 0 ? 2 : 0, json.data(),
+                                            static_cast<uint32_t>(json.size()));
+        if (rc) {
+            std::fprintf(stderr, "residency failed (%d): %s\n", rc, fme_last_error());
+            return rc;
+        }
+        std::printf("%s\n", json.data());
+        return 0;
+    }
+    std::fprintf(stderr, "usage: fm_engine write-tiny PATH [SEED] | run PATH cpu|gpu HEX N SLOTS SCALAR OUT | "
+                         "compare PATH cpu|gpu REFROOT PROMPTS TOKENS SLOTS | residency PATH cpu|gpu\n");
     return 2;
 }
