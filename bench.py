@@ -65,6 +65,44 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
+def stack_config(type_name: str, tokens: int, world: int) -> dict:
+    """The headline workload's config, one dict for both arms (same keys, same
+    strings), so that the two JSON lines name the same configuration."""
+    t = TYPES[type_name]
+    mb = EXPERTS * expert_bytes(t) / 1e6
+    return {"workload": f"{type_name} 8-expert stack [{FFN}x{D_MODEL}]x2+[{D_MODEL}x{FFN}], "
+                        f"T={tokens} bf16 tokens, top-8 of 8", "tokens": tokens,
+            "parallelism": f"ep{world}",
+            "l2": f"inputs larger than L2 ({mb:.1f} MB {type_name.upper()} stack vs 126 MB L2)"}
+
+
+def host_cpu() -> dict:
+    """The host CPU the baseline ran on: model name and the vector extensions
+    the reference's kernels can use, plus the ISA the reference itself resolved
+    (fm::resolved_isa) when its compiled code is present."""
+    model, flags = None, set()
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if model is None and line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                elif not flags and line.startswith("flags"):
+                    flags = set(line.split(":", 1)[1].split())
+                if model and flags:
+                    break
+    except OSError:
+        pass
+    out = {"cpu_model": model, "cpu_flags": [f for f in ("avx2", "fma", "f16c", "avx512f") if f in flags]}
+    try:
+        from oracle.oracle import Reference, reference_available
+
+        if reference_available():
+            out["isa"] = Reference().isa()
+    except Exception:  # noqa: BLE001 - the ISA is informative only
+        pass
+    return out
+
+
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
 
@@ -169,6 +207,58 @@ def pipelined_e2e(call, hx, hl, like_x, like_l, like_y, steps, stream):
     e1.record(stream)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps, hy[(steps - 1) & 1]
+
+
+def report_stages(stage_ms: dict, tokens: int, experts: int = EXPERTS) -> dict:
+    """Per-stage device times of one decode MoE block.  Up to 64 tokens and 64
+    experts (plain router) the router, grouping and x planes are one launch and
+    the down projection's x planes are written by the gate/up epilogue, so the
+    library's events between those stages time nothing: report the launches."""
+    if tokens <= 64 and experts <= 64:
+        return {"front": stage_ms["router"] + stage_ms["grouping"] + stage_ms["x_planes"],
+                "gate_up": stage_ms["gate_up"] + stage_ms["act_planes"], "down": stage_ms["down"],
+                "combine": stage_ms["combine"]}
+    return dict(stage_ms)
+
+
+# Further configurations measured by the default run after the headline, each
+# in a child process of its own (BASELINE configs[1] in Q8_0 and at T = 1, the
+# Mixtral-shaped decode layer at T = 1, 4, 16, 64, the DeepSeek- and
+# Qwen3-shaped prefill layers); their lines are attached under "configs".
+EXTRA_RUNS = (
+    ("stack_q8_0_T8", ["--type", "q8_0"]),
+    ("stack_q4_k_T1", ["--tokens", "1"]),
+    ("mixtral_T1", ["--config", "mixtral", "--tokens", "1"]),
+    ("mixtral_T4", ["--config", "mixtral", "--tokens", "4"]),
+    ("mixtral_T16", ["--config", "mixtral", "--tokens", "16"]),
+    ("mixtral_T64", ["--config", "mixtral", "--tokens", "64"]),
+    ("deepseek_prefill_T4096", ["--config", "deepseek"]),
+    ("qwen3_prefill_T8192", ["--config", "qwen3"]),
+)
+EXTRA_KEYS = ("metric", "value", "unit", "ms_per_step", "dtype", "config", "stage_ms", "roofline", "e2e",
+              "cpu_baseline", "hbm_gbs", "tokens_per_s", "gpu_launches", "clocks", "steps", "warmup")
+
+
+def run_extras(args) -> dict:
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT")}
+    out = {}
+    for name, extra in EXTRA_RUNS:
+        cmd = [sys.executable, str(Path(__file__).resolve()), "--steps", str(args.extra_steps), "--warmup", "3",
+               "--no-extras", "--cpu-seconds", "3", *(["--no-cpu"] if args.no_cpu else []), *extra]
+        try:
+            p = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=str(ROOT))
+        except subprocess.TimeoutExpired:
+            out[name] = {"error": "timed out after 600 s"}
+            continue
+        lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+        if p.returncode or not lines:
+            tail = (p.stderr or p.stdout).strip().splitlines()[-3:]
+            out[name] = {"error": f"exit {p.returncode}: {' | '.join(tail)}"}
+            continue
+        d = json.loads(lines[-1])
+        out[name] = {k: d[k] for k in EXTRA_KEYS if k in d}
+    return out
 
 
 def dist_setup(args):
@@ -290,13 +380,11 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": args.type, "data": "synthetic",
-        "config": {"workload": f"{args.type} 8-expert stack [{FFN}x{D_MODEL}]x2+[{D_MODEL}x{FFN}], "
-                               f"T={args.tokens} bf16 tokens, top-8 of 8", "tokens": args.tokens,
-                   "l2": "inputs larger than L2"},
+        "config": stack_config(args.type, args.tokens, args.gpus),
         "tokens_per_s": args.tokens / (dt * frac),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"{EXPERTS} experts x {args.tokens} tokens, feature rows 0..{ffn - 1} of "
-                                   f"{FFN} per step (full step {t_full * 1e3:.0f} ms)"},
+                                   f"{FFN} per step (full step {t_full * 1e3:.0f} ms)", **host_cpu()},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -441,13 +529,11 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": args.type, "data": "synthetic",
-        "config": {"workload": f"{args.type} 8-expert stack [{FFN}x{D_MODEL}]x2+[{D_MODEL}x{FFN}], "
-                               f"T={T} bf16 tokens, top-8 of 8 (fmcuda_moe_block)", "tokens": T,
-                   "parallelism": f"ep{world} (replicated stack per rank, no exchange)",
-                   "l2": "inputs larger than L2 (792.7 MB Q4_K stack vs 126 MB L2)"},
+        "config": stack_config(args.type, T, world),
+        "entry_point": "fmcuda_moe_block (one call per step)",
         "tokens_per_s": world * T / (ms / 1e3),
         "pct_of_8tbs": value / world / 8000.0 * 100.0,
-        "stage_ms": stage_ms,
+        "stage_ms": report_stages(stage_ms, T),
         "roofline": {"bound": "hbm", "kernel": "qgemv gate/up + SwiGLU (8 experts)", "achieved": gu_achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": gu_achieved / peak,
                      "traffic": traffic, "algorithmic_bytes": gu_bytes,
@@ -465,13 +551,15 @@ def run_ours(args):
         threads = os.cpu_count() or 1
         runner(x_np, lg_np, T, threads)
         n, t0 = 0, time.perf_counter()
-        while n < 3 or (time.perf_counter() - t0 < 10.0 and n < 50):
+        while n < 3 or (time.perf_counter() - t0 < args.cpu_seconds and n < 50):
             runner(x_np, lg_np, T, threads)
             n += 1
         dt = (time.perf_counter() - t0) / n
         line["cpu_baseline"] = {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
                                 "sample": f"{n} full steps ({EXPERTS} experts x {T} tokens), "
-                                          f"{dt * 1e3:.1f} ms each"}
+                                          f"{dt * 1e3:.1f} ms each", **host_cpu()}
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["configs"] = run_extras(args)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -643,7 +731,7 @@ def run_layer(args):
                        "tokens": T, "pairs": pairs, "experts_hit": int((counts > 0).sum()),
                        "max_group": int(counts.max()), "min_group": int(counts.min()),
                        "l2": "expert weights larger than L2"},
-            "stage_ms": stage_ms,
+            "stage_ms": stage_ms if prefill else report_stages(stage_ms, T, E),
             "e2e": {"value": T / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4,
                     "d2h_bytes_per_step": y.numel() * 4, "ms_per_step": ms_e2e},
             "gpu_launches": None, "clocks": clocks.summary()}
@@ -688,7 +776,8 @@ def run_layer(args):
             ref.moe_block(t, host_slots, gb, 2 * gb, x_np[:n_s], ids_r, w_r, d, ffn, threads=threads)
             dt = time.perf_counter() - t0
             line["cpu_baseline"] = {"value": n_s / dt, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                                    "sample": f"{n_s} of the {T} tokens (routed experts only), {dt:.2f} s"}
+                                    "sample": f"{n_s} of the {T} tokens (routed experts only), {dt:.2f} s",
+                                    **host_cpu()}
     print(json.dumps(line), flush=True)
 
 
@@ -1037,7 +1126,7 @@ def run_reference_layer(args):
             "config": {"workload": f"{args.config}: {E} experts d {d} ffn {ffn} top-{k} (routed experts), "
                                    f"{n_s} of T={T} tokens per step", "tokens": n_s},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
-                             "sample": f"{n_s} tokens of the {T}-token batch per step"},
+                             "sample": f"{n_s} tokens of the {T}-token batch per step", **host_cpu()},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -1154,6 +1243,11 @@ def main():
     ap.add_argument("--type", default="q4_k", choices=sorted(TYPES))
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="time budget of the headline's CPU baseline sample")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="measure the headline only (not the further configurations under 'configs')")
+    ap.add_argument("--extra-steps", type=int, default=200, help="timed steps of each further configuration")
     ap.add_argument("--sample", type=int, default=32,
                     help="tokens per step of the reference arm on a layer configuration")
     ap.add_argument("--config", default="stack", choices=["stack", *LAYERS, "gemv", "coldload"],
