@@ -17,6 +17,7 @@
 #include "gemv_async.cuh"
 #include "gemv_kernels.cuh"
 #include "router_core.cuh"
+#include "tgemv_host.h"
 
 namespace fmb {
 
@@ -81,6 +82,7 @@ struct MoeLayout {
     uint64_t xh, xl, xs;
     uint64_t act, ah, al, as;
     uint64_t part;
+    uint64_t tg_img_gu, tg_img_dn, tg_partial, tg_cnt, tg_maps; // tcgen05 expert stage (tgemv.cu)
     uint64_t total;
 };
 
@@ -108,6 +110,12 @@ MoeLayout moe_layout(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t
     L.al = take(P * ffn * 2);
     L.as = take(P * (ffn / 32) * 4);
     L.part = take(P * d * 4);
+    const TgSections tg = tg_sections(tokens, experts, top_k, d, ffn);
+    L.tg_img_gu = take(tg.img_gu);
+    L.tg_img_dn = take(tg.img_dn);
+    L.tg_partial = take(tg.partial);
+    L.tg_cnt = take(tg.cnt);
+    L.tg_maps = take(tg.maps);
     L.total = o;
     return L;
 }
@@ -226,6 +234,43 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     const bool plain_router = !cfg || (cfg->gating == FM_GATING_SOFTMAX && !cfg->logit_bias && !cfg->selection_bias &&
                                        cfg->groups <= 1 && !cfg->epsilon_additive);
     mark(0);
+    if (tg_eligible(a)) {
+        // Q4_K experts, bf16 activations: the tcgen05 expert stage (tgemv.cu)
+        if (plain_router && a->tokens <= kFrontMaxTokens && a->experts <= kFrontMaxExperts) {
+            const int norm = cfg ? cfg->normalise : a->normalise;
+            const double eps = cfg ? cfg->epsilon : a->epsilon, scl = cfg ? cfg->scale : a->scale;
+            // one CTA: router, then grouping (no x planes on this path)
+            moe_front_kernel<__nv_bfloat16><<<1, 1024, 0, s>>>(
+                a->logits, static_cast<const __nv_bfloat16 *>(a->x), a->tokens, a->experts, a->top_k, norm, eps, scl,
+                a->d_model, 0, ids, weights, counts, offsets, pairs, slot_of, nullptr, nullptr, nullptr,
+                device_status_word());
+            if ((rc = check_launch("MoE front launch"))) return rc;
+            mark(1);
+        } else {
+            if ((rc = launch_route_cfg(a->logits, a->tokens, a->experts, a->top_k, a->router, a->normalise,
+                                       a->epsilon, a->scale, ids, weights, nullptr, s)))
+                return rc;
+            mark(1);
+            if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
+        }
+        mark(2);
+        struct MarkCtx {
+            decltype(mark) *fn;
+        } mctx{&mark};
+        rc = tg_expert_stage(
+            a, counts, offsets, pairs, ws + L.tg_img_gu, ws + L.tg_img_dn, reinterpret_cast<float *>(ws + L.tg_partial),
+            reinterpret_cast<uint32_t *>(ws + L.tg_cnt), ws + L.tg_maps, part,
+            [](void *ctx, int i) { (*static_cast<MarkCtx *>(ctx)->fn)(i); }, &mctx, s);
+        if (rc) return rc;
+        if ((rc = launch_combine(part, weights, slot_of, a->tokens, a->top_k, a->d_model, a->y, s))) return rc;
+        mark(7);
+        if (a->ids_out)
+            cudaMemcpyAsync(a->ids_out, ids, static_cast<uint64_t>(P) * 4, cudaMemcpyDeviceToDevice, s);
+        if (a->weights_out)
+            cudaMemcpyAsync(a->weights_out, weights, static_cast<uint64_t>(P) * 4, cudaMemcpyDeviceToDevice, s);
+        if (mark_rc) return mark_rc;
+        return check_launch("MoE output copies");
+    }
     if (plain_router && gu_staged && a->tokens <= kFrontMaxTokens && a->experts <= kFrontMaxExperts) {
         const int norm = cfg ? cfg->normalise : a->normalise;
         const double eps = cfg ? cfg->epsilon : a->epsilon, scl = cfg ? cfg->scale : a->scale;

@@ -1,0 +1,166 @@
+// tgemv.cu -- host side of the tcgen05 decode GEMVs (tgemv.cuh): workspace
+// sections, eligibility and the launch sequence of the MoE block's expert
+// stage for Q4_K experts and bf16 activations.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
+#include "tgemv.cuh"
+#include "tgemv_host.h"
+
+namespace fmb {
+
+namespace {
+
+inline uint64_t a256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+int tg_sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int NMAT> int tg_configure() {
+    static int done = 0;
+    if (!done) {
+        const cudaError_t err = cudaFuncSetAttribute(tgemv_kernel<NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     TgLayout<NMAT>::smem_bytes(TG_MAX_EXPERTS));
+        if (err != cudaSuccess) return cuda_status(err, "tgemv shared-memory attribute");
+        done = 1;
+    }
+    return FM_STATUS_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tg_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        else
+            (void)cudaGetLastError();
+    });
+    return fn;
+}
+
+// Template map of one Q4_K matrix [rows][row_bytes] (uint8), 144-byte x 128-row
+// boxes, no swizzle; the device writes a copy per expert with its own address.
+int tg_template(CUtensorMap *map, const void *any_base, uint32_t row_bytes, uint32_t rows) {
+    auto enc = tg_encoder();
+    if (!enc) return set_error(FM_STATUS_INTERNAL_ERROR, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {TG_RB, TG_ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(any_base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(FM_STATUS_INTERNAL_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    return FM_STATUS_OK;
+}
+
+} // namespace
+
+// Upper bound of token tiles of one block: every expert's last tile may be partial.
+uint32_t tg_max_tiles(uint32_t tokens, uint32_t experts, uint32_t top_k) {
+    const uint64_t P = static_cast<uint64_t>(tokens) * top_k;
+    return static_cast<uint32_t>(P / TG_NT + (P < experts ? P : experts));
+}
+
+bool tg_shape(uint32_t d, uint32_t ffn) { return d % 256 == 0 && ffn % 256 == 0 && d > 0 && ffn > 0; }
+
+TgSections tg_sections(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t d, uint32_t ffn) {
+    TgSections t{};
+    if (!tg_shape(d, ffn)) return t;
+    const uint64_t tiles = tg_max_tiles(tokens, experts, top_k);
+    t.img_gu = a256(tiles * (d / 256) * TG_IMG);
+    t.img_dn = a256(tiles * (ffn / 256) * TG_IMG);
+    t.partial = a256(2ull * TG_MAX_CTAS * 2 * 2 * TG_NT * TG_ROWS * 4);
+    t.cnt = a256(tiles * (ffn / TG_ROWS + d / TG_ROWS) * 4);
+    t.maps = a256(static_cast<uint64_t>(experts) * 3 * sizeof(CUtensorMap) + 256);
+    return t;
+}
+
+bool tg_eligible(const fmcuda_moe_args *a) {
+    return a->gate_type == FM_TYPE_Q4_K && a->up_type == FM_TYPE_Q4_K && a->down_type == FM_TYPE_Q4_K &&
+           a->x_dtype == FM_X_BF16 && tg_shape(a->d_model, a->ffn) && a->experts <= TG_MAX_EXPERTS &&
+           a->up_offset % 16 == 0 && a->down_offset % 16 == 0;
+}
+
+// Steps after routing and grouping: x images, gate/up + SwiGLU (writing the
+// down images), down.  `part` receives one f32 row per grouped pair.
+int tg_expert_stage(const fmcuda_moe_args *a, const uint32_t *counts, const uint32_t *offsets, const uint32_t *pairs,
+                    uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt, uint8_t *maps_area, float *part,
+                    void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
+    int rc;
+    if ((rc = tg_configure<2>())) return rc;
+    if ((rc = tg_configure<1>())) return rc;
+    const uint32_t tiles = tg_max_tiles(a->tokens, a->experts, a->top_k);
+    const uint32_t n_cnt = tiles * (a->ffn / TG_ROWS + a->d_model / TG_ROWS);
+    TgMapArgs ma{};
+    ma.maps = reinterpret_cast<CUtensorMap *>(maps_area + 256);
+    ma.slots = reinterpret_cast<const uint8_t *const *>(a->expert_slots);
+    ma.up_off = a->up_offset;
+    ma.down_off = a->down_offset;
+    ma.cnt = cnt;
+    ma.n_cnt = n_cnt;
+    const uint32_t rb_gu = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, a->d_model));
+    const uint32_t rb_dn = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, a->ffn));
+    if ((rc = tg_template(&ma.tmpl_gu, ma.maps, rb_gu, a->ffn))) return rc;
+    if ((rc = tg_template(&ma.tmpl_dn, ma.maps, rb_dn, a->d_model))) return rc;
+    tg_ximage_kernel<<<tiles * (a->d_model / 256), 256, 0, s>>>(
+        ma, static_cast<const __nv_bfloat16 *>(a->x), a->d_model, counts, offsets, pairs, a->top_k, a->experts,
+        tiles, img_gu);
+    if ((rc = check_launch("tgemv x images"))) return rc;
+    mark(mark_ctx, 3);
+
+    const uint32_t grid = static_cast<uint32_t>(tg_sm_count() < static_cast<int>(TG_MAX_CTAS) ? tg_sm_count()
+                                                                                              : TG_MAX_CTAS);
+    TgParams gu{};
+    gu.slots = ma.slots;
+    gu.w_off0 = 0;
+    gu.w_off1 = a->up_offset;
+    gu.maps = ma.maps;
+    gu.map0 = 0;
+    gu.out_dim = a->ffn;
+    gu.in_dim = a->d_model;
+    gu.experts = a->experts;
+    gu.counts = counts;
+    gu.offsets = offsets;
+    gu.img = img_gu;
+    gu.out_img = img_dn;
+    gu.partial = partial;
+    gu.unit_cnt = cnt;
+    gu.status = device_status_word();
+    tgemv_kernel<2><<<grid, TG_THREADS, TgLayout<2>::smem_bytes(a->experts), s>>>(gu);
+    if ((rc = check_launch("tgemv gate/up"))) return rc;
+    mark(mark_ctx, 4);
+    mark(mark_ctx, 5);
+
+    TgParams dn = gu;
+    dn.w_off0 = a->down_offset;
+    dn.w_off1 = a->down_offset;
+    dn.map0 = 2;
+    dn.out_dim = a->d_model;
+    dn.in_dim = a->ffn;
+    dn.img = img_dn;
+    dn.out_img = nullptr;
+    dn.part = part;
+    dn.unit_cnt = cnt + tiles * (a->ffn / TG_ROWS);
+    tgemv_kernel<1><<<grid, TG_THREADS, TgLayout<1>::smem_bytes(a->experts), s>>>(dn);
+    if ((rc = check_launch("tgemv down"))) return rc;
+    mark(mark_ctx, 6);
+    return FM_STATUS_OK;
+}
+
+} // namespace fmb
