@@ -534,13 +534,17 @@ def run_ours(args):
         "tokens_per_s": world * T / (ms / 1e3),
         "pct_of_8tbs": value / world / 8000.0 * 100.0,
         "stage_ms": report_stages(stage_ms, T),
-        "roofline": {"bound": "hbm", "kernel": "qgemv gate/up + SwiGLU (8 experts)", "achieved": gu_achieved,
+        "roofline": {"bound": "hbm", "kernel": ("tgemv_kernel<2> gate/up + SwiGLU (tcgen05), 8 experts" if type_id == 12
+                                                else "qgemv_async_kernel gate/up + SwiGLU (mma.sync), 8 experts"),
+                     "achieved": gu_achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": gu_achieved / peak,
                      "traffic": traffic, "algorithmic_bytes": gu_bytes,
                      "down_achieved": (EXPERTS * D_MODEL * row_bytes(type_id, FFN)) / (dn_ms / 1e3) / 1e9},
         "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": ms_e2e},
-        "gpu_launches": 4 * args.steps,  # router + grouping + x planes, gate/up (+ down's x planes), down, combine
+        # Q4_K: router + grouping, B images, gate/up (+ down's B images), down, combine;
+        # Q8_0: router + grouping + x planes, gate/up (+ down's x planes), down, combine
+        "gpu_launches": (5 if type_id == 12 else 4) * args.steps,
         "clocks": clocks.summary(),
     }
 
@@ -760,7 +764,7 @@ def run_layer(args):
         line["roofline"] = {"bound": "hbm", "kernel": "MoE block (distinct experts' bytes)",
                             "achieved": line["hbm_gbs"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
                             "frac": line["hbm_gbs"] / peak, "traffic": None, "algorithmic_bytes": wbytes}
-        line["gpu_launches"] = 4 * args.steps
+        line["gpu_launches"] = (5 if t == 12 else 4) * args.steps
 
     if not args.no_cpu:
         # the reference's CPU code on a bounded sample of the same tokens
