@@ -1236,6 +1236,126 @@ def run_layer_ep(args):
     dist.destroy_process_group()
 
 
+def run_stack_ep(args):
+    """--gpus N > 1 on the headline stack: expert parallelism over the torchrun
+    ranks.  Experts e live on rank e / (8 / N) with the N = 1 line's weights; the
+    step's T tokens are split over the ranks (T / N each, strong scaling: the
+    same stack and tokens as N = 1); each rank routes its tokens (top-8 of 8),
+    sends every token once to each rank over peer memory (mode p2p; NCCL
+    all-to-all with --ep-mode rows), runs the received rows through its experts
+    (tcgen05 decode stage) and combines the returned partial sums.  value = the
+    N = 1 line's bytes (every expert's weights once, x and y) / the step time,
+    max over ranks."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200.ep import DeviceOps, EPLayer
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    hotpath.init(local)
+    type_id = TYPES[args.type]
+    T = args.tokens
+    if EXPERTS % world or T % world:
+        raise SystemExit(f"{EXPERTS} experts / {T} tokens do not shard over {world} ranks")
+    per, tp = EXPERTS // world, T // world
+    gb = FFN * row_bytes(type_id, D_MODEL)
+    slots = []
+    for e in range(rank * per, (rank + 1) * per):  # the N = 1 line's weights (its rank-0 seeds)
+        slots.append(torch.cat([hotpath.synth_weights(type_id, rows, cols, 1000 + 3 * e + j)
+                                for j, (rows, cols) in enumerate(((FFN, D_MODEL), (FFN, D_MODEL), (D_MODEL, FFN)))]))
+    x_np, lg_np = host_inputs(T, seed=0)  # the N = 1 line's tokens
+    sl = slice(rank * tp, (rank + 1) * tp)
+    x = torch.from_numpy(x_np[sl]).cuda().to(torch.bfloat16)
+    logits = torch.from_numpy(lg_np[sl]).cuda()
+    ops = DeviceOps(experts_total=EXPERTS, top_k=EXPERTS, d_model=D_MODEL, ffn=FFN, gate_type=type_id,
+                    up_type=type_id, down_type=type_id, local_slots=slots, up_offset=gb, down_offset=2 * gb)
+    layer = EPLayer(ops, record_timing=True, mode=args.ep_mode)
+    for _ in range(args.warmup):
+        layer.forward(x, logits)
+    torch.cuda.synchronize()
+    assert hotpath.device_status() == 0
+    layer.phase_ms()  # drop the warm-up marks
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # value: timed without the phase events; the phases come from a second pass
+    layer.record_timing = False
+    with ClockSampler(local) as clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            layer.forward(x, logits)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms_t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    layer.record_timing = True
+    for _ in range(min(args.steps, 200)):
+        layer.forward(x, logits)
+    torch.cuda.synchronize()
+    phases = layer.phase_ms()
+    ph_t = torch.tensor([phases[k] for k in EPLayer.PHASES], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ph_t, op=dist.ReduceOp.MAX)
+    phases = dict(zip(EPLayer.PHASES, ph_t.tolist()))
+    layer.record_timing = False
+    # e2e: this rank's tokens and logits from pinned host memory, y back, every step
+    hx = torch.from_numpy(x_np[sl]).to(torch.bfloat16).pin_memory()
+    hl = torch.from_numpy(lg_np[sl]).pin_memory()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms_loc, hy = pipelined_e2e(lambda dx, dl, dy: dy.copy_(layer.forward(dx, dl)), hx, hl, x, logits,
+                               torch.empty(tp, D_MODEL, dtype=torch.float32, device="cuda"), args.steps, stream)
+    ms_e = torch.tensor([ms_loc], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms_e, op=dist.ReduceOp.MAX)
+    assert np.isfinite(hy.numpy()).all()
+    assert hotpath.device_status() == 0
+    nbytes = step_bytes(type_id, T)
+    peak, peak_kind = load_peaks()
+    # the rank's expert phase streams its experts' bytes once
+    local_bytes = per * expert_bytes(type_id)
+    exp_ms = phases.get("experts", 0.0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": args.type, "data": "synthetic",
+            "config": stack_config(args.type, T, world),
+            "entry_point": "freemoe_b200.ep.EPLayer.forward (route, dispatch, experts, combine per step)",
+            "exchange": {"p2p": "peer-memory stores fused into the dispatch and partial-sum kernels (CUDA IPC "
+                                "mailboxes, no collective in the data path)",
+                         "rows": "NCCL all-to-all (torch.distributed), one row per token and rank",
+                         "pairs": "NCCL all-to-all (torch.distributed), one row per pair"}[args.ep_mode],
+            "sharding": f"experts {per}/rank, tokens {tp}/rank",
+            "tokens_per_s": T / (ms / 1e3),
+            "phase_ms_max_over_ranks": phases,
+            "roofline": {"bound": "hbm", "kernel": "one rank's expert phase (tcgen05 decode stage, its "
+                                                   f"{per} experts' weights once)",
+                         "achieved": local_bytes / (exp_ms / 1e3) / 1e9 if exp_ms else None, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": local_bytes / (exp_ms / 1e3) / 1e9 / peak if exp_ms else None, "traffic": None,
+                         "algorithmic_bytes": local_bytes},
+            "e2e": {"value": nbytes / (float(ms_e.item()) / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": world * (hx.numel() * 2 + hl.numel() * 4),
+                    "d2h_bytes_per_step": world * hy.numel() * 4, "ms_per_step": float(ms_e.item())},
+            # per rank and step in mode p2p: route; dispatch keys, grouping, counts, plan,
+            # pack + send; wait, expert keys, grouping, B images, gate/up, down, partial
+            # return; wait, combine
+            "gpu_launches": 15 * args.steps if args.ep_mode == "p2p" else None,
+            "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    layer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1277,6 +1397,8 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args)
+    elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_stack_ep(args)
     else:
         run_ours(args)
 

@@ -22,6 +22,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "tgemv_host.h"
 
 namespace fmb {
 
@@ -159,8 +160,22 @@ ExpertsLayout experts_layout(uint32_t rows, uint32_t experts, uint32_t d, uint32
 }
 
 struct PartialLayout {
-    uint64_t keys, counts, offsets, pairs, gscratch, xg, act, out, total;
+    uint64_t keys, counts, offsets, pairs, gscratch, xg, act, tg, out, total;
 };
+
+// Routed pairs at most: a row holds one slot per local expert it was sent for.
+inline uint32_t partial_pairs_max(uint32_t rows, uint32_t top_k, uint32_t experts) {
+    return rows * (top_k < experts ? top_k : experts);
+}
+
+// The tcgen05 decode stage (tgemv.cu) takes the experts' GEMMs when the weights
+// are Q4_K and the experts hold one 8-token tile each on average (decode-sized
+// batches: pairs <= 8 x experts); larger batches go to the grouped GEMM, which
+// converts each weight tile once for up to 192 tokens.
+inline bool partial_uses_tg(uint32_t rows, uint32_t top_k, uint32_t experts, uint32_t d, uint32_t ffn) {
+    return tg_shape(d, ffn) && experts <= 1024 &&
+           static_cast<uint64_t>(partial_pairs_max(rows, top_k, experts)) <= 8ull * experts;
+}
 
 PartialLayout partial_layout(uint32_t rows, uint32_t top_k, uint32_t experts, uint32_t d, uint32_t ffn) {
     PartialLayout L{};
@@ -178,6 +193,9 @@ PartialLayout partial_layout(uint32_t rows, uint32_t top_k, uint32_t experts, ui
     L.gscratch = take(group_scratch_bytes(static_cast<uint32_t>(n), experts));
     L.xg = take(n * d * 2);
     L.act = take(n * ffn * 2);
+    L.tg = partial_uses_tg(rows, top_k, experts, d, ffn)
+               ? take(tg_sections(partial_pairs_max(rows, top_k, experts), experts, d, ffn).total())
+               : o;
     L.out = take(n * d * 4);
     L.total = o;
     return L;
@@ -299,6 +317,33 @@ int experts_partial_run(const void *x, const int32_t *meta_expert, const float *
     if ((rc = launch_group_large(keys, n, experts, counts, offsets, pairs, nullptr,
                                  reinterpret_cast<uint32_t *>(ws + L.gscratch), s)))
         return rc;
+    if (gate_type == FM_TYPE_Q4_K && down_type == FM_TYPE_Q4_K && partial_uses_tg(rows, top_k, experts, d_model, ffn) &&
+        up_offset % 16 == 0 && down_offset % 16 == 0) {
+        // decode-sized batch: the tcgen05 decode stage reads the received rows in
+        // place and writes the output of grouped pair g to slot pairs[g]
+        const uint32_t pmax = partial_pairs_max(rows, top_k, experts);
+        const TgSections ts = tg_sections(pmax, experts, d_model, ffn);
+        uint8_t *tg = ws + L.tg;
+        TgStage t{};
+        t.x = x;
+        t.x_f16 = true;
+        t.pairs_max = pmax;
+        t.top_k = top_k;
+        t.experts = experts;
+        t.d = d_model;
+        t.ffn = ffn;
+        t.slots = expert_slots;
+        t.up_offset = up_offset;
+        t.down_offset = down_offset;
+        t.counts = counts;
+        t.offsets = offsets;
+        t.pairs = pairs;
+        t.out_rows = pairs;
+        return tg_expert_stage(t, tg, tg + ts.img_gu, reinterpret_cast<float *>(tg + ts.img_gu + ts.img_dn),
+                               reinterpret_cast<uint32_t *>(tg + ts.img_gu + ts.img_dn + ts.partial),
+                               tg + ts.img_gu + ts.img_dn + ts.partial + ts.cnt, out_pairs,
+                               [](void *, int) {}, nullptr, s);
+    }
     gather_pair_rows_kernel<<<n, 128, 0, s>>>(static_cast<const __half *>(x), pairs, offsets + experts, top_k,
                                               d_model, xg);
     if ((rc = check_launch("expert gather launch"))) return rc;

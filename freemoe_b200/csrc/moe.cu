@@ -110,7 +110,7 @@ MoeLayout moe_layout(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t
     L.al = take(P * ffn * 2);
     L.as = take(P * (ffn / 32) * 4);
     L.part = take(P * d * 4);
-    const TgSections tg = tg_sections(tokens, experts, top_k, d, ffn);
+    const TgSections tg = tg_sections(static_cast<uint32_t>(P), experts, d, ffn);
     L.tg_img_gu = take(tg.img_gu);
     L.tg_img_dn = take(tg.img_dn);
     L.tg_partial = take(tg.partial);
@@ -257,8 +257,23 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
         struct MarkCtx {
             decltype(mark) *fn;
         } mctx{&mark};
+        TgStage ts{};
+        ts.x = a->x;
+        ts.x_f16 = false;
+        ts.pairs_max = P;
+        ts.top_k = a->top_k;
+        ts.experts = a->experts;
+        ts.d = a->d_model;
+        ts.ffn = a->ffn;
+        ts.slots = a->expert_slots;
+        ts.up_offset = a->up_offset;
+        ts.down_offset = a->down_offset;
+        ts.counts = counts;
+        ts.offsets = offsets;
+        ts.pairs = pairs;
+        ts.out_rows = nullptr;
         rc = tg_expert_stage(
-            a, counts, offsets, pairs, ws + L.tg_img_gu, ws + L.tg_img_dn, reinterpret_cast<float *>(ws + L.tg_partial),
+            ts, ws + L.tg_img_gu, ws + L.tg_img_dn, reinterpret_cast<float *>(ws + L.tg_partial),
             reinterpret_cast<uint32_t *>(ws + L.tg_cnt), ws + L.tg_maps, part,
             [](void *ctx, int i) { (*static_cast<MarkCtx *>(ctx)->fn)(i); }, &mctx, s);
         if (rc) return rc;

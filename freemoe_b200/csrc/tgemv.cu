@@ -71,18 +71,17 @@ int tg_template(CUtensorMap *map, const void *any_base, uint32_t row_bytes, uint
 
 } // namespace
 
-// Upper bound of token tiles of one block: every expert's last tile may be partial.
-uint32_t tg_max_tiles(uint32_t tokens, uint32_t experts, uint32_t top_k) {
-    const uint64_t P = static_cast<uint64_t>(tokens) * top_k;
-    return static_cast<uint32_t>(P / TG_NT + (P < experts ? P : experts));
+// Upper bound of token tiles: every expert's last tile may be partial.
+uint32_t tg_max_tiles(uint32_t pairs_max, uint32_t experts) {
+    return pairs_max / TG_NT + (pairs_max < experts ? pairs_max : experts);
 }
 
 bool tg_shape(uint32_t d, uint32_t ffn) { return d % 256 == 0 && ffn % 256 == 0 && d > 0 && ffn > 0; }
 
-TgSections tg_sections(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t d, uint32_t ffn) {
+TgSections tg_sections(uint32_t pairs_max, uint32_t experts, uint32_t d, uint32_t ffn) {
     TgSections t{};
     if (!tg_shape(d, ffn)) return t;
-    const uint64_t tiles = tg_max_tiles(tokens, experts, top_k);
+    const uint64_t tiles = tg_max_tiles(pairs_max, experts);
     t.img_gu = a256(tiles * (d / 256) * TG_IMG);
     t.img_dn = a256(tiles * (ffn / 256) * TG_IMG);
     t.partial = a256(2ull * TG_MAX_CTAS * 2 * 2 * TG_NT * TG_ROWS * 4);
@@ -98,29 +97,33 @@ bool tg_eligible(const fmcuda_moe_args *a) {
 }
 
 // Steps after routing and grouping: x images, gate/up + SwiGLU (writing the
-// down images), down.  `part` receives one f32 row per grouped pair.
-int tg_expert_stage(const fmcuda_moe_args *a, const uint32_t *counts, const uint32_t *offsets, const uint32_t *pairs,
-                    uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt, uint8_t *maps_area, float *part,
-                    void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
+// down images), down.
+int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
+                    uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
     int rc;
     if ((rc = tg_configure<2>())) return rc;
     if ((rc = tg_configure<1>())) return rc;
-    const uint32_t tiles = tg_max_tiles(a->tokens, a->experts, a->top_k);
-    const uint32_t n_cnt = tiles * (a->ffn / TG_ROWS + a->d_model / TG_ROWS);
+    const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
+    const uint32_t n_cnt = tiles * (t.ffn / TG_ROWS + t.d / TG_ROWS);
     TgMapArgs ma{};
     ma.maps = reinterpret_cast<CUtensorMap *>(maps_area + 256);
-    ma.slots = reinterpret_cast<const uint8_t *const *>(a->expert_slots);
-    ma.up_off = a->up_offset;
-    ma.down_off = a->down_offset;
+    ma.slots = reinterpret_cast<const uint8_t *const *>(t.slots);
+    ma.up_off = t.up_offset;
+    ma.down_off = t.down_offset;
     ma.cnt = cnt;
     ma.n_cnt = n_cnt;
-    const uint32_t rb_gu = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, a->d_model));
-    const uint32_t rb_dn = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, a->ffn));
-    if ((rc = tg_template(&ma.tmpl_gu, ma.maps, rb_gu, a->ffn))) return rc;
-    if ((rc = tg_template(&ma.tmpl_dn, ma.maps, rb_dn, a->d_model))) return rc;
-    tg_ximage_kernel<<<tiles * (a->d_model / 256), 256, 0, s>>>(
-        ma, static_cast<const __nv_bfloat16 *>(a->x), a->d_model, counts, offsets, pairs, a->top_k, a->experts,
-        tiles, img_gu);
+    const uint32_t rb_gu = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, t.d));
+    const uint32_t rb_dn = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, t.ffn));
+    if ((rc = tg_template(&ma.tmpl_gu, ma.maps, rb_gu, t.ffn))) return rc;
+    if ((rc = tg_template(&ma.tmpl_dn, ma.maps, rb_dn, t.d))) return rc;
+    if (t.x_f16)
+        tg_ximage_kernel<__half><<<tiles * (t.d / 256), 256, 0, s>>>(
+            ma, static_cast<const __half *>(t.x), t.d, t.counts, t.offsets, t.pairs, t.top_k, t.experts, tiles,
+            img_gu);
+    else
+        tg_ximage_kernel<__nv_bfloat16><<<tiles * (t.d / 256), 256, 0, s>>>(
+            ma, static_cast<const __nv_bfloat16 *>(t.x), t.d, t.counts, t.offsets, t.pairs, t.top_k, t.experts,
+            tiles, img_gu);
     if ((rc = check_launch("tgemv x images"))) return rc;
     mark(mark_ctx, 3);
 
@@ -129,35 +132,36 @@ int tg_expert_stage(const fmcuda_moe_args *a, const uint32_t *counts, const uint
     TgParams gu{};
     gu.slots = ma.slots;
     gu.w_off0 = 0;
-    gu.w_off1 = a->up_offset;
+    gu.w_off1 = t.up_offset;
     gu.maps = ma.maps;
     gu.map0 = 0;
-    gu.out_dim = a->ffn;
-    gu.in_dim = a->d_model;
-    gu.experts = a->experts;
-    gu.counts = counts;
-    gu.offsets = offsets;
+    gu.out_dim = t.ffn;
+    gu.in_dim = t.d;
+    gu.experts = t.experts;
+    gu.counts = t.counts;
+    gu.offsets = t.offsets;
     gu.img = img_gu;
     gu.out_img = img_dn;
     gu.partial = partial;
     gu.unit_cnt = cnt;
     gu.status = device_status_word();
-    tgemv_kernel<2><<<grid, TG_THREADS, TgLayout<2>::smem_bytes(a->experts), s>>>(gu);
+    tgemv_kernel<2><<<grid, TG_THREADS, TgLayout<2>::smem_bytes(t.experts), s>>>(gu);
     if ((rc = check_launch("tgemv gate/up"))) return rc;
     mark(mark_ctx, 4);
     mark(mark_ctx, 5);
 
     TgParams dn = gu;
-    dn.w_off0 = a->down_offset;
-    dn.w_off1 = a->down_offset;
+    dn.w_off0 = t.down_offset;
+    dn.w_off1 = t.down_offset;
     dn.map0 = 2;
-    dn.out_dim = a->d_model;
-    dn.in_dim = a->ffn;
+    dn.out_dim = t.d;
+    dn.in_dim = t.ffn;
     dn.img = img_dn;
     dn.out_img = nullptr;
     dn.part = part;
-    dn.unit_cnt = cnt + tiles * (a->ffn / TG_ROWS);
-    tgemv_kernel<1><<<grid, TG_THREADS, TgLayout<1>::smem_bytes(a->experts), s>>>(dn);
+    dn.out_rows = t.out_rows;
+    dn.unit_cnt = cnt + tiles * (t.ffn / TG_ROWS);
+    tgemv_kernel<1><<<grid, TG_THREADS, TgLayout<1>::smem_bytes(t.experts), s>>>(dn);
     if ((rc = check_launch("tgemv down"))) return rc;
     mark(mark_ctx, 6);
     return FM_STATUS_OK;

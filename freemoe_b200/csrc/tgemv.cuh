@@ -65,6 +65,8 @@
 
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "gemv_kernels.cuh"
@@ -98,6 +100,7 @@ struct TgParams {
     const uint8_t *img;          // B images [tile][in_dim / 256][TG_IMG]
     uint8_t *out_img;            // gate/up: the down GEMV's images [tile][out_dim / 256][TG_IMG]
     float *part;                 // down: [pair][out_dim]
+    const uint32_t *out_rows;    // down: part row of grouped pair g (NULL: g)
     float *partial;              // stream-K parts [pipeline][2][NMAT][TG_NT][128]
     uint32_t *unit_cnt;          // stream-K arrivals per unit (zero on entry, left zero)
     int *status;
@@ -598,7 +601,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             } else {
 #pragma unroll
                 for (uint32_t n = 0; n < TG_NT; ++n)
-                    if (n < g.ntok) p.part[static_cast<uint64_t>(g.pair0 + n) * p.out_dim + f] = val[0][n];
+                    if (n < g.ntok) {
+                        const uint32_t row = p.out_rows ? __ldg(p.out_rows + g.pair0 + n) : g.pair0 + n;
+                        p.part[static_cast<uint64_t>(row) * p.out_dim + f] = val[0][n];
+                    }
             }
             return true;
         };
@@ -686,8 +692,9 @@ struct TgMapArgs {
 // expert's matrix through tensormap.replace; experts without tokens or without
 // a usable slot are skipped, the GEMV kernels report those) and clears the
 // stream-K counters.
+template <typename XT>
 __global__ void __launch_bounds__(256)
-    tg_ximage_kernel(const __grid_constant__ TgMapArgs ma, const __nv_bfloat16 *__restrict__ x, uint32_t d,
+    tg_ximage_kernel(const __grid_constant__ TgMapArgs ma, const XT *__restrict__ x, uint32_t d,
                      const uint32_t *__restrict__ counts, const uint32_t *__restrict__ offsets,
                      const uint32_t *__restrict__ pairs, uint32_t top_k, uint32_t experts, uint32_t max_tiles,
                      uint8_t *__restrict__ img) {
@@ -729,7 +736,9 @@ __global__ void __launch_bounds__(256)
         float v = 0.0f;
         if (n < ntok) {
             const uint32_t tok = pairs[pair0 + n] / top_k;
-            v = __bfloat162float(x[static_cast<uint64_t>(tok) * d + 256u * b + k]);
+            const XT xv = x[static_cast<uint64_t>(tok) * d + 256u * b + k];
+            if constexpr (sizeof(XT) == 2 && std::is_same<XT, __half>::value) v = __half2float(xv);
+            else v = __bfloat162float(xv);
         }
         s_x[n][k] = v;
     }

@@ -1,5 +1,6 @@
 // tgemv_host.h -- host interface of the tcgen05 decode GEMVs (tgemv.cu) for
-// the MoE block (moe.cu): workspace sections, eligibility, the expert stage.
+// the MoE block (moe.cu) and the expert-parallel expert compute (ep.cu):
+// workspace sections, eligibility, the expert stage.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -12,14 +13,30 @@ namespace fmb {
 // Workspace bytes of the tcgen05 expert stage (zero where the shape has no such path).
 struct TgSections {
     uint64_t img_gu, img_dn, partial, cnt, maps;
+    uint64_t total() const { return img_gu + img_dn + partial + cnt + maps; }
 };
 
-TgSections tg_sections(uint32_t tokens, uint32_t experts, uint32_t top_k, uint32_t d, uint32_t ffn);
+// One expert stage: grouped pairs (router.cu's grouping) in, one f32 output row
+// per pair out.  x rows are bf16 or fp16; pair g reads x row pairs[g] / top_k.
+struct TgStage {
+    const void *x;
+    bool x_f16;                   // fp16 rows (the expert-parallel receive buffer), else bf16
+    uint32_t pairs_max;           // upper bound of the routed pairs (sizes the token tiles)
+    uint32_t top_k, experts, d, ffn;
+    const void *const *slots;
+    uint64_t up_offset, down_offset;
+    const uint32_t *counts, *offsets, *pairs;
+    const uint32_t *out_rows;     // output row of grouped pair g (NULL: g)
+};
+
+// pairs_max = routed pairs of one call, at most
+TgSections tg_sections(uint32_t pairs_max, uint32_t experts, uint32_t d, uint32_t ffn);
+bool tg_shape(uint32_t d, uint32_t ffn);
 // Q4_K gate/up/down, bf16 activations, d and ffn multiples of 256, <= 1024 experts.
 bool tg_eligible(const fmcuda_moe_args *a);
-// x images, gate/up + SwiGLU, down; `mark(ctx, i)` records stage event i.
-int tg_expert_stage(const fmcuda_moe_args *a, const uint32_t *counts, const uint32_t *offsets, const uint32_t *pairs,
-                    uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt, uint8_t *maps_area, float *part,
-                    void (*mark)(void *, int), void *mark_ctx, cudaStream_t s);
+// B images, gate/up + SwiGLU, down; `mark(ctx, i)` records stage event i (3 after
+// the images, 4 and 5 after gate/up, 6 after down).
+int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
+                    uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s);
 
 } // namespace fmb

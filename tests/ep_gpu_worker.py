@@ -5,7 +5,10 @@ EPLayer, and rank 0 compares the gathered output with fmcuda_moe_prefill over
 all experts on one GPU: identical bits in the per-pair exchange ("pairs"); in
 the de-duplicated exchange ("rows") the terms are summed grouped by rank, so
 the bar is 1e-5 of max |y|; the peer-memory exchange ("p2p") must equal "rows"
-bit for bit on three successive calls."""
+bit for bit on three successive calls.  With a last argument "block" the
+reference is fmcuda_moe_block instead (decode-sized batches, where each rank's
+experts run on the tcgen05 decode stage): within 1e-5 of max |y| for "rows"
+and "p2p"."""
 from __future__ import annotations
 
 import datetime
@@ -24,6 +27,7 @@ import torch.distributed as dist  # noqa: E402
 def main():
     E, k, d, ffn, T, t = (int(v) for v in sys.argv[1:7])
     mode = sys.argv[7] if len(sys.argv) > 7 else "pairs"
+    ref = sys.argv[8] if len(sys.argv) > 8 else "prefill"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -63,10 +67,13 @@ def main():
     ok = torch.tensor([1], device="cuda")
     if rank == 0:
         y_ep = torch.cat(parts)
-        y_one = hotpath.moe_prefill(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
+        if ref == "block":
+            y_one = hotpath.moe_block(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
+        else:
+            y_one = hotpath.moe_prefill(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
         same = torch.equal(y_ep.view(torch.int32), y_one.view(torch.int32))
         err = float((y_ep - y_one).abs().max() / y_one.abs().max())
-        print(f"ep world={world} mode={mode}: identical={same} max_rel={err:.3e}", flush=True)
+        print(f"ep world={world} mode={mode} ref={ref}: identical={same} max_rel={err:.3e}", flush=True)
         ok[0] = int(same) if mode == "pairs" else int(err <= 1e-5)
     dist.broadcast(ok, 0)
     dist.destroy_process_group()

@@ -31,6 +31,71 @@ def test_ep_matches_single_gpu(shape, mode):
     assert ("identical=True" if mode == "pairs" else "max_rel=") in p.stdout
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("shape", [(8, 8, 512, 768, 8, 12), (8, 2, 4096, 14336, 4, 12)])
+@pytest.mark.parametrize("mode", ["rows", "p2p"])
+def test_ep_decode_matches_moe_block(shape, mode):
+    """Decode-sized batches (one 8-token tile per expert on average): every rank's
+    experts run on the tcgen05 decode stage; the gathered output is within 1e-5
+    of max |y| of fmcuda_moe_block over all experts on one GPU."""
+    n = min(torch.cuda.device_count(), 8)
+    n = 2 if shape[0] % n or shape[4] % n else n
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29733",
+           str(ROOT / "tests" / "ep_gpu_worker.py"), *map(str, shape), mode, "block"]
+    p = subprocess.run(cmd, capture_output=True, text=True, cwd=str(ROOT), env={**__import__("os").environ,
+                       "NCCL_NVLS_ENABLE": "0"})
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    assert "ref=block" in p.stdout and "max_rel=" in p.stdout
+
+
+def test_p2p_decode_single_rank(cuda, oracle):
+    """One rank through the peer-memory exchange with a decode-sized batch (the
+    tcgen05 decode stage computes the experts from the fp16 mailbox rows): three
+    calls in a row, each within 1e-5 of max |y| of fmcuda_moe_block and within
+    1e-3 of the oracle's per-token expert loop."""
+    import socket
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200.ep import DeviceOps, EPLayer
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        E, k, d, ffn, T, t = 8, 2, 512, 768, 6, 12
+        rb = hotpath.row_bytes
+        slots = [torch.cat([hotpath.synth_weights(t, ffn, d, 7100 + 3 * e), hotpath.synth_weights(t, ffn, d, 7101 + 3 * e),
+                            hotpath.synth_weights(t, d, ffn, 7102 + 3 * e)]) for e in range(E)]
+        gb = rb(t, d) * ffn
+        rng = np.random.default_rng(4)
+        x_np = rng.normal(0, 1, size=(T, d)).astype(np.float32)
+        x = torch.from_numpy(x_np).cuda().to(torch.bfloat16)
+        lg_np = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+        logits = torch.from_numpy(lg_np).cuda()
+        ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
+                        local_slots=slots, up_offset=gb, down_offset=2 * gb)
+        y_block = hotpath.moe_block(x, logits, slots, top_k=k, ffn=ffn, gate_type=t)
+        rc, ids_o, w_o, _ = oracle.route(lg_np, k)
+        y_o = oracle.moe_block(x.float().cpu().numpy(), ids_o, w_o, [s.cpu().numpy() for s in slots], d, ffn, t)
+        layer = EPLayer(ops, mode="p2p")
+        for _ in range(3):
+            y = layer.forward(x, logits)
+            torch.cuda.synchronize()
+            assert cuda.device_status() == 0
+            err_b = float((y - y_block).abs().max() / y_block.abs().max())
+            assert err_b <= 1e-5, err_b
+            err_o = float(np.abs(y.cpu().numpy() - y_o).max() / np.abs(y_o).max())
+            assert err_o <= 1e-3, err_o
+        layer.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def test_p2p_exchange_single_rank_and_timeout(cuda):
     """One rank (world 1) through the peer-memory exchange: mailbox, IPC handle,
     the count/plan/send/return/combine kernels writing to its own mailbox,
