@@ -85,6 +85,32 @@ class MoeArgs(C.Structure):
     ]
 
 
+class EpLayerArgs(C.Structure):
+    """fmcuda_ep_layer_args (include/freemoe_b200.h)."""
+    _fields_ = [
+        ("x", C.c_void_p),
+        ("x_dtype", C.c_int32),
+        ("logits", C.c_void_p),
+        ("tokens", C.c_uint32),
+        ("experts", C.c_uint32),
+        ("top_k", C.c_uint32),
+        ("d_model", C.c_uint32),
+        ("ffn", C.c_uint32),
+        ("local_slots", C.c_void_p),
+        ("up_offset", C.c_uint64),
+        ("down_offset", C.c_uint64),
+        ("gate_type", C.c_uint32),
+        ("up_type", C.c_uint32),
+        ("down_type", C.c_uint32),
+        ("normalise", C.c_int32),
+        ("epsilon", C.c_double),
+        ("scale", C.c_double),
+        ("y", C.c_void_p),
+    ]
+
+
+EP_NCCL_ID_BYTES = 128
+
 GATING_SOFTMAX, GATING_SIGMOID, GATING_SQRT_SOFTPLUS, GATING_SOFTMAX_WEIGHT = 0, 1, 2, 3
 
 
@@ -189,6 +215,11 @@ SIGNATURES = [
     ("fmcuda_moe_experts_partial", C.c_int, [_P, _P, _P, _U32, _U32, _U32, _P, _U64, _U64, _U32, _U32, _U32, _U32,
                                              _U32, _P, _P, _U64, _P]),
     ("fmcuda_ep_combine_rows", C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P]),
+    ("fmcuda_ep_nccl_unique_id", C.c_int, [_P]),
+    ("fmcuda_ep_init", C.c_int, [_P, _U32, _U32, C.POINTER(C.c_void_p)]),
+    ("fmcuda_ep_destroy", C.c_int, [_P]),
+    ("fmcuda_ep_layer_workspace_bytes", C.c_int, [_U32, _U32, _U32, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
+    ("fmcuda_ep_layer", C.c_int, [_P, C.POINTER(EpLayerArgs), _U32, _P, C.c_uint64, _P]),
     ("fmcuda_ep_mailbox_bytes", _U64, [_U32, _U32, _U32, _U32]),
     ("fmcuda_ep_mailbox_alloc", C.c_int, [_U64, C.POINTER(C.c_void_p), _P]),
     ("fmcuda_ep_mailbox_open", C.c_int, [_P, C.POINTER(C.c_void_p)]),

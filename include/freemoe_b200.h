@@ -378,6 +378,49 @@ int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_expert, const 
 int fmcuda_ep_combine_rows(const float *back, const uint32_t *row_of, uint32_t tokens, uint32_t world,
                            uint32_t d_model, float *y, void *stream);
 
+/* ============ expert parallelism over NCCL, driven from C ============ *
+ * No reference counterpart (FreeMoe runs every expert in one process); this is
+ * the SURVEY-listed fmcuda_ep_init(nccl_uid, rank, G) boundary for hosts that
+ * are not Python.  NCCL is loaded at run time (libnccl.so.2: the copy the
+ * process already holds, else the system's).
+ *
+ * fmcuda_ep_nccl_unique_id: rank 0 creates the group's id (FM_EP_NCCL_ID_BYTES
+ * bytes) and shares it with the other ranks out of band (a store, a file, MPI).
+ * fmcuda_ep_init: every rank, with its device current, joins the group
+ * (ncclCommInitRank; collective); fmcuda_ep_destroy leaves it.
+ * fmcuda_ep_layer: one routed-expert MoE layer for this rank's `tokens` tokens,
+ * experts sharded over the group (expert e on rank e / (experts / world),
+ * `local_slots` = this rank's experts in order): route, one fp16 row per
+ * (token, destination rank) with its slots' local experts and weights, NCCL
+ * send/recv of the counts (read on the host: one stream synchronisation per
+ * call), of the rows, this rank's experts (fmcuda_moe_experts_partial), the
+ * f32 partial rows back, combine -- the de-duplicated ("rows") exchange of
+ * freemoe_b200/ep.py, with the same result bit for bit.  Every rank calls it
+ * once per layer, in the same order; `tokens_max` >= every rank's token count
+ * (sizes the workspace: fmcuda_ep_layer_workspace_bytes).  NCCL failures come
+ * back as TRANSFER_FAILED with NCCL's message. */
+#define FM_EP_NCCL_ID_BYTES 128
+typedef struct fmcuda_ep_layer_args {
+    const void *x;                    /* [tokens][d_model] bf16 or f32 */
+    int32_t x_dtype;                  /* FM_X_F32 or FM_X_BF16 */
+    const float *logits;              /* [tokens][experts] router logits */
+    uint32_t tokens, experts, top_k;  /* experts = all experts of the layer */
+    uint32_t d_model, ffn;
+    const void *const *local_slots;   /* device array: this rank's expert records */
+    uint64_t up_offset, down_offset;  /* inside a record */
+    uint32_t gate_type, up_type, down_type;
+    int32_t normalise;                /* renormalise the selected weights */
+    double epsilon, scale;            /* src/engine.cpp:1680-1702 */
+    float *y;                         /* [tokens][d_model] f32 */
+} fmcuda_ep_layer_args;
+int fmcuda_ep_nccl_unique_id(void *uid);
+int fmcuda_ep_init(const void *nccl_uid, uint32_t rank, uint32_t world, void **comm);
+int fmcuda_ep_destroy(void *comm);
+int fmcuda_ep_layer_workspace_bytes(uint32_t tokens_max, uint32_t world, uint32_t experts_local, uint32_t top_k,
+                                    uint32_t d_model, uint32_t ffn, uint64_t *bytes);
+int fmcuda_ep_layer(void *comm, const fmcuda_ep_layer_args *args, uint32_t tokens_max, void *workspace,
+                    uint64_t workspace_bytes, void *stream);
+
 /* ============ expert parallelism over peer memory (one node) ============ *
  * The same de-duplicated exchange with no collective library call and no host
  * read of the split sizes: each rank owns a mailbox (device memory shared with

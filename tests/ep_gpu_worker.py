@@ -47,7 +47,42 @@ def main():
     ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
                     local_slots=slots[rank * per:(rank + 1) * per], up_offset=gb, down_offset=2 * gb)
     xs, ls = x[rank * tp:(rank + 1) * tp].contiguous(), logits[rank * tp:(rank + 1) * tp].contiguous()
-    if mode == "p2p":
+    if mode == "nccl_c":
+        # the layer driven from the C ABI over its own NCCL communicator must equal
+        # the Python layer's "rows" exchange bit for bit, call after call
+        import ctypes as C
+
+        from freemoe_b200._lib import X_BF16, EpLayerArgs, check, load
+
+        lib = load()
+        y_rows = EPLayer(ops, mode="rows").forward(xs, ls)
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            h = (C.c_uint8 * 128)()
+            check(lib.fmcuda_ep_nccl_unique_id(h))
+            uid.copy_(torch.tensor(list(h), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        uid_h = (C.c_uint8 * 128)(*uid.cpu().tolist())
+        comm = C.c_void_p()
+        check(lib.fmcuda_ep_init(uid_h, rank, world, C.byref(comm)))
+        a = EpLayerArgs()
+        a.x, a.x_dtype, a.logits = xs.data_ptr(), X_BF16, ls.data_ptr()
+        a.tokens, a.experts, a.top_k, a.d_model, a.ffn = xs.shape[0], E, k, d, ffn
+        a.local_slots, a.up_offset, a.down_offset = ops.table.data_ptr(), gb, 2 * gb
+        a.gate_type = a.up_type = a.down_type = t
+        a.normalise, a.epsilon, a.scale = 1, 6.103515625e-5, 1.0
+        y = torch.empty(xs.shape[0], d, device="cuda")
+        a.y = y.data_ptr()
+        nbytes = C.c_uint64()
+        check(lib.fmcuda_ep_layer_workspace_bytes(tp, world, per, k, d, ffn, C.byref(nbytes)))
+        ws = torch.empty(nbytes.value, dtype=torch.uint8, device="cuda")
+        for call in range(3):
+            check(lib.fmcuda_ep_layer(comm, C.byref(a), tp, C.c_void_p(ws.data_ptr()), ws.numel(), None))
+            torch.cuda.synchronize()
+            assert hotpath.device_status() == 0
+            assert torch.equal(y.view(torch.int32), y_rows.view(torch.int32)), f"call {call} differs from mode rows"
+        check(lib.fmcuda_ep_destroy(comm))
+    elif mode == "p2p":
         # the peer-memory exchange must reproduce mode "rows" bit for bit, call after call
         y_rows = EPLayer(ops, mode="rows").forward(xs, ls)
         layer = EPLayer(ops, mode="p2p")
@@ -74,7 +109,7 @@ def main():
         same = torch.equal(y_ep.view(torch.int32), y_one.view(torch.int32))
         err = float((y_ep - y_one).abs().max() / y_one.abs().max())
         print(f"ep world={world} mode={mode} ref={ref}: identical={same} max_rel={err:.3e}", flush=True)
-        ok[0] = int(same) if mode == "pairs" else int(err <= 1e-5)
+        ok[0] = int(same) if mode == "pairs" else int(err <= 1e-5)  # nccl_c: "rows" checked on every rank above
     dist.broadcast(ok, 0)
     dist.destroy_process_group()
     sys.exit(0 if ok.item() else 1)

@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("shape", [(16, 4, 256, 256, 512, 12), (128, 8, 4096, 1536, 1024, 12), (64, 6, 2048, 1408, 512, 8)])
-@pytest.mark.parametrize("mode", ["pairs", "rows", "p2p"])
+@pytest.mark.parametrize("mode", ["pairs", "rows", "p2p", "nccl_c"])
 def test_ep_matches_single_gpu(shape, mode):
     n = min(torch.cuda.device_count(), 8)
     n = 2 if shape[0] % n else n
@@ -33,7 +33,7 @@ def test_ep_matches_single_gpu(shape, mode):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("shape", [(8, 8, 512, 768, 8, 12), (8, 2, 4096, 14336, 4, 12)])
-@pytest.mark.parametrize("mode", ["rows", "p2p"])
+@pytest.mark.parametrize("mode", ["rows", "p2p", "nccl_c"])
 def test_ep_decode_matches_moe_block(shape, mode):
     """Decode-sized batches (one 8-token tile per expert on average): every rank's
     experts run on the tcgen05 decode stage; the gathered output is within 1e-5
@@ -94,6 +94,90 @@ def test_p2p_decode_single_rank(cuda, oracle):
         layer.close()
     finally:
         dist.destroy_process_group()
+
+
+def nccl_c_layer(lib, comm, x, logits, slots_table, *, world, n_local, E, k, d, ffn, t, gb, tokens_max):
+    """One fmcuda_ep_layer call through the C ABI (the NCCL-driven layer)."""
+    import ctypes as C
+
+    from freemoe_b200._lib import X_BF16, EpLayerArgs, check
+
+    a = EpLayerArgs()
+    a.x, a.x_dtype, a.logits = x.data_ptr(), X_BF16, logits.data_ptr()
+    a.tokens, a.experts, a.top_k, a.d_model, a.ffn = x.shape[0], E, k, d, ffn
+    a.local_slots, a.up_offset, a.down_offset = slots_table.data_ptr(), gb, 2 * gb
+    a.gate_type = a.up_type = a.down_type = t
+    a.normalise, a.epsilon, a.scale = 1, 6.103515625e-5, 1.0
+    y = torch.empty(x.shape[0], d, device=x.device)
+    a.y = y.data_ptr()
+    nbytes = C.c_uint64()
+    check(lib.fmcuda_ep_layer_workspace_bytes(tokens_max, world, n_local, k, d, ffn, C.byref(nbytes)))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+    check(lib.fmcuda_ep_layer(comm, C.byref(a), tokens_max, C.c_void_p(ws.data_ptr()), ws.numel(), None))
+    return y
+
+
+@pytest.mark.parametrize("shape", [(16, 4, 256, 256, 64, 12), (8, 2, 512, 768, 6, 12)])
+def test_nccl_c_layer_single_rank(cuda, shape):
+    """fmcuda_ep_init / fmcuda_ep_layer with one rank (NCCL sends to itself): the
+    layer driven from the C ABI equals the Python layer's "rows" exchange bit for
+    bit, twice in a row, for a prefill-sized batch (grouped GEMM) and a
+    decode-sized one (tcgen05 decode stage)."""
+    import ctypes as C
+    import socket
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from freemoe_b200 import hotpath
+    from freemoe_b200._lib import EP_NCCL_ID_BYTES, check, load
+    from freemoe_b200.ep import DeviceOps, EPLayer
+
+    E, k, d, ffn, T, t = shape
+    lib = load()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    comm = C.c_void_p()
+    try:
+        rb = hotpath.row_bytes
+        slots = [torch.cat([hotpath.synth_weights(t, ffn, d, 7200 + 3 * e), hotpath.synth_weights(t, ffn, d, 7201 + 3 * e),
+                            hotpath.synth_weights(t, d, ffn, 7202 + 3 * e)]) for e in range(E)]
+        gb = rb(t, d) * ffn
+        rng = np.random.default_rng(5)
+        x = torch.from_numpy(rng.normal(0, 1, size=(T, d)).astype(np.float32)).cuda().to(torch.bfloat16)
+        logits = torch.from_numpy(rng.normal(0, 1, size=(T, E)).astype(np.float32)).cuda()
+        ops = DeviceOps(experts_total=E, top_k=k, d_model=d, ffn=ffn, gate_type=t, up_type=t, down_type=t,
+                        local_slots=slots, up_offset=gb, down_offset=2 * gb)
+        y_rows = EPLayer(ops, mode="rows").forward(x, logits)
+        uid = (C.c_uint8 * EP_NCCL_ID_BYTES)()
+        check(lib.fmcuda_ep_nccl_unique_id(uid))
+        check(lib.fmcuda_ep_init(uid, 0, 1, C.byref(comm)))
+        for _ in range(2):
+            y = nccl_c_layer(lib, comm, x, logits, ops.table, world=1, n_local=E, E=E, k=k, d=d, ffn=ffn, t=t, gb=gb,
+                             tokens_max=T)
+            torch.cuda.synchronize()
+            assert cuda.device_status() == 0
+            assert torch.equal(y.view(torch.int32), y_rows.view(torch.int32))
+    finally:
+        if comm.value:
+            lib.fmcuda_ep_destroy(comm)
+        dist.destroy_process_group()
+
+
+def test_nccl_c_layer_rejects_bad_arguments(cuda):
+    """Host-side validation of the NCCL layer: typed INVALID_ARGUMENT, nothing launched."""
+    import ctypes as C
+
+    from freemoe_b200._lib import EpLayerArgs, load
+
+    lib = load()
+    assert lib.fmcuda_ep_init(None, 0, 1, None) == 26
+    uid = (C.c_uint8 * 128)()
+    out = C.c_void_p()
+    assert lib.fmcuda_ep_init(uid, 2, 2, C.byref(out)) == 26  # rank >= world
+    assert lib.fmcuda_ep_layer(None, C.byref(EpLayerArgs()), 1, None, 0, None) == 26
 
 
 def test_p2p_exchange_single_rank_and_timeout(cuda):
