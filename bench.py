@@ -1275,7 +1275,8 @@ def run_stack_ep(args):
     logits = torch.from_numpy(lg_np[sl]).cuda()
     ops = DeviceOps(experts_total=EXPERTS, top_k=EXPERTS, d_model=D_MODEL, ffn=FFN, gate_type=type_id,
                     up_type=type_id, down_type=type_id, local_slots=slots, up_offset=gb, down_offset=2 * gb)
-    layer = EPLayer(ops, record_timing=True, mode=args.ep_mode)
+    p2p = args.ep_mode == "p2p"
+    layer = EPLayer(ops, record_timing=True, mode=args.ep_mode, device_epoch=p2p)
     for _ in range(args.warmup):
         layer.forward(x, logits)
     torch.cuda.synchronize()
@@ -1285,12 +1286,37 @@ def run_stack_ep(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # value: timed without the phase events; the phases come from a second pass
     layer.record_timing = False
+    graph, xs, ls, y_static = None, x, logits, None
+    if p2p:
+        # the peer-memory layer numbers its calls on the device, so one captured
+        # forward replays as a whole step: every step's 15 launches from one
+        # graph launch (the Python layer's host work no longer paces the GPUs)
+        xs, ls = x.clone(), logits.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            layer.forward(xs, ls)
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y_static = layer.forward(xs, ls)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert hotpath.device_status() == 0
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            layer.forward(x, logits)
+
     with ClockSampler(local) as clocks:
         dist.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
-            layer.forward(x, logits)
+            step()
         e1.record(stream)
         torch.cuda.synchronize()
         dist.barrier()
@@ -1311,12 +1337,22 @@ def run_stack_ep(args):
     hl = torch.from_numpy(lg_np[sl]).pin_memory()
     dist.barrier()
     torch.cuda.synchronize()
-    ms_loc, hy = pipelined_e2e(lambda dx, dl, dy: dy.copy_(layer.forward(dx, dl)), hx, hl, x, logits,
+    def e2e_call(dx, dl, dy):
+        if graph is None:
+            dy.copy_(layer.forward(dx, dl))
+            return
+        xs.copy_(dx)
+        ls.copy_(dl)
+        graph.replay()
+        dy.copy_(y_static)
+
+    ms_loc, hy = pipelined_e2e(e2e_call, hx, hl, x, logits,
                                torch.empty(tp, D_MODEL, dtype=torch.float32, device="cuda"), args.steps, stream)
     ms_e = torch.tensor([ms_loc], dtype=torch.float64, device="cuda")
     dist.all_reduce(ms_e, op=dist.ReduceOp.MAX)
     assert np.isfinite(hy.numpy()).all()
     assert hotpath.device_status() == 0
+    del graph
     nbytes = step_bytes(type_id, T)
     peak, peak_kind = load_peaks()
     # the rank's expert phase streams its experts' bytes once
@@ -1330,7 +1366,7 @@ def run_stack_ep(args):
             "config": stack_config(args.type, T, world),
             "entry_point": "freemoe_b200.ep.EPLayer.forward (route, dispatch, experts, combine per step)",
             "exchange": {"p2p": "peer-memory stores fused into the dispatch and partial-sum kernels (CUDA IPC "
-                                "mailboxes, no collective in the data path)",
+                                "mailboxes, no collective in the data path); each step one CUDA graph replay",
                          "rows": "NCCL all-to-all (torch.distributed), one row per token and rank",
                          "pairs": "NCCL all-to-all (torch.distributed), one row per pair"}[args.ep_mode],
             "sharding": f"experts {per}/rank, tokens {tp}/rank",

@@ -17,7 +17,11 @@
 //                 routing weights per top-k slot (-1 / 0 for other ranks')
 //   back          f32 partial sums returned for this rank's sent rows
 // A call carries an epoch (1, 2, ...); flags are only ever raised to the
-// current epoch, so nothing is reset between calls.  Buffer reuse is ordered
+// current epoch, so nothing is reset between calls.  Epoch 0 in the three
+// calls means "the device's epoch": the dispatch call advances a counter in
+// this rank's own mailbox and every kernel of the call reads it there, so a
+// layer's calls can be captured once in a CUDA graph and replayed (a layer
+// uses either explicit epochs or device epochs, not both).  Buffer reuse is ordered
 // by the protocol itself: a rank sends epoch e+1 rows only after its epoch-e
 // partials came back from every destination, which each destination writes
 // only after it has read its epoch-e rows.
@@ -99,6 +103,14 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+// The call's epoch: the explicit one, else the device counter.
+__device__ __forceinline__ uint32_t call_epoch(uint32_t epoch, const uint32_t *ectr) {
+    return epoch ? epoch : *reinterpret_cast<const volatile uint32_t *>(ectr);
+}
+
+// Advances the device epoch counter (one thread, first kernel of a call).
+__global__ void p2p_epoch_next_kernel(uint32_t *ectr) { *ectr += 1; }
+
 // Bounded wait for flag >= epoch; false (and FENCE_TIMEOUT raised) on expiry.
 __device__ bool wait_flag(const uint32_t *flag, uint32_t epoch, uint64_t timeout_ns, int *status) {
     if (flag_acquire(flag) >= epoch) return true;
@@ -116,9 +128,10 @@ __device__ bool wait_flag(const uint32_t *flag, uint32_t epoch, uint64_t timeout
 // Thread p writes this rank's row of the count matrix into mailbox p, then
 // raises mflag[rank] there.
 __global__ void p2p_counts_kernel(uint8_t *const *peers, uint32_t world, uint32_t rank, const uint32_t *send_counts,
-                                  uint64_t off_matrix, uint64_t off_mflag, uint32_t epoch) {
+                                  uint64_t off_matrix, uint64_t off_mflag, uint32_t epoch, const uint32_t *ectr) {
     const uint32_t p = threadIdx.x;
     if (p >= world) return;
+    epoch = call_epoch(epoch, ectr);
     uint32_t *m = at<uint32_t>(peers[p], off_matrix) + static_cast<uint64_t>(rank) * world;
     for (uint32_t r = 0; r < world; ++r) m[r] = send_counts[r];
     __threadfence_system();
@@ -129,6 +142,7 @@ __global__ void p2p_counts_kernel(uint8_t *const *peers, uint32_t world, uint32_
 __global__ void p2p_plan_kernel(uint8_t *mine, Mailbox L, uint32_t world, uint32_t rank, uint32_t epoch,
                                 uint64_t timeout_ns, int *status) {
     const uint32_t lane = threadIdx.x;
+    epoch = call_epoch(epoch, at<uint32_t>(mine, L.ctr) + 2);
     for (uint32_t s = lane; s < world; s += 32) wait_flag(at<uint32_t>(mine, L.mflag) + s, epoch, timeout_ns, status);
     __syncwarp();
     if (lane != 0) return;
@@ -162,6 +176,7 @@ __global__ void p2p_pack_send_kernel(const XT *__restrict__ x, const uint32_t *_
                                      uint32_t world, uint32_t rank, uint32_t d, uint8_t *const *peers, uint8_t *mine,
                                      Mailbox L, uint32_t cap, uint32_t epoch, int *status) {
     const uint32_t j = blockIdx.x;
+    epoch = call_epoch(epoch, at<uint32_t>(mine, L.ctr) + 2);
     if (j < send_offsets[world]) {
         const uint32_t item = items[j], t = item / world, dest = item % world;
         const uint32_t pos = at<uint32_t>(mine, L.my_pos)[dest] + (j - send_offsets[dest]);
@@ -174,7 +189,10 @@ __global__ void p2p_pack_send_kernel(const XT *__restrict__ x, const uint32_t *_
         const XT *src = x + static_cast<uint64_t>(t) * d;
         uint4 *dst = reinterpret_cast<uint4 *>(at<__half>(peer, L.recv_x) + static_cast<uint64_t>(pos) * d);
         const bool vec = sizeof(XT) == 2 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-        for (uint32_t c = threadIdx.x; c < d / 8; c += blockDim.x) {
+        // this block's share of the row's 16-byte pieces (grid.y splits the row)
+        const uint32_t per = (d / 8 + gridDim.y - 1) / gridDim.y, c0 = blockIdx.y * per;
+        const uint32_t c1 = min(d / 8, c0 + per);
+        for (uint32_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
             __align__(16) __half h[8];
             if (vec) { // eight bf16 in one 16-byte load
                 const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src) + c);
@@ -192,7 +210,7 @@ __global__ void p2p_pack_send_kernel(const XT *__restrict__ x, const uint32_t *_
         }
         int32_t *me = at<int32_t>(peer, L.recv_e) + static_cast<uint64_t>(pos) * top_k;
         float *mw = at<float>(peer, L.recv_w) + static_cast<uint64_t>(pos) * top_k;
-        for (uint32_t r = threadIdx.x; r < top_k; r += blockDim.x) {
+        for (uint32_t r = threadIdx.x; blockIdx.y == 0 && r < top_k; r += blockDim.x) {
             const uint32_t e = ids[static_cast<uint64_t>(t) * top_k + r];
             const bool local = e / per_rank == dest;
             me[r] = local ? static_cast<int32_t>(e % per_rank) : -1;
@@ -205,7 +223,7 @@ done:
     __syncthreads();
     if (threadIdx.x == 0) {
         uint32_t *ctr = at<uint32_t>(mine, L.ctr);
-        if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
+        if (atomicAdd(ctr, 1u) == gridDim.x * gridDim.y - 1) {
             *ctr = 0;
             __threadfence_system();
             for (uint32_t r = 0; r < world; ++r) flag_release(at<uint32_t>(peers[r], L.dflag) + rank, epoch);
@@ -214,19 +232,22 @@ done:
 }
 
 // One warp waits until every source's rows (flag `off_flag`) are in.
-__global__ void p2p_wait_kernel(uint8_t *mine, uint64_t off_flag, uint32_t world, uint32_t epoch, uint64_t timeout_ns,
-                                int *status) {
+__global__ void p2p_wait_kernel(uint8_t *mine, uint64_t off_flag, uint32_t world, uint32_t epoch, uint64_t off_ctr,
+                                uint64_t timeout_ns, int *status) {
+    epoch = call_epoch(epoch, at<uint32_t>(mine, off_ctr) + 2);
     for (uint32_t s = threadIdx.x; s < world; s += 32)
         wait_flag(at<uint32_t>(mine, off_flag) + s, epoch, timeout_ns, status);
 }
 
-// Block j (< rows received): partial[j] = sum over the row's top-k slots of
-// w_r * out[j*k + r] (top-k order, multiply then add), written straight into
-// the source rank's return rows.  The last block raises bflag[rank] there.
+// Block (j, c) (j < rows received): columns piece c of partial[j] = sum over
+// the row's top-k slots of w_r * out[j*k + r] (top-k order, multiply then add),
+// written straight into the source rank's return rows.  The last block to
+// finish raises bflag[rank] there.
 __global__ void p2p_partial_return_kernel(const float *__restrict__ out, uint32_t top_k, uint32_t d, uint32_t world,
                                           uint32_t rank, uint8_t *const *peers, uint8_t *mine, Mailbox L, uint32_t cap,
                                           uint32_t epoch, int *status) {
     const uint32_t j = blockIdx.x;
+    epoch = call_epoch(epoch, at<uint32_t>(mine, L.ctr) + 2);
     const uint32_t n = *at<uint32_t>(mine, L.n_recv);
     if (j < n) {
         const uint32_t *recv_off = at<uint32_t>(mine, L.recv_off);
@@ -241,7 +262,9 @@ __global__ void p2p_partial_return_kernel(const float *__restrict__ out, uint32_
         const int32_t *me = at<int32_t>(mine, L.recv_e) + static_cast<uint64_t>(j) * top_k;
         const float *mw = at<float>(mine, L.recv_w) + static_cast<uint64_t>(j) * top_k;
         float4 *dst = reinterpret_cast<float4 *>(at<float>(peers[s], L.back) + static_cast<uint64_t>(pos) * d);
-        for (uint32_t c = threadIdx.x; c < d / 4; c += blockDim.x) {
+        const uint32_t per = (d / 4 + gridDim.y - 1) / gridDim.y, c0 = blockIdx.y * per;
+        const uint32_t c1 = min(d / 4, c0 + per);
+        for (uint32_t c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             for (uint32_t r = 0; r < top_k; ++r) {
                 if (me[r] < 0) continue;
@@ -261,7 +284,7 @@ done:
     __syncthreads();
     if (threadIdx.x == 0) {
         uint32_t *ctr = at<uint32_t>(mine, L.ctr) + 1;
-        if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
+        if (atomicAdd(ctr, 1u) == gridDim.x * gridDim.y - 1) {
             *ctr = 0;
             __threadfence_system();
             for (uint32_t r = 0; r < world; ++r) flag_release(at<uint32_t>(peers[r], L.bflag) + rank, epoch);
@@ -366,7 +389,6 @@ extern "C" int fmcuda_ep_p2p_dispatch(const uint32_t *ids, const float *weights,
         return set_error(FM_STATUS_INVALID_ARGUMENT, "null peer-dispatch pointer");
     if (x_dtype != FM_X_F32 && x_dtype != FM_X_BF16)
         return set_error(FM_STATUS_INVALID_ARGUMENT, "unknown activation dtype");
-    if (epoch == 0) return set_error(FM_STATUS_INVALID_ARGUMENT, "epochs start at 1");
     if (experts_per_rank == 0) return set_error(FM_STATUS_INVALID_ARGUMENT, "no experts per rank");
     const uint64_t n64 = static_cast<uint64_t>(tokens) * world;
     if (n64 > capacity) return set_error(FM_STATUS_INVALID_ARGUMENT, "tokens x world exceeds the mailbox capacity");
@@ -386,11 +408,17 @@ extern "C" int fmcuda_ep_p2p_dispatch(const uint32_t *ids, const float *weights,
     if ((rc = launch_group_large(keys, n, world, counts, offsets, items, row_of, gscratch, s))) return rc;
     uint8_t *const *pp = reinterpret_cast<uint8_t *const *>(peers);
     uint8_t *mine = static_cast<uint8_t *>(mailbox);
-    p2p_counts_kernel<<<1, 64, 0, s>>>(pp, world, rank, counts, L.matrix, L.mflag, epoch);
+    if (epoch == 0) { // device epochs: this call's epoch is the counter's next value
+        p2p_epoch_next_kernel<<<1, 1, 0, s>>>(reinterpret_cast<uint32_t *>(mine + L.ctr) + 2);
+        if ((rc = check_launch("peer epoch launch"))) return rc;
+    }
+    p2p_counts_kernel<<<1, 64, 0, s>>>(pp, world, rank, counts, L.matrix, L.mflag, epoch,
+                                       reinterpret_cast<const uint32_t *>(mine + L.ctr) + 2);
     if ((rc = check_launch("peer counts launch"))) return rc;
     p2p_plan_kernel<<<1, 32, 0, s>>>(mine, L, world, rank, epoch, timeout_ns_of(timeout_ms), device_status_word());
     if ((rc = check_launch("peer plan launch"))) return rc;
-    const unsigned grid = n ? n : 1;
+    // rows x column pieces of 128 x 16 bytes (one piece per thread)
+    const dim3 grid(n ? n : 1, (d_model / 8 + 127) / 128);
     if (x_dtype == FM_X_F32)
         p2p_pack_send_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float *>(x), ids, weights, items, offsets,
                                                          top_k, experts_per_rank, world, rank, d_model, pp, mine, L,
@@ -417,7 +445,6 @@ extern "C" int fmcuda_ep_p2p_experts(void *mailbox, void *const *peers, uint32_t
     int rc = check_p2p(world, rank, capacity, d_model, top_k);
     if (rc) return rc;
     if (!mailbox || !peers || !expert_slots || !workspace) return set_error(FM_STATUS_INVALID_ARGUMENT, "null peer-experts pointer");
-    if (epoch == 0) return set_error(FM_STATUS_INVALID_ARGUMENT, "epochs start at 1");
     const uint64_t need = fmcuda_ep_p2p_experts_workspace_bytes(capacity, top_k, experts, d_model, ffn);
     if (workspace_bytes < need)
         return set_error(FM_STATUS_INVALID_ARGUMENT, "peer-experts workspace too small: need " + std::to_string(need));
@@ -425,7 +452,7 @@ extern "C" int fmcuda_ep_p2p_experts(void *mailbox, void *const *peers, uint32_t
     const Mailbox L = mailbox_layout(world, capacity, top_k, d_model);
     uint8_t *const *pp = reinterpret_cast<uint8_t *const *>(peers);
     uint8_t *mine = static_cast<uint8_t *>(mailbox);
-    p2p_wait_kernel<<<1, 32, 0, s>>>(mine, L.dflag, world, epoch, timeout_ns_of(timeout_ms), device_status_word());
+    p2p_wait_kernel<<<1, 32, 0, s>>>(mine, L.dflag, world, epoch, L.ctr, timeout_ns_of(timeout_ms), device_status_word());
     if ((rc = check_launch("peer wait launch"))) return rc;
     float *out_pairs = static_cast<float *>(workspace);
     uint8_t *ws = static_cast<uint8_t *>(workspace) + a256(static_cast<uint64_t>(capacity) * top_k * d_model * 4);
@@ -435,7 +462,7 @@ extern "C" int fmcuda_ep_p2p_experts(void *mailbox, void *const *peers, uint32_t
                                   up_offset, down_offset, gate_type, up_type, down_type, d_model, ffn, out_pairs, ws,
                                   workspace_bytes - (ws - static_cast<uint8_t *>(workspace)), s)))
         return rc;
-    p2p_partial_return_kernel<<<capacity, 128, 0, s>>>(out_pairs, top_k, d_model, world, rank, pp, mine, L, capacity,
+    p2p_partial_return_kernel<<<dim3(capacity, (d_model / 4 + 127) / 128), 128, 0, s>>>(out_pairs, top_k, d_model, world, rank, pp, mine, L, capacity,
                                                        epoch, device_status_word());
     return check_launch("peer partial-return launch");
 }
@@ -446,11 +473,10 @@ extern "C" int fmcuda_ep_p2p_combine(void *mailbox, uint32_t world, uint32_t ran
     int rc = check_p2p(world, rank, capacity, d_model, top_k);
     if (rc) return rc;
     if (!mailbox || !row_of || !y) return set_error(FM_STATUS_INVALID_ARGUMENT, "null peer-combine pointer");
-    if (epoch == 0) return set_error(FM_STATUS_INVALID_ARGUMENT, "epochs start at 1");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const Mailbox L = mailbox_layout(world, capacity, top_k, d_model);
     uint8_t *mine = static_cast<uint8_t *>(mailbox);
-    p2p_wait_kernel<<<1, 32, 0, s>>>(mine, L.bflag, world, epoch, timeout_ns_of(timeout_ms), device_status_word());
+    p2p_wait_kernel<<<1, 32, 0, s>>>(mine, L.bflag, world, epoch, L.ctr, timeout_ns_of(timeout_ms), device_status_word());
     if ((rc = check_launch("peer wait launch"))) return rc;
     if (tokens == 0) return FM_STATUS_OK;
     const uint64_t n = static_cast<uint64_t>(tokens) * d_model;

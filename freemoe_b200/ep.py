@@ -248,7 +248,7 @@ class EPLayer:
     PHASES = ("route", "dispatch", "counts", "rows_out", "experts", "rows_back", "combine")
 
     def __init__(self, ops, group=None, record_timing: bool = False, mode: str = "rows", capacity: int = 0,
-                 timeout_ms: int = 0):
+                 timeout_ms: int = 0, device_epoch: bool = False):
         if mode not in ("rows", "pairs", "p2p"):
             raise ValueError(f"unknown exchange mode {mode!r}")
         self.ops, self.group, self.mode = ops, group, mode
@@ -262,6 +262,10 @@ class EPLayer:
         # mode "p2p": mailboxes are set up on the first call (capacity = the
         # largest tokens per rank of that call x world unless given)
         self.capacity, self.timeout_ms, self.epoch = capacity, timeout_ms, 0
+        # mode "p2p" with device_epoch: the kernels number the calls themselves
+        # (epoch 0 to the library), so forward() can be captured in a CUDA graph
+        # once the mailboxes exist (after the first call) and replayed
+        self.device_epoch = device_epoch
 
     def close(self):
         """Releases the peer mailboxes (mode "p2p"); collective over the group."""
@@ -278,17 +282,18 @@ class EPLayer:
                 self.capacity = int(t.item()) * self.world
             ops.p2p_setup(self.world, self.rank, self.capacity, self.group, self.timeout_ms)
         self.epoch += 1
+        ep = 0 if self.device_epoch else self.epoch
         self._mark()
         ids, w = ops.route(logits)
         self._mark()
-        row_of = ops.p2p_dispatch(ids, w, x, self.epoch)
+        row_of = ops.p2p_dispatch(ids, w, x, ep)
         self._mark()
         self._mark()  # counts: inside the dispatch kernels
         self._mark()  # rows out: written by the dispatch kernel
-        ops.p2p_experts(self.epoch)
+        ops.p2p_experts(ep)
         self._mark()  # the partial sums go back from the experts call
         self._mark()
-        y = ops.p2p_combine(row_of, x.shape[0], self.epoch)
+        y = ops.p2p_combine(row_of, x.shape[0], ep)
         self._mark()
         return y
 

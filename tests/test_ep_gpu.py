@@ -92,6 +92,28 @@ def test_p2p_decode_single_rank(cuda, oracle):
             err_o = float(np.abs(y.cpu().numpy() - y_o).max() / np.abs(y_o).max())
             assert err_o <= 1e-3, err_o
         layer.close()
+        # device epochs: one forward captured in a CUDA graph and replayed, each
+        # replay equal to the explicit-epoch calls bit for bit
+        g_layer = EPLayer(ops, mode="p2p", device_epoch=True)
+        y0 = g_layer.forward(x, logits)
+        torch.cuda.synchronize()
+        assert torch.equal(y0.view(torch.int32), y.view(torch.int32))
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            g_layer.forward(x, logits)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y_g = g_layer.forward(x, logits)
+        for _ in range(3):
+            y_g.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert cuda.device_status() == 0
+            assert torch.equal(y_g.view(torch.int32), y.view(torch.int32))
+        del graph
+        g_layer.close()
     finally:
         dist.destroy_process_group()
 
