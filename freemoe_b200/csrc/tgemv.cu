@@ -26,11 +26,11 @@ int tg_sm_count() {
     return n;
 }
 
-template <int NMAT> int tg_configure() {
+template <int MODE> int tg_configure() {
     static int done = 0;
     if (!done) {
-        const cudaError_t err = cudaFuncSetAttribute(tgemv_kernel<NMAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     TgLayout<NMAT>::smem_bytes(TG_MAX_EXPERTS));
+        const cudaError_t err = cudaFuncSetAttribute(tgemv_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     TgLayout<MODE>::smem_bytes(TG_MAX_EXPERTS));
         if (err != cudaSuccess) return cuda_status(err, "tgemv shared-memory attribute");
         done = 1;
     }
@@ -101,8 +101,8 @@ bool tg_eligible(const fmcuda_moe_args *a) {
 int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
                     uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
     int rc;
-    if ((rc = tg_configure<2>())) return rc;
-    if ((rc = tg_configure<1>())) return rc;
+    if ((rc = tg_configure<TG_GATE_UP>())) return rc;
+    if ((rc = tg_configure<TG_DOWN>())) return rc;
     const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
     const uint32_t n_cnt = tiles * (t.ffn / TG_ROWS + t.d / TG_ROWS);
     TgMapArgs ma{};
@@ -145,7 +145,7 @@ int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *p
     gu.partial = partial;
     gu.unit_cnt = cnt;
     gu.status = device_status_word();
-    tgemv_kernel<2><<<grid, TG_THREADS, TgLayout<2>::smem_bytes(t.experts), s>>>(gu);
+    tgemv_kernel<TG_GATE_UP><<<grid, TG_THREADS, TgLayout<TG_GATE_UP>::smem_bytes(t.experts), s>>>(gu);
     if ((rc = check_launch("tgemv gate/up"))) return rc;
     mark(mark_ctx, 4);
     mark(mark_ctx, 5);
@@ -161,7 +161,7 @@ int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *p
     dn.part = part;
     dn.out_rows = t.out_rows;
     dn.unit_cnt = cnt + tiles * (t.ffn / TG_ROWS);
-    tgemv_kernel<1><<<grid, TG_THREADS, TgLayout<1>::smem_bytes(t.experts), s>>>(dn);
+    tgemv_kernel<TG_DOWN><<<grid, TG_THREADS, TgLayout<TG_DOWN>::smem_bytes(t.experts), s>>>(dn);
     if ((rc = check_launch("tgemv down"))) return rc;
     mark(mark_ctx, 6);
     return FM_STATUS_OK;

@@ -39,18 +39,24 @@
 //   gate/up (one x plane): accumulator columns 0-7 = codes x tokens (image rows
 //          0-7; rows 8-15 are zero), columns 8-15 = mins x sums (sums image
 //          rows 8-15; rows 0-7 are zero), one 16-column accumulator per matrix.
-//   down   (act in two fp16 planes hi + lo): per MMA issuer 16 columns (0-7 hi,
-//          8-15 lo), then 16 columns of mins (0-7).
+//   down   (act in two fp16 planes hi + lo): a step takes two 128-row tiles of
+//          the down matrix (two rows per thread, as gate/up), 16 columns per
+//          tile (0-7 hi, 8-15 lo), then one 16-column mins accumulator for both
+//          tiles: the sums image holds X in rows 0-7 at K 0-15 and in rows 8-15
+//          at K 16-31 (zeros elsewhere), so tile 0's mins MMA (K 0-15) fills
+//          columns 0-7 and tile 1's (K 16-31) columns 8-15, both issued in order
+//          by one thread.
 //
 // CTA = 13 warps, one per SM, two pipelines (p = 2 x CTA + w):
 //   warp 0        producer of both pipelines: per step one bulk copy of the B
 //                 image and one TMA box per matrix, polled without blocking;
 //   warps 1-4     MMA issuers, two per pipeline (warp 1 + 2w + i; one thread
-//                 each: M = 128, N = 16, K = 16): gate/up one per matrix, down
-//                 one per chunk parity, each into its own accumulator (fixed
+//                 each: M = 128, N = 16, K = 16): one per matrix (gate/up) or
+//                 row tile (down), each into its own accumulator (fixed
 //                 summation order);
 //   warps 5-12    converters, four per pipeline (warp v reaches TMEM lanes
-//                 32 (v % 4) ..): decode their 32 rows of every matrix into TMEM,
+//                 32 (v % 4) ..): decode their 32 rows of both matrices (row
+//                 tiles) into TMEM,
 //                 read the accumulators back and run the epilogue.
 // Work split ("stream-K"): the (unit, block) steps of all units are divided
 // into equal contiguous ranges, one per pipeline.  A unit split between
@@ -101,12 +107,15 @@ struct TgParams {
     uint8_t *out_img;            // gate/up: the down GEMV's images [tile][out_dim / 256][TG_IMG]
     float *part;                 // down: [pair][out_dim]
     const uint32_t *out_rows;    // down: part row of grouped pair g (NULL: g)
-    float *partial;              // stream-K parts [pipeline][2][NMAT][TG_NT][128]
+    float *partial;              // stream-K parts [pipeline][2][2][TG_NT][128]
     uint32_t *unit_cnt;          // stream-K arrivals per unit (zero on entry, left zero)
     int *status;
 };
 
-template <int NMAT> struct TgLayout {
+enum { TG_GATE_UP = 0, TG_DOWN = 1 };
+
+template <int MODE> struct TgLayout {
+    static constexpr uint32_t NMAT = 2;                    // matrices (gate/up) or row tiles (down) per step
     static constexpr uint32_t STAGE = NMAT * TG_BOX;      // one step's raw boxes
     static constexpr uint32_t P = TG_RAW / STAGE;          // raw stages per pipeline
     static constexpr uint32_t OFF_RAW = 2 * TG_XS * TG_IMG;
@@ -116,12 +125,12 @@ template <int NMAT> struct TgLayout {
     static constexpr uint32_t OFF_TILES = OFF_MISC + 64;
     static constexpr uint32_t smem_bytes(uint32_t experts) { return 1024 + OFF_TILES + 4 * (experts + 1); }
     // TMEM columns inside a pipeline's 256
-    static constexpr uint32_t ACC_COLS = NMAT == 2 ? 32 : 48;  // one buffer's accumulators
+    static constexpr uint32_t ACC_COLS = MODE == TG_GATE_UP ? 32 : 48;  // one buffer's accumulators
     static constexpr uint32_t ACC = 0;                         // [2 buffers][ACC_COLS]
     static constexpr uint32_t ASTG = 2 * ACC_COLS;             // [2 stages][NMAT * 32]
     static constexpr uint32_t MINS = ASTG + 2 * NMAT * 32;     // [2 buffers][NMAT * 8]
     static_assert(MINS + 2 * NMAT * 8 <= 256, "TMEM columns of one pipeline");
-    static_assert(P >= 2 && P <= 4 && P * STAGE == TG_RAW, "raw ring");
+    static_assert(P == 2 && P * STAGE == TG_RAW, "raw ring");
     static_assert(1024 + OFF_TILES + 4 * (TG_MAX_EXPERTS + 1) <= 227u * 1024u, "shared memory per CTA");
 };
 
@@ -274,9 +283,11 @@ __host__ __device__ __forceinline__ uint32_t tg_sw_off(uint32_t n, uint32_t k) {
 }
 
 
-template <int NMAT>
+template <int MODE>
 __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) {
-    using L = TgLayout<NMAT>;
+    using L = TgLayout<MODE>;
+    constexpr int NMAT = 2;
+    constexpr bool DN = MODE == TG_DOWN;
     extern __shared__ uint8_t tg_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tg_smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
@@ -315,7 +326,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             }
             for (uint32_t q = 0; q < 2; ++q) {
                 mbar_init(&b.a_full[q], 4);
-                mbar_init(&b.a_free[q], NMAT == 2 ? 2 : 1);
+                mbar_init(&b.a_free[q], 2); // both issuers read every chunk
                 mbar_init(&b.acc_full[q], 2);
                 mbar_init(&b.acc_free[q], 4);
                 mbar_init(&b.drain[q], 1);
@@ -328,7 +339,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         if (threadIdx.x == 0) raise_device_status(p.status, static_cast<int>(misc[2]));
         return;
     }
-    const uint32_t row_tiles = p.out_dim / TG_ROWS, nb = p.in_dim / 256;
+    const uint32_t row_tiles = p.out_dim / (DN ? 2 * TG_ROWS : TG_ROWS), nb = p.in_dim / 256;
     const uint64_t W = static_cast<uint64_t>(s_tile[E]) * row_tiles * nb;
     if (W == 0) return;
 
@@ -371,7 +382,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                         g[w] = tg_unit(s_tile, E, row_tiles, u, p.counts, p.offsets);
                         if (g[w].e != old_e)
 #pragma unroll
-                            for (int m = 0; m < NMAT; ++m) tma_fence_acquire(p.maps + 3 * g[w].e + p.map0 + m);
+                            for (int m = 0; m < (DN ? 1 : NMAT); ++m)
+                                tma_fence_acquire(p.maps + 3 * g[w].e + p.map0 + m);
                         cur_u[w] = u;
                     }
                     uint8_t *xdst = smem + (w * TG_XS + xs) * TG_IMG;
@@ -382,8 +394,9 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                     mbar_expect_tx(&bw[w].raw_full[rs], L::STAGE);
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m)
-                        tma_load_2d(rdst + m * TG_BOX, p.maps + 3 * g[w].e + p.map0 + m,
-                                    static_cast<int32_t>(b * TG_RB), static_cast<int32_t>(g[w].rho * TG_ROWS),
+                        tma_load_2d(rdst + m * TG_BOX, p.maps + 3 * g[w].e + p.map0 + (DN ? 0 : m),
+                                    static_cast<int32_t>(b * TG_RB),
+                                    static_cast<int32_t>((DN ? 2 * g[w].rho + m : g[w].rho) * TG_ROWS),
                                     &bw[w].raw_full[rs]);
                     ++j[w];
                     progress = true;
@@ -423,28 +436,34 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 if (!tg_wait(&bw.acc_free[ab], ((j >> 1) & 1u) ^ 1u, abort_flag, p.status)) break;
                 tc_fence_after();
                 const uint64_t bd0 = smem_desc_sw128(smem_u32(smem + (wg * TG_XS + st) * TG_IMG));
-                const uint32_t acc = tw + L::ACC + ab * L::ACC_COLS + iss * 16u;
+                const uint32_t acc = tw + L::ACC + ab * L::ACC_COLS + iss * 16u; // matrix / row tile iss
                 bool ok = true;
 #pragma unroll
                 for (uint32_t c = 0; c < 4; ++c) {
-                    if (NMAT == 1 && (c & 1u) != iss) continue; // down: this issuer's chunk parity
                     const uint32_t cc = 4 * j + c, as = cc & 1u;
                     if (!tg_wait(&bw.a_full[as], (cc >> 1) & 1u, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t astg = tw + L::ASTG + as * (NMAT * 32u) + (NMAT == 2 ? iss * 32u : 0u);
+                    const uint32_t astg = tw + L::ASTG + as * (NMAT * 32u) + iss * 32u;
 #pragma unroll
                     for (uint32_t kk = 0; kk < 4; ++kk)
-                        mma_f16_ts(acc, astg + kk * 8u, bd0 + ((c * 2048u + kk * 32u) >> 4), idesc,
-                                   (NMAT == 2 ? c : (c > iss ? 1u : 0u)) != 0u || kk != 0u);
-                    if (c == 0 && (NMAT == 2 || iss == 0)) {
+                        mma_f16_ts(acc, astg + kk * 8u, bd0 + ((c * 2048u + kk * 32u) >> 4), idesc, (c | kk) != 0u);
+                    if (c == 0) {
                         // the block's mins (their A was stored before chunk 0's arrival)
                         const uint64_t bm = bd0 + (TG_MINS_OFF >> 4);
                         const uint32_t ma = tw + L::MINS + ab * (NMAT * 8u);
-                        if (NMAT == 2) mma_f16_ts(acc, ma + iss * 8u, bm, idesc, 1u);
-                        else mma_f16_ts(tw + L::ACC + ab * L::ACC_COLS + 32u, ma, bm, idesc, 0u);
+                        if (!DN) {
+                            mma_f16_ts(acc, ma + iss * 8u, bm, idesc, 1u);
+                        } else if (iss == 0) {
+                            // both row tiles into one accumulator, in order: tile 0 from
+                            // K 0-15 of the sums image (columns 0-7), tile 1 from K 16-31
+                            // (columns 8-15)
+                            const uint32_t am = tw + L::ACC + ab * L::ACC_COLS + 32u;
+                            mma_f16_ts(am, ma, bm, idesc, 0u);
+                            mma_f16_ts(am, ma + 8u, bm + (32u >> 4), idesc, 1u);
+                        }
                     }
                     issued = true;
                     tc_commit(&bw.a_free[as]);
@@ -487,7 +506,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             tc_fence_after();
             uint32_t a[32];
             tmem_ld32(tw + L::ACC + ab * L::ACC_COLS, a);
-            if (NMAT == 2) {
+            if (!DN) {
                 tmem_wait_ld();
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
@@ -496,14 +515,16 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                         tot[m][n] = fmaf(pd[m], __uint_as_float(a[16 * m + n]),
                                          fmaf(-pdm[m], __uint_as_float(a[16 * m + 8 + n]), tot[m][n]));
             } else {
-                uint32_t mn[8];
+                uint32_t mn[8], mn1[8];
                 tmem_ld8(tw + L::ACC + ab * L::ACC_COLS + 32u, mn);
+                tmem_ld8(tw + L::ACC + ab * L::ACC_COLS + 40u, mn1);
                 tmem_wait_ld();
 #pragma unroll
                 for (uint32_t n = 0; n < TG_NT; ++n) {
-                    const float c0 = __uint_as_float(a[n]) + __uint_as_float(a[8 + n]);
-                    const float c1 = __uint_as_float(a[16 + n]) + __uint_as_float(a[24 + n]);
-                    tot[0][n] = fmaf(pd[0], c0 + c1, fmaf(-pdm[0], __uint_as_float(mn[n]), tot[0][n]));
+                    tot[0][n] = fmaf(pd[0], __uint_as_float(a[n]) + __uint_as_float(a[8 + n]),
+                                     fmaf(-pdm[0], __uint_as_float(mn[n]), tot[0][n]));
+                    tot[1][n] = fmaf(pd[1], __uint_as_float(a[16 + n]) + __uint_as_float(a[24 + n]),
+                                     fmaf(-pdm[1], __uint_as_float(mn1[n]), tot[1][n]));
                 }
             }
             tc_fence_before();
@@ -569,8 +590,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                             if (n < g.ntok) val[m][n] += __ldcg(src + (m * TG_NT + n) * TG_ROWS + r);
                 }
             }
-            const uint32_t f = g.rho * TG_ROWS + r; // output row
-            if (NMAT == 2) {
+            if (!DN) {
+                const uint32_t f = g.rho * TG_ROWS + r; // output feature
                 // SwiGLU (include/fm/activation.hpp:62-84), then the down GEMV's B image:
                 // act hi plane in rows 0-7, lo plane in rows 8-15, at the staged k
                 // position of feature f; sub-block sums of 32 features (one warp)
@@ -587,15 +608,26 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                     *reinterpret_cast<__half *>(chunk + tg_sw_off(n, kpos)) = h;
                     *reinterpret_cast<__half *>(chunk + tg_sw_off(8 + n, kpos)) = l;
                 }
+                // sums image of the down GEMV: X (hi at K j, lo at K 8 + j) in rows 0-7 for
+                // its first row tile and (K 16 + j, 24 + j) in rows 8-15 for its second,
+                // zeros in the other half of each row
                 const uint32_t jsub = (f & 255u) >> 5;
+                const __half z = __float2half_rn(0.0f);
 #pragma unroll
                 for (uint32_t n = 0; n < TG_NT; ++n) {
                     const float X = warp_sum(act[n]);
                     if (lane == 0) {
                         const __half h = __float2half_rn(X);
                         const __half l = __float2half_rn(X - __half2float(h));
-                        *reinterpret_cast<__half *>(img + TG_MINS_OFF + tg_sw_off(n, jsub)) = h;
-                        *reinterpret_cast<__half *>(img + TG_MINS_OFF + tg_sw_off(n, 8 + jsub)) = l;
+                        uint8_t *mi = img + TG_MINS_OFF;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(n, jsub)) = h;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(n, 8 + jsub)) = l;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(n, 16 + jsub)) = z;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(n, 24 + jsub)) = z;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(8 + n, jsub)) = z;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(8 + n, 8 + jsub)) = z;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(8 + n, 16 + jsub)) = h;
+                        *reinterpret_cast<__half *>(mi + tg_sw_off(8 + n, 24 + jsub)) = l;
                     }
                 }
             } else {
@@ -603,7 +635,9 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 for (uint32_t n = 0; n < TG_NT; ++n)
                     if (n < g.ntok) {
                         const uint32_t row = p.out_rows ? __ldg(p.out_rows + g.pair0 + n) : g.pair0 + n;
-                        p.part[static_cast<uint64_t>(row) * p.out_dim + f] = val[0][n];
+#pragma unroll
+                        for (int m = 0; m < NMAT; ++m)
+                            p.part[static_cast<uint64_t>(row) * p.out_dim + (2 * g.rho + m) * TG_ROWS + r] = val[m][n];
                     }
             }
             return true;
@@ -621,7 +655,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             TgHdr hd[2];
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
-                rows[m] = raw + rs * L::STAGE + (m < NMAT ? m : 0) * TG_BOX;
+                rows[m] = raw + rs * L::STAGE + m * TG_BOX;
                 hd[m] = tg_hdr(*reinterpret_cast<const uint4 *>(rows[m]));
             }
             // mins A of this step (its buffer was last read by step j - 2's MMAs,
