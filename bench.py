@@ -534,7 +534,7 @@ def run_ours(args):
         "tokens_per_s": world * T / (ms / 1e3),
         "pct_of_8tbs": value / world / 8000.0 * 100.0,
         "stage_ms": report_stages(stage_ms, T),
-        "roofline": {"bound": "hbm", "kernel": ("tgemv_kernel<2> gate/up + SwiGLU (tcgen05), 8 experts" if type_id == 12
+        "roofline": {"bound": "hbm", "kernel": ("tgemv_kernel<0> gate/up + SwiGLU (tcgen05), 8 experts" if type_id == 12
                                                 else "qgemv_async_kernel gate/up + SwiGLU (mma.sync), 8 experts"),
                      "achieved": gu_achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": gu_achieved / peak,
