@@ -211,9 +211,10 @@ def pipelined_e2e(call, hx, hl, like_x, like_l, like_y, steps, stream):
 
 def report_stages(stage_ms: dict, tokens: int, experts: int = EXPERTS) -> dict:
     """Per-stage device times of one decode MoE block.  Up to 64 tokens and 64
-    experts (plain router) the router, grouping and x planes are one launch and
-    the down projection's x planes are written by the gate/up epilogue, so the
-    library's events between those stages time nothing: report the launches."""
+    experts (plain router) the router, grouping and x planes (Q4_K: B images)
+    are one launch and the down projection's x planes (images) are written by
+    the gate/up epilogue, so the library's events between those stages time
+    nothing: report the launches."""
     if tokens <= 64 and experts <= 64:
         return {"front": stage_ms["router"] + stage_ms["grouping"] + stage_ms["x_planes"],
                 "gate_up": stage_ms["gate_up"] + stage_ms["act_planes"], "down": stage_ms["down"],
@@ -542,9 +543,9 @@ def run_ours(args):
                      "down_achieved": (EXPERTS * D_MODEL * row_bytes(type_id, FFN)) / (dn_ms / 1e3) / 1e9},
         "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": ms_e2e},
-        # Q4_K: router + grouping, B images, gate/up (+ down's B images), down, combine;
+        # Q4_K: router + grouping + B images, gate/up (+ down's B images), down, combine;
         # Q8_0: router + grouping + x planes, gate/up (+ down's x planes), down, combine
-        "gpu_launches": (5 if type_id == 12 else 4) * args.steps,
+        "gpu_launches": 4 * args.steps,
         "clocks": clocks.summary(),
     }
 
@@ -764,7 +765,7 @@ def run_layer(args):
         line["roofline"] = {"bound": "hbm", "kernel": "MoE block (distinct experts' bytes)",
                             "achieved": line["hbm_gbs"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
                             "frac": line["hbm_gbs"] / peak, "traffic": None, "algorithmic_bytes": wbytes}
-        line["gpu_launches"] = (5 if t == 12 else 4) * args.steps
+        line["gpu_launches"] = 4 * args.steps
 
     if not args.no_cpu:
         # the reference's CPU code on a bounded sample of the same tokens

@@ -12,6 +12,10 @@
 //   7. combine       y[t] = sum over r of w[t,r] * part[slot_of(t,r)], in top-k
 //                    order, multiply then add (src/engine.cpp:1770)
 // Each expert's weight rows are read once per 8 of its tokens.
+// Q4_K experts with bf16 activations take the tcgen05 expert stage (tgemv.cu)
+// instead of 3-6: for short batches with the plain router one launch
+// (tg_front_kernel) routes, groups and writes the gate/up B images, then the
+// gate/up and down GEMVs and the combine: four launches per block.
 #include <string>
 
 #include "gemv_async.cuh"
@@ -174,6 +178,7 @@ int launch_combine(const float *part, const float *weights, const uint32_t *slot
     return check_launch("combine launch");
 }
 
+
 // Shared by the allocating entry point and any variant that brings its own scratch.
 int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_bytes,
                   cudaStream_t s) {
@@ -236,27 +241,10 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
     mark(0);
     if (tg_eligible(a)) {
         // Q4_K experts, bf16 activations: the tcgen05 expert stage (tgemv.cu)
-        if (plain_router && a->tokens <= kFrontMaxTokens && a->experts <= kFrontMaxExperts) {
-            const int norm = cfg ? cfg->normalise : a->normalise;
-            const double eps = cfg ? cfg->epsilon : a->epsilon, scl = cfg ? cfg->scale : a->scale;
-            // one CTA: router, then grouping (no x planes on this path)
-            moe_front_kernel<__nv_bfloat16><<<1, 1024, 0, s>>>(
-                a->logits, static_cast<const __nv_bfloat16 *>(a->x), a->tokens, a->experts, a->top_k, norm, eps, scl,
-                a->d_model, 0, ids, weights, counts, offsets, pairs, slot_of, nullptr, nullptr, nullptr,
-                device_status_word());
-            if ((rc = check_launch("MoE front launch"))) return rc;
-            mark(1);
-        } else {
-            if ((rc = launch_route_cfg(a->logits, a->tokens, a->experts, a->top_k, a->router, a->normalise,
-                                       a->epsilon, a->scale, ids, weights, nullptr, s)))
-                return rc;
-            mark(1);
-            if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
-        }
-        mark(2);
         struct MarkCtx {
             decltype(mark) *fn;
         } mctx{&mark};
+        auto mark_fn = [](void *ctx, int i) { (*static_cast<MarkCtx *>(ctx)->fn)(i); };
         TgStage ts{};
         ts.x = a->x;
         ts.x_f16 = false;
@@ -272,10 +260,29 @@ int moe_block_run(const fmcuda_moe_args *a, void *workspace, uint64_t workspace_
         ts.offsets = offsets;
         ts.pairs = pairs;
         ts.out_rows = nullptr;
-        rc = tg_expert_stage(
-            ts, ws + L.tg_img_gu, ws + L.tg_img_dn, reinterpret_cast<float *>(ws + L.tg_partial),
-            reinterpret_cast<uint32_t *>(ws + L.tg_cnt), ws + L.tg_maps, part,
-            [](void *ctx, int i) { (*static_cast<MarkCtx *>(ctx)->fn)(i); }, &mctx, s);
+        if (plain_router && tg_front_eligible(a->tokens, a->experts, a->top_k)) {
+            // router, grouping and B images in one launch
+            TgFront f{};
+            f.logits = a->logits;
+            f.tokens = a->tokens;
+            f.normalise = cfg ? cfg->normalise : a->normalise;
+            f.epsilon = cfg ? cfg->epsilon : a->epsilon;
+            f.scale = cfg ? cfg->scale : a->scale;
+            f.ids = ids;
+            f.weights = weights;
+            f.slot_of = slot_of;
+            rc = tg_block_stage(ts, f, ws + L.tg_img_gu, ws + L.tg_img_dn, reinterpret_cast<float *>(ws + L.tg_partial),
+                                reinterpret_cast<uint32_t *>(ws + L.tg_cnt), ws + L.tg_maps, part, mark_fn, &mctx, s);
+        } else {
+            if ((rc = launch_route_cfg(a->logits, a->tokens, a->experts, a->top_k, a->router, a->normalise,
+                                       a->epsilon, a->scale, ids, weights, nullptr, s)))
+                return rc;
+            mark(1);
+            if ((rc = launch_group(ids, P, a->experts, counts, offsets, pairs, slot_of, s))) return rc;
+            mark(2);
+            rc = tg_expert_stage(ts, ws + L.tg_img_gu, ws + L.tg_img_dn, reinterpret_cast<float *>(ws + L.tg_partial),
+                                 reinterpret_cast<uint32_t *>(ws + L.tg_cnt), ws + L.tg_maps, part, mark_fn, &mctx, s);
+        }
         if (rc) return rc;
         if ((rc = launch_combine(part, weights, slot_of, a->tokens, a->top_k, a->d_model, a->y, s))) return rc;
         mark(7);

@@ -96,37 +96,31 @@ bool tg_eligible(const fmcuda_moe_args *a) {
            a->up_offset % 16 == 0 && a->down_offset % 16 == 0;
 }
 
-// Steps after routing and grouping: x images, gate/up + SwiGLU (writing the
-// down images), down.
-int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
-                    uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
+namespace {
+
+// Stream-K counters and the raw-weight map templates of one expert stage.
+int tg_map_args(const TgStage &t, uint32_t *cnt, uint8_t *maps_area, TgMapArgs &ma) {
     int rc;
     if ((rc = tg_configure<TG_GATE_UP>())) return rc;
     if ((rc = tg_configure<TG_DOWN>())) return rc;
     const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
-    const uint32_t n_cnt = tiles * (t.ffn / TG_ROWS + t.d / TG_ROWS);
-    TgMapArgs ma{};
+    ma = TgMapArgs{};
     ma.maps = reinterpret_cast<CUtensorMap *>(maps_area + 256);
     ma.slots = reinterpret_cast<const uint8_t *const *>(t.slots);
     ma.up_off = t.up_offset;
     ma.down_off = t.down_offset;
     ma.cnt = cnt;
-    ma.n_cnt = n_cnt;
+    ma.n_cnt = tiles * (t.ffn / TG_ROWS + t.d / TG_ROWS);
     const uint32_t rb_gu = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, t.d));
     const uint32_t rb_dn = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, t.ffn));
     if ((rc = tg_template(&ma.tmpl_gu, ma.maps, rb_gu, t.ffn))) return rc;
-    if ((rc = tg_template(&ma.tmpl_dn, ma.maps, rb_dn, t.d))) return rc;
-    if (t.x_f16)
-        tg_ximage_kernel<__half><<<tiles * (t.d / 256), 256, 0, s>>>(
-            ma, static_cast<const __half *>(t.x), t.d, t.counts, t.offsets, t.pairs, t.top_k, t.experts, tiles,
-            img_gu);
-    else
-        tg_ximage_kernel<__nv_bfloat16><<<tiles * (t.d / 256), 256, 0, s>>>(
-            ma, static_cast<const __nv_bfloat16 *>(t.x), t.d, t.counts, t.offsets, t.pairs, t.top_k, t.experts,
-            tiles, img_gu);
-    if ((rc = check_launch("tgemv x images"))) return rc;
-    mark(mark_ctx, 3);
+    return tg_template(&ma.tmpl_dn, ma.maps, rb_dn, t.d);
+}
 
+// gate/up + SwiGLU (writing the down images), then down.
+int tg_gemvs(const TgStage &t, const TgMapArgs &ma, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
+             float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
+    const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
     const uint32_t grid = static_cast<uint32_t>(tg_sm_count() < static_cast<int>(TG_MAX_CTAS) ? tg_sm_count()
                                                                                               : TG_MAX_CTAS);
     TgParams gu{};
@@ -145,6 +139,7 @@ int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *p
     gu.partial = partial;
     gu.unit_cnt = cnt;
     gu.status = device_status_word();
+    int rc;
     tgemv_kernel<TG_GATE_UP><<<grid, TG_THREADS, TgLayout<TG_GATE_UP>::smem_bytes(t.experts), s>>>(gu);
     if ((rc = check_launch("tgemv gate/up"))) return rc;
     mark(mark_ctx, 4);
@@ -165,6 +160,57 @@ int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *p
     if ((rc = check_launch("tgemv down"))) return rc;
     mark(mark_ctx, 6);
     return FM_STATUS_OK;
+}
+
+} // namespace
+
+// Steps after routing and grouping: x images, gate/up + SwiGLU (writing the
+// down images), down.
+int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
+                    uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s) {
+    TgMapArgs ma;
+    int rc = tg_map_args(t, cnt, maps_area, ma);
+    if (rc) return rc;
+    const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
+    if (t.x_f16)
+        tg_ximage_kernel<__half><<<tiles * (t.d / 256), 256, 0, s>>>(
+            ma, static_cast<const __half *>(t.x), t.d, t.counts, t.offsets, t.pairs, t.top_k, t.experts, tiles,
+            img_gu);
+    else
+        tg_ximage_kernel<__nv_bfloat16><<<tiles * (t.d / 256), 256, 0, s>>>(
+            ma, static_cast<const __nv_bfloat16 *>(t.x), t.d, t.counts, t.offsets, t.pairs, t.top_k, t.experts,
+            tiles, img_gu);
+    if ((rc = check_launch("tgemv x images"))) return rc;
+    mark(mark_ctx, 3);
+    return tg_gemvs(t, ma, img_gu, img_dn, partial, cnt, part, mark, mark_ctx, s);
+}
+
+bool tg_front_eligible(uint32_t tokens, uint32_t experts, uint32_t top_k) {
+    return tokens <= TG_FRONT_MAX_TOKENS && experts <= TG_FRONT_MAX_EXPERTS &&
+           static_cast<uint64_t>(tokens) * top_k <= TG_FRONT_MAX_PAIRS;
+}
+
+// The whole block after the router logits: router, grouping and B images in one
+// launch (tg_front_kernel, which writes ids / weights / slot_of and the grouping
+// named in `t`), then the GEMVs.
+int tg_block_stage(const TgStage &t, const TgFront &f, uint8_t *img_gu, uint8_t *img_dn, float *partial,
+                   uint32_t *cnt, uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx,
+                   cudaStream_t s) {
+    if (!tg_front_eligible(f.tokens, t.experts, t.top_k) || t.x_f16)
+        return set_error(FM_STATUS_INTERNAL_ERROR, "tg_block_stage: batch too large for the fused front");
+    TgMapArgs ma;
+    int rc = tg_map_args(t, cnt, maps_area, ma);
+    if (rc) return rc;
+    const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
+    tg_front_kernel<__nv_bfloat16><<<tiles * (t.d / 256), 256, 0, s>>>(
+        ma, f.logits, static_cast<const __nv_bfloat16 *>(t.x), f.tokens, t.experts, t.top_k, f.normalise, f.epsilon,
+        f.scale, t.d, tiles, f.ids, f.weights, const_cast<uint32_t *>(t.counts), const_cast<uint32_t *>(t.offsets),
+        const_cast<uint32_t *>(t.pairs), f.slot_of, img_gu, device_status_word());
+    if ((rc = check_launch("tgemv front"))) return rc;
+    mark(mark_ctx, 1);
+    mark(mark_ctx, 2);
+    mark(mark_ctx, 3);
+    return tg_gemvs(t, ma, img_gu, img_dn, partial, cnt, part, mark, mark_ctx, s);
 }
 
 } // namespace fmb

@@ -76,6 +76,7 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "gemv_kernels.cuh"
+#include "router_core.cuh"
 #include "tcgen05.cuh"
 
 namespace fmb {
@@ -490,6 +491,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         const uint8_t *raw = smem + L::OFF_RAW + wg * TG_RAW + r * TG_RB;
         const uint32_t first_u = static_cast<uint32_t>(s0 / nb);
         const int bar_sk = 1 + wg;
+        // (unit, block) of the next step to read back, advanced by one per read-back
+        uint32_t rb_u = first_u, rb_b = static_cast<uint32_t>(s0 - static_cast<uint64_t>(first_u) * nb);
 
         float tot[NMAT][TG_NT];
 #pragma unroll
@@ -531,8 +534,11 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             __syncwarp();
             if (lane == 0) mbar_arrive(&bw.acc_free[ab]);
 
-            const uint64_t s = s0 + j;
-            const uint32_t u = static_cast<uint32_t>(s / nb), b = static_cast<uint32_t>(s - static_cast<uint64_t>(u) * nb);
+            const uint32_t u = rb_u, b = rb_b;
+            if (++rb_b == nb) {
+                rb_b = 0;
+                ++rb_u;
+            }
             if (b != nb - 1 && j != my - 1) return true;
             // ---- the unit's epilogue --------------------------------------------
             const TgUnit g = tg_unit(s_tile, E, row_tiles, u, p.counts, p.offsets);
@@ -718,29 +724,19 @@ struct TgMapArgs {
     uint32_t n_cnt;
 };
 
-// B images of the gate/up GEMV: CTA (tile, block) writes the 16 x 256 staged
-// x values of its tile's tokens (rows >= the tile's tokens and rows 8-15
-// zero) and the sub-block sums (rows 8-15 of the sums part, as hi and lo fp16
-// planes; rows 0-7 zero).  The grid also writes the per-expert raw-weight
-// tensor maps (a copy of the template with its global address replaced by the
-// expert's matrix through tensormap.replace; experts without tokens or without
-// a usable slot are skipped, the GEMV kernels report those) and clears the
-// stream-K counters.
-template <typename XT>
-__global__ void __launch_bounds__(256)
-    tg_ximage_kernel(const __grid_constant__ TgMapArgs ma, const XT *__restrict__ x, uint32_t d,
-                     const uint32_t *__restrict__ counts, const uint32_t *__restrict__ offsets,
-                     const uint32_t *__restrict__ pairs, uint32_t top_k, uint32_t experts, uint32_t max_tiles,
-                     uint8_t *__restrict__ img) {
-    __shared__ uint32_t s_tile[TG_MAX_EXPERTS + 1];
-    __shared__ float s_x[TG_NT][256];
+// Grid-wide part of the image launch: the per-expert raw-weight tensor maps (a
+// copy of the template with its global address replaced by the expert's
+// matrix through tensormap.replace; experts without tokens or without a usable
+// slot are skipped, the GEMV kernels report those) and the cleared stream-K
+// counters.  `counts` may point to shared memory.
+__device__ __forceinline__ void tg_maps_and_counters(const TgMapArgs &ma, const uint32_t *counts, uint32_t experts) {
     const uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x, gsz = gridDim.x * blockDim.x;
     for (uint32_t i = gid; i < ma.n_cnt; i += gsz) ma.cnt[i] = 0;
     for (uint32_t id = gid; id < 3 * experts; id += gsz) {
         const uint32_t e = id / 3, m = id - 3 * e;
         const uint8_t *base = ma.slots[e];
         const uint64_t off = m == 0 ? 0 : (m == 1 ? ma.up_off : ma.down_off);
-        if (__ldg(counts + e) == 0 || !base || (reinterpret_cast<uintptr_t>(base) + off) % 16) continue;
+        if (counts[e] == 0 || !base || (reinterpret_cast<uintptr_t>(base) + off) % 16) continue;
         CUtensorMap *dst = ma.maps + id;
         const uint4 *src = reinterpret_cast<const uint4 *>(m == 2 ? &ma.tmpl_dn : &ma.tmpl_gu);
 #pragma unroll
@@ -750,9 +746,23 @@ __global__ void __launch_bounds__(256)
                      : "memory");
         asm volatile("fence.proxy.tensormap::generic.release.gpu;\n" ::: "memory");
     }
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    if (warp == 0) tg_tile_prefix(s_tile, counts, experts, lane);
-    __syncthreads();
+}
+
+struct TgImageSmem {
+    float x[TG_NT][256];
+    float sum[TG_NT][8];
+};
+
+// CTA (tile, block) of the image launch writes the 16 x 256 staged x values of
+// its tile's tokens (rows >= the tile's tokens and rows 8-15 zero) and the
+// sub-block sums (rows 8-15 of the sums part, as hi and lo fp16 planes; rows
+// 0-7 zero).  s_tile holds the exclusive tile prefix over the experts;
+// counts / offsets / pairs may point to shared memory.
+template <typename XT>
+__device__ __forceinline__ void tg_image_block(const XT *__restrict__ x, uint32_t d, const uint32_t *counts,
+                                               const uint32_t *offsets, const uint32_t *pairs, uint32_t top_k,
+                                               uint32_t experts, uint32_t max_tiles, const uint32_t *s_tile,
+                                               uint8_t *__restrict__ img, TgImageSmem &sm) {
     const uint32_t nb = d / 256;
     const uint32_t tile = blockIdx.x / nb, b = blockIdx.x - tile * nb;
     if (tile >= s_tile[experts] || tile >= max_tiles) return;
@@ -774,7 +784,7 @@ __global__ void __launch_bounds__(256)
             if constexpr (sizeof(XT) == 2 && std::is_same<XT, __half>::value) v = __half2float(xv);
             else v = __bfloat162float(xv);
         }
-        s_x[n][k] = v;
+        sm.x[n][k] = v;
     }
     __syncthreads();
     uint8_t *out = img + (static_cast<uint64_t>(tile) * nb + b) * TG_IMG;
@@ -786,7 +796,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
             for (uint32_t e = 0; e < 8; e += 2) {
                 const uint32_t k0 = 64u * c + xplane_pos(8u * q + e), k1 = 64u * c + xplane_pos(8u * q + e + 1);
-                const __half2 h = __floats2half2_rn(s_x[n][k0], s_x[n][k1]);
+                const __half2 h = __floats2half2_rn(sm.x[n][k0], sm.x[n][k1]);
                 w[e >> 1] = *reinterpret_cast<const uint32_t *>(&h);
             }
         }
@@ -794,13 +804,12 @@ __global__ void __launch_bounds__(256)
     }
     // sums: rows 8-15 = tokens 0-7, K 0-7 hi and 8-15 lo of the 8 sub-blocks
     // (each sum in ascending order by one thread)
-    __shared__ float s_sum[TG_NT][8];
     if (threadIdx.x < TG_NT * 8) {
         const uint32_t t = threadIdx.x >> 3, jj = threadIdx.x & 7u;
         float sum = 0.0f;
 #pragma unroll 8
-        for (uint32_t k = 0; k < 32; ++k) sum += s_x[t][32 * jj + k];
-        s_sum[t][jj] = sum;
+        for (uint32_t k = 0; k < 32; ++k) sum += sm.x[t][32 * jj + k];
+        sm.sum[t][jj] = sum;
     }
     __syncthreads();
     for (uint32_t i = threadIdx.x; i < 16 * 8; i += blockDim.x) {
@@ -811,7 +820,7 @@ __global__ void __launch_bounds__(256)
             __half hv[8];
 #pragma unroll
             for (uint32_t jj = 0; jj < 8; ++jj) {
-                const float sum = s_sum[t][jj];
+                const float sum = sm.sum[t][jj];
                 const __half h = __float2half_rn(sum);
                 hv[jj] = q == 0 ? h : __float2half_rn(sum - __half2float(h));
             }
@@ -822,6 +831,87 @@ __global__ void __launch_bounds__(256)
         }
         *reinterpret_cast<uint4 *>(out + TG_MINS_OFF + tg_sw_off(n, 8u * q)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
+}
+
+// B images of the gate/up GEMV from the grouping in global memory: grid =
+// (upper bound of tiles) x (d / 256) CTAs.
+template <typename XT>
+__global__ void __launch_bounds__(256)
+    tg_ximage_kernel(const __grid_constant__ TgMapArgs ma, const XT *__restrict__ x, uint32_t d,
+                     const uint32_t *__restrict__ counts, const uint32_t *__restrict__ offsets,
+                     const uint32_t *__restrict__ pairs, uint32_t top_k, uint32_t experts, uint32_t max_tiles,
+                     uint8_t *__restrict__ img) {
+    __shared__ uint32_t s_tile[TG_MAX_EXPERTS + 1];
+    __shared__ TgImageSmem sm;
+    tg_maps_and_counters(ma, counts, experts);
+    if ((threadIdx.x >> 5) == 0) tg_tile_prefix(s_tile, counts, experts, threadIdx.x & 31u);
+    __syncthreads();
+    tg_image_block(x, d, counts, offsets, pairs, top_k, experts, max_tiles, s_tile, img, sm);
+}
+
+// Router, grouping and the gate/up B images in one launch, for short batches:
+// every CTA routes all tokens and groups the pairs in its own shared memory
+// (the same device code and inputs, so the same result in every CTA), CTA 0
+// writes the routing and grouping to global memory, and CTA (tile, block)
+// writes its image from its shared copy.  Replaces the router + grouping
+// kernels and tg_ximage_kernel (one launch and one dependency instead of two).
+constexpr uint32_t TG_FRONT_MAX_TOKENS = 64, TG_FRONT_MAX_EXPERTS = 64, TG_FRONT_MAX_PAIRS = 1024;
+
+template <typename XT>
+__global__ void __launch_bounds__(256)
+    tg_front_kernel(const __grid_constant__ TgMapArgs ma, const float *__restrict__ logits, const XT *__restrict__ x,
+                    uint32_t tokens, uint32_t experts, uint32_t top_k, int normalise, double epsilon, double scale,
+                    uint32_t d, uint32_t max_tiles, uint32_t *ids, float *weights, uint32_t *counts,
+                    uint32_t *offsets, uint32_t *pairs, uint32_t *slot_of, uint8_t *__restrict__ img, int *status) {
+    __shared__ double s_ex[8][TG_FRONT_MAX_EXPERTS];
+    __shared__ float s_pr[8][TG_FRONT_MAX_EXPERTS];
+    __shared__ uint32_t s_ids[TG_FRONT_MAX_PAIRS], s_pairs[TG_FRONT_MAX_PAIRS], s_slot[TG_FRONT_MAX_PAIRS];
+    __shared__ float s_w[TG_FRONT_MAX_PAIRS];
+    __shared__ uint32_t s_cnt[TG_FRONT_MAX_EXPERTS], s_offs[TG_FRONT_MAX_EXPERTS + 1];
+    __shared__ uint32_t s_count[TG_FRONT_MAX_EXPERTS], s_off[TG_FRONT_MAX_EXPERTS], s_warp_tot[32];
+    __shared__ uint32_t s_tile[TG_FRONT_MAX_EXPERTS + 1];
+    __shared__ TgImageSmem sm;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, nwarps = blockDim.x >> 5;
+    const uint32_t P = tokens * top_k;
+    if (threadIdx.x < 32) s_warp_tot[threadIdx.x] = 0;
+    for (uint32_t t = warp; t < tokens; t += nwarps)
+        route_token(logits, t, experts, top_k, normalise, epsilon, scale, s_ids, s_w, nullptr, status, s_ex[warp],
+                    s_pr[warp], static_cast<int>(lane));
+    __syncthreads();
+    group_block(s_ids, P, experts, s_cnt, s_offs, s_pairs, s_slot, status, s_count, s_off, s_warp_tot);
+    __syncthreads();
+    if (blockIdx.x == 0) {
+        for (uint32_t i = threadIdx.x; i < P; i += blockDim.x) {
+            ids[i] = s_ids[i];
+            weights[i] = s_w[i];
+            pairs[i] = s_pairs[i];
+            slot_of[i] = s_slot[i];
+        }
+        for (uint32_t e = threadIdx.x; e <= experts; e += blockDim.x) {
+            if (e < experts) counts[e] = s_cnt[e];
+            offsets[e] = s_offs[e];
+        }
+    }
+    tg_maps_and_counters(ma, s_cnt, experts);
+    if (warp == 0) {
+        // exclusive prefix of token tiles over the experts (experts <= 64)
+        uint32_t carry = 0;
+        for (uint32_t base = 0; base < experts; base += 32) {
+            const uint32_t e = base + lane;
+            const uint32_t v = e < experts ? (s_cnt[e] + TG_NT - 1) / TG_NT : 0u;
+            uint32_t incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += t;
+            }
+            if (e < experts) s_tile[e] = carry + incl - v;
+            carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+        }
+        if (lane == 0) s_tile[experts] = carry;
+    }
+    __syncthreads();
+    tg_image_block(x, d, s_cnt, s_offs, s_pairs, top_k, experts, max_tiles, s_tile, img, sm);
 }
 
 } // namespace fmb

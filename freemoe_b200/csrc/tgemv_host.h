@@ -39,4 +39,22 @@ bool tg_eligible(const fmcuda_moe_args *a);
 int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *partial, uint32_t *cnt,
                     uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx, cudaStream_t s);
 
+// Router inputs and outputs of tg_block_stage (the plain softmax top-k router).
+struct TgFront {
+    const float *logits;
+    uint32_t tokens;
+    int normalise;
+    double epsilon, scale;
+    uint32_t *ids;
+    float *weights;
+    uint32_t *slot_of;
+};
+// A batch the fused front takes: <= 64 tokens, <= 64 experts, <= 1024 pairs.
+bool tg_front_eligible(uint32_t tokens, uint32_t experts, uint32_t top_k);
+// Router, grouping (into t.counts / t.offsets / t.pairs) and B images in one
+// launch, then gate/up + SwiGLU and down; marks 1-3 after the first launch.
+int tg_block_stage(const TgStage &t, const TgFront &f, uint8_t *img_gu, uint8_t *img_dn, float *partial,
+                   uint32_t *cnt, uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx,
+                   cudaStream_t s);
+
 } // namespace fmb
