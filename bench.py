@@ -1385,7 +1385,7 @@ def run_stack_ep(args):
             # per rank and step in mode p2p: route; dispatch keys, grouping, counts, plan,
             # pack + send; wait, expert keys, grouping, B images, gate/up, down, partial
             # return; wait, combine
-            "gpu_launches": 15 * args.steps if args.ep_mode == "p2p" else None,
+            "gpu_launches": 7 * args.steps if args.ep_mode == "p2p" else None,
             "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     layer.close()

@@ -277,11 +277,23 @@ extern "C" uint64_t fmcuda_moe_experts_partial_workspace_bytes(uint32_t rows, ui
 namespace fmb {
 // The expert GEMMs of fmcuda_moe_experts_partial up to the per-pair outputs
 // out_pairs[row * k + r] (rows = capacity when rows_dev holds the live count).
+// Whether experts_partial_run takes the fused receive front of the tcgen05
+// stage (then it also waits for the rows: the caller launches no wait).
+bool partial_fused_recv(uint32_t rows, uint32_t top_k, uint32_t experts, uint32_t d_model, uint32_t ffn,
+                        uint32_t gate_type, uint32_t up_type, uint32_t down_type, uint64_t up_offset,
+                        uint64_t down_offset) {
+    return rows > 0 && gate_type == FM_TYPE_Q4_K && up_type == FM_TYPE_Q4_K && down_type == FM_TYPE_Q4_K &&
+           up_offset % 16 == 0 && down_offset % 16 == 0 && partial_uses_tg(rows, top_k, experts, d_model, ffn) &&
+           tg_recv_eligible(rows, top_k, experts);
+}
+
+// recv: the peer exchange's receive wait, taken by the fused receive front
+// (partial_fused_recv true), else NULL.
 int experts_partial_run(const void *x, const int32_t *meta_expert, const float *meta_weight, uint32_t rows,
                         const uint32_t *rows_dev, uint32_t top_k, uint32_t experts, const void *const *expert_slots,
                         uint64_t up_offset, uint64_t down_offset, uint32_t gate_type, uint32_t up_type,
                         uint32_t down_type, uint32_t d_model, uint32_t ffn, float *out_pairs, void *workspace,
-                        uint64_t workspace_bytes, cudaStream_t s) {
+                        uint64_t workspace_bytes, cudaStream_t s, const TgRecvWait *recv) {
     if (rows == 0) return FM_STATUS_OK;
     if (!x || !meta_expert || !meta_weight || !expert_slots || !out_pairs)
         return set_error(FM_STATUS_INVALID_ARGUMENT, "null expert-compute pointer");
@@ -310,20 +322,8 @@ int experts_partial_run(const void *x, const int32_t *meta_expert, const float *
     uint32_t *pairs = reinterpret_cast<uint32_t *>(ws + L.pairs);
     __half *xg = reinterpret_cast<__half *>(ws + L.xg);
     __half *act = reinterpret_cast<__half *>(ws + L.act);
-    ep_meta_keys_kernel<<<static_cast<unsigned>((n64 + 255) / 256), 256, 0, s>>>(meta_expert, n64, top_k, rows_dev,
-                                                                                 keys);
-    int rc = check_launch("expert keys launch");
-    if (rc) return rc;
-    if ((rc = launch_group_large(keys, n, experts, counts, offsets, pairs, nullptr,
-                                 reinterpret_cast<uint32_t *>(ws + L.gscratch), s)))
-        return rc;
-    if (gate_type == FM_TYPE_Q4_K && down_type == FM_TYPE_Q4_K && partial_uses_tg(rows, top_k, experts, d_model, ffn) &&
-        up_offset % 16 == 0 && down_offset % 16 == 0) {
-        // decode-sized batch: the tcgen05 decode stage reads the received rows in
-        // place and writes the output of grouped pair g to slot pairs[g]
+    auto tg_stage = [&]() {
         const uint32_t pmax = partial_pairs_max(rows, top_k, experts);
-        const TgSections ts = tg_sections(pmax, experts, d_model, ffn);
-        uint8_t *tg = ws + L.tg;
         TgStage t{};
         t.x = x;
         t.x_f16 = true;
@@ -339,6 +339,35 @@ int experts_partial_run(const void *x, const int32_t *meta_expert, const float *
         t.offsets = offsets;
         t.pairs = pairs;
         t.out_rows = pairs;
+        return t;
+    };
+    if (recv) {
+        if (!partial_fused_recv(rows, top_k, experts, d_model, ffn, gate_type, up_type, down_type, up_offset,
+                                down_offset))
+            return set_error(FM_STATUS_INTERNAL_ERROR, "receive wait passed to a batch without the fused front");
+        // wait, grouping and images in one launch, then the decode GEMVs; the
+        // output of grouped pair g goes to slot pairs[g]
+        const TgStage t = tg_stage();
+        const TgSections ts = tg_sections(t.pairs_max, experts, d_model, ffn);
+        uint8_t *tg = ws + L.tg;
+        return tg_recv_stage(t, *recv, tg, tg + ts.img_gu, reinterpret_cast<float *>(tg + ts.img_gu + ts.img_dn),
+                             reinterpret_cast<uint32_t *>(tg + ts.img_gu + ts.img_dn + ts.partial),
+                             tg + ts.img_gu + ts.img_dn + ts.partial + ts.cnt, out_pairs, s);
+    }
+    ep_meta_keys_kernel<<<static_cast<unsigned>((n64 + 255) / 256), 256, 0, s>>>(meta_expert, n64, top_k, rows_dev,
+                                                                                 keys);
+    int rc = check_launch("expert keys launch");
+    if (rc) return rc;
+    if ((rc = launch_group_large(keys, n, experts, counts, offsets, pairs, nullptr,
+                                 reinterpret_cast<uint32_t *>(ws + L.gscratch), s)))
+        return rc;
+    if (gate_type == FM_TYPE_Q4_K && down_type == FM_TYPE_Q4_K && partial_uses_tg(rows, top_k, experts, d_model, ffn) &&
+        up_offset % 16 == 0 && down_offset % 16 == 0) {
+        // decode-sized batch: the tcgen05 decode stage reads the received rows in
+        // place and writes the output of grouped pair g to slot pairs[g]
+        const TgStage t = tg_stage();
+        const TgSections ts = tg_sections(t.pairs_max, experts, d_model, ffn);
+        uint8_t *tg = ws + L.tg;
         return tg_expert_stage(t, tg, tg + ts.img_gu, reinterpret_cast<float *>(tg + ts.img_gu + ts.img_dn),
                                reinterpret_cast<uint32_t *>(tg + ts.img_gu + ts.img_dn + ts.partial),
                                tg + ts.img_gu + ts.img_dn + ts.partial + ts.cnt, out_pairs,
@@ -374,7 +403,7 @@ extern "C" int fmcuda_moe_experts_partial(const void *x, const int32_t *meta_exp
     float *out = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + L.out);
     int rc = experts_partial_run(x, meta_expert, meta_weight, rows, nullptr, top_k, experts, expert_slots, up_offset,
                                  down_offset, gate_type, up_type, down_type, d_model, ffn, out, workspace,
-                                 workspace_bytes, s);
+                                 workspace_bytes, s, nullptr);
     if (rc) return rc;
     const uint64_t m = static_cast<uint64_t>(rows) * d_model;
     ep_partial_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, s>>>(out, meta_expert, meta_weight, rows,

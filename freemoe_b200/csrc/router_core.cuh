@@ -107,7 +107,8 @@ __device__ __forceinline__ void route_token(const float *__restrict__ logits, ui
 }
 
 // Grouping by expert in one CTA: histogram, exclusive scan, then a stable
-// rank of each pair within its expert.  The ranking walks the pairs in flat
+// rank of each pair within its expert.  Key 0xFFFFFFFF is an absent pair (no
+// slot, no error), any other key >= experts raises INVALID_EXPERT_ID.  The ranking walks the pairs in flat
 // order 32 at a time with __match_any_sync, so the result is the ascending
 // token order of the host grouping, independent of scheduling.
 // The whole CTA (1024 threads) groups; s_count / s_off hold `experts` words,
@@ -121,7 +122,7 @@ __device__ __forceinline__ void group_block(const uint32_t *__restrict__ ids, ui
     for (uint32_t i = threadIdx.x; i < n_pairs; i += blockDim.x) {
         const uint32_t e = ids[i];
         if (e < experts) atomicAdd(&s_count[e], 1u);
-        else raise_device_status(status, FM_STATUS_INVALID_EXPERT_ID);
+        else if (e != 0xFFFFFFFFu) raise_device_status(status, FM_STATUS_INVALID_EXPERT_ID);
     }
     __syncthreads();
     // exclusive scan over experts (blockDim.x == 1024 >= experts)

@@ -185,6 +185,28 @@ int tg_expert_stage(const TgStage &t, uint8_t *img_gu, uint8_t *img_dn, float *p
     return tg_gemvs(t, ma, img_gu, img_dn, partial, cnt, part, mark, mark_ctx, s);
 }
 
+bool tg_recv_eligible(uint32_t rows, uint32_t top_k, uint32_t experts) {
+    return experts <= TG_FRONT_MAX_EXPERTS && static_cast<uint64_t>(rows) * top_k <= TG_FRONT_MAX_PAIRS;
+}
+
+// The expert-parallel receive side: wait, grouping and B images in one launch
+// (tg_recv_front_kernel, writing the grouping named in `t`), then the GEMVs.
+int tg_recv_stage(const TgStage &t, const TgRecvWait &r, uint8_t *img_gu, uint8_t *img_dn, float *partial,
+                  uint32_t *cnt, uint8_t *maps_area, float *part, cudaStream_t s) {
+    if (!tg_recv_eligible(r.rows, t.top_k, t.experts) || !t.x_f16)
+        return set_error(FM_STATUS_INTERNAL_ERROR, "tg_recv_stage: batch too large for the fused receive front");
+    TgMapArgs ma;
+    int rc = tg_map_args(t, cnt, maps_area, ma);
+    if (rc) return rc;
+    const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
+    tg_recv_front_kernel<<<tiles * (t.d / 256), 256, 0, s>>>(
+        ma, r.flags, r.world, r.epoch, r.ectr, r.timeout_ns, r.n_rows, r.meta_e, static_cast<const __half *>(t.x),
+        r.rows, t.top_k, t.experts, t.d, tiles, const_cast<uint32_t *>(t.counts), const_cast<uint32_t *>(t.offsets),
+        const_cast<uint32_t *>(t.pairs), img_gu, device_status_word());
+    if ((rc = check_launch("tgemv receive front"))) return rc;
+    return tg_gemvs(t, ma, img_gu, img_dn, partial, cnt, part, [](void *, int) {}, nullptr, s);
+}
+
 bool tg_front_eligible(uint32_t tokens, uint32_t experts, uint32_t top_k) {
     return tokens <= TG_FRONT_MAX_TOKENS && experts <= TG_FRONT_MAX_EXPERTS &&
            static_cast<uint64_t>(tokens) * top_k <= TG_FRONT_MAX_PAIRS;

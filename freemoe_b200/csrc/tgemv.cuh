@@ -76,6 +76,7 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "gemv_kernels.cuh"
+#include "p2p_flags.cuh"
 #include "router_core.cuh"
 #include "tcgen05.cuh"
 
@@ -555,13 +556,19 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             if (!whole) {
                 // the pipelines holding the unit's steps, in order (pipelines with
                 // empty ranges are skipped): pf, then the holder of the next step
-                // after each one's range
+                // after each one's range; with at least one step per pipeline
+                // (dense) simply pf .. the holder of the unit's last step
                 const uint32_t pf = tg_pipe_of(us, W, NP);
+                const bool dense = W >= NP;
                 uint32_t nparts = 1;
-                for (uint32_t q = pf;; ++nparts) {
-                    const uint64_t e = tg_start(q + 1ull, W, NP);
-                    if (e >= us + nb) break;
-                    q = tg_pipe_of(e, W, NP);
+                if (dense) {
+                    nparts = tg_pipe_of(us + nb - 1, W, NP) - pf + 1;
+                } else {
+                    for (uint32_t q = pf;; ++nparts) {
+                        const uint64_t e = tg_start(q + 1ull, W, NP);
+                        if (e >= us + nb) break;
+                        q = tg_pipe_of(e, W, NP);
+                    }
                 }
                 const uint32_t slot = (u == first_u) ? 0u : 1u;
                 float *mine = p.partial + (pipe * 2 + slot) * (NMAT * TG_NT * TG_ROWS);
@@ -586,8 +593,12 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 for (int m = 0; m < NMAT; ++m)
 #pragma unroll
                     for (uint32_t n = 0; n < TG_NT; ++n) val[m][n] = 0.0f;
-                for (uint32_t q = pf, i = 0; i < nparts; ++i, q = tg_pipe_of(tg_start(q + 1ull, W, NP), W, NP)) {
-                    const uint32_t qslot = (u == static_cast<uint32_t>(tg_start(q, W, NP) / nb)) ? 0u : 1u;
+                // slot 0 holds a pipeline's first unit: every holder after pf starts
+                // inside this unit
+                const uint32_t slot_pf = (u == static_cast<uint32_t>(tg_start(pf, W, NP) / nb)) ? 0u : 1u;
+                for (uint32_t q = pf, i = 0; i < nparts;
+                     ++i, q = dense ? q + 1 : tg_pipe_of(tg_start(q + 1ull, W, NP), W, NP)) {
+                    const uint32_t qslot = i == 0 ? slot_pf : 0u;
                     const float *src = p.partial + (static_cast<uint64_t>(q) * 2 + qslot) * (NMAT * TG_NT * TG_ROWS);
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m)
@@ -895,6 +906,64 @@ __global__ void __launch_bounds__(256)
     tg_maps_and_counters(ma, s_cnt, experts);
     if (warp == 0) {
         // exclusive prefix of token tiles over the experts (experts <= 64)
+        uint32_t carry = 0;
+        for (uint32_t base = 0; base < experts; base += 32) {
+            const uint32_t e = base + lane;
+            const uint32_t v = e < experts ? (s_cnt[e] + TG_NT - 1) / TG_NT : 0u;
+            uint32_t incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += t;
+            }
+            if (e < experts) s_tile[e] = carry + incl - v;
+            carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+        }
+        if (lane == 0) s_tile[experts] = carry;
+    }
+    __syncthreads();
+    tg_image_block(x, d, s_cnt, s_offs, s_pairs, top_k, experts, max_tiles, s_tile, img, sm);
+}
+
+// The expert-parallel receive side in one launch: every CTA waits for every
+// source's rows (epoch flags of the peer exchange), groups the received
+// (row, slot) pairs by local expert in shared memory (keys: the local expert
+// id of each slot, absent for other ranks' slots and rows past the received
+// count), CTA 0 publishes the grouping, and CTA (tile, block) writes its gate/up
+// B image from the fp16 receive rows.  Replaces the wait, key, grouping and
+// image kernels of the receive side.
+__global__ void __launch_bounds__(256)
+    tg_recv_front_kernel(const __grid_constant__ TgMapArgs ma, const uint32_t *flags, uint32_t world, uint32_t epoch,
+                         const uint32_t *ectr, uint64_t timeout_ns, const uint32_t *n_rows,
+                         const int32_t *__restrict__ meta_e, const __half *__restrict__ x, uint32_t rows,
+                         uint32_t top_k, uint32_t experts, uint32_t d, uint32_t max_tiles, uint32_t *counts,
+                         uint32_t *offsets, uint32_t *pairs, uint8_t *__restrict__ img, int *status) {
+    __shared__ uint32_t s_keys[TG_FRONT_MAX_PAIRS], s_pairs[TG_FRONT_MAX_PAIRS];
+    __shared__ uint32_t s_cnt[TG_FRONT_MAX_EXPERTS], s_offs[TG_FRONT_MAX_EXPERTS + 1];
+    __shared__ uint32_t s_count[TG_FRONT_MAX_EXPERTS], s_off[TG_FRONT_MAX_EXPERTS], s_warp_tot[32];
+    __shared__ uint32_t s_tile[TG_FRONT_MAX_EXPERTS + 1];
+    __shared__ TgImageSmem sm;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    wait_flags_cta(flags, world, call_epoch(epoch, ectr), timeout_ns, status);
+    const uint32_t live = *reinterpret_cast<const volatile uint32_t *>(n_rows);
+    const uint32_t P = rows * top_k;
+    for (uint32_t i = threadIdx.x; i < P; i += blockDim.x) {
+        const int32_t e = i / top_k < live ? meta_e[i] : -1;
+        s_keys[i] = e >= 0 ? static_cast<uint32_t>(e) : 0xFFFFFFFFu;
+    }
+    if (threadIdx.x < 32) s_warp_tot[threadIdx.x] = 0;
+    __syncthreads();
+    group_block(s_keys, P, experts, s_cnt, s_offs, s_pairs, nullptr, status, s_count, s_off, s_warp_tot);
+    __syncthreads();
+    if (blockIdx.x == 0) {
+        for (uint32_t i = threadIdx.x; i < P; i += blockDim.x) pairs[i] = s_pairs[i];
+        for (uint32_t e = threadIdx.x; e <= experts; e += blockDim.x) {
+            if (e < experts) counts[e] = s_cnt[e];
+            offsets[e] = s_offs[e];
+        }
+    }
+    tg_maps_and_counters(ma, s_cnt, experts);
+    if (warp == 0) {
         uint32_t carry = 0;
         for (uint32_t base = 0; base < experts; base += 32) {
             const uint32_t e = base + lane;

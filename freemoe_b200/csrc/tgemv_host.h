@@ -57,4 +57,24 @@ int tg_block_stage(const TgStage &t, const TgFront &f, uint8_t *img_gu, uint8_t 
                    uint32_t *cnt, uint8_t *maps_area, float *part, void (*mark)(void *, int), void *mark_ctx,
                    cudaStream_t s);
 
+// The peer exchange's receive side for tg_recv_stage: wait until flags[0 ..
+// world) reach the call's epoch (explicit, else one past *ectr), then take the
+// first *n_rows of `rows` receive rows, meta_e the local expert of each
+// (row, top-k slot) or -1.
+struct TgRecvWait {
+    const uint32_t *flags;
+    uint32_t world, epoch;
+    const uint32_t *ectr;
+    uint64_t timeout_ns;
+    const uint32_t *n_rows;
+    const int32_t *meta_e;
+    uint32_t rows;
+};
+// A receive batch the fused receive front takes: <= 64 local experts, <= 1024 (row, slot) pairs.
+bool tg_recv_eligible(uint32_t rows, uint32_t top_k, uint32_t experts);
+// Wait, grouping (into t.counts / t.offsets / t.pairs) and B images in one launch,
+// then gate/up + SwiGLU and down; t.x are the fp16 receive rows.
+int tg_recv_stage(const TgStage &t, const TgRecvWait &r, uint8_t *img_gu, uint8_t *img_dn, float *partial,
+                  uint32_t *cnt, uint8_t *maps_area, float *part, cudaStream_t s);
+
 } // namespace fmb

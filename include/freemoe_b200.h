@@ -435,10 +435,11 @@ int fmcuda_ep_layer(void *comm, const fmcuda_ep_layer_args *args, uint32_t token
  *   fmcuda_ep_p2p_combine    wait for the partial sums, y[t] = their sum over
  *                            ranks (ascending): the result of mode "rows"
  * `epoch` numbers the calls 1, 2, ... (the same on every rank), or is 0 in
- * all three calls: then fmcuda_ep_p2p_dispatch advances a counter in this
- * rank's own mailbox and the kernels of the call read their epoch there, so
- * the calls can be captured in a CUDA graph once and replayed (one layer uses
- * one of the two forms).  `capacity`
+ * all three calls: then the kernels of the call take one past a counter in
+ * this rank's own mailbox as their epoch and fmcuda_ep_p2p_combine advances
+ * the counter when it has finished (every device-epoch call runs all three),
+ * so the calls can be captured in a CUDA graph once and replayed (one layer
+ * uses one of the two forms).  `capacity`
  * (the same on every rank) bounds the rows a mailbox receives: at least the
  * largest tokens-per-rank times world.  `peers` is a device array of the
  * world mailbox addresses as this process sees them (its own included);

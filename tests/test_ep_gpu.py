@@ -16,6 +16,11 @@ from conftest import ROOT
 pytestmark = pytest.mark.gpu
 
 
+def _file_store(tmp_path) -> str:
+    """Rendezvous of a one-rank process group through a file (no port to race for)."""
+    return f"file://{tmp_path / 'pg_store'}"
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("shape", [(16, 4, 256, 256, 512, 12), (128, 8, 4096, 1536, 1024, 12), (64, 6, 2048, 1408, 512, 8)])
 @pytest.mark.parametrize("mode", ["pairs", "rows", "p2p", "nccl_c"])
@@ -49,12 +54,11 @@ def test_ep_decode_matches_moe_block(shape, mode):
     assert "ref=block" in p.stdout and "max_rel=" in p.stdout
 
 
-def test_p2p_decode_single_rank(cuda, oracle):
+def test_p2p_decode_single_rank(cuda, oracle, tmp_path):
     """One rank through the peer-memory exchange with a decode-sized batch (the
     tcgen05 decode stage computes the experts from the fp16 mailbox rows): three
     calls in a row, each within 1e-5 of max |y| of fmcuda_moe_block and within
     1e-3 of the oracle's per-token expert loop."""
-    import socket
 
     import numpy as np
     import torch.distributed as dist
@@ -62,10 +66,7 @@ def test_p2p_decode_single_rank(cuda, oracle):
     from freemoe_b200 import hotpath
     from freemoe_b200.ep import DeviceOps, EPLayer
 
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    dist.init_process_group("gloo", init_method=_file_store(tmp_path), rank=0, world_size=1)
     try:
         E, k, d, ffn, T, t = 8, 2, 512, 768, 6, 12
         rb = hotpath.row_bytes
@@ -140,13 +141,12 @@ def nccl_c_layer(lib, comm, x, logits, slots_table, *, world, n_local, E, k, d, 
 
 
 @pytest.mark.parametrize("shape", [(16, 4, 256, 256, 64, 12), (8, 2, 512, 768, 6, 12)])
-def test_nccl_c_layer_single_rank(cuda, shape):
+def test_nccl_c_layer_single_rank(cuda, shape, tmp_path):
     """fmcuda_ep_init / fmcuda_ep_layer with one rank (NCCL sends to itself): the
     layer driven from the C ABI equals the Python layer's "rows" exchange bit for
     bit, twice in a row, for a prefill-sized batch (grouped GEMM) and a
     decode-sized one (tcgen05 decode stage)."""
     import ctypes as C
-    import socket
 
     import numpy as np
     import torch.distributed as dist
@@ -157,10 +157,7 @@ def test_nccl_c_layer_single_rank(cuda, shape):
 
     E, k, d, ffn, T, t = shape
     lib = load()
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    dist.init_process_group("gloo", init_method=_file_store(tmp_path), rank=0, world_size=1)
     comm = C.c_void_p()
     try:
         rb = hotpath.row_bytes
@@ -202,14 +199,13 @@ def test_nccl_c_layer_rejects_bad_arguments(cuda):
     assert lib.fmcuda_ep_layer(None, C.byref(EpLayerArgs()), 1, None, 0, None) == 26
 
 
-def test_p2p_exchange_single_rank_and_timeout(cuda):
+def test_p2p_exchange_single_rank_and_timeout(cuda, tmp_path):
     """One rank (world 1) through the peer-memory exchange: mailbox, IPC handle,
     the count/plan/send/return/combine kernels writing to its own mailbox,
     three calls in a row, each equal bit for bit to fmcuda_moe_prefill.  Then a
     wait whose flag nothing raises gives up after its limit with FENCE_TIMEOUT
     in the device status word (the wait is bounded, the context stays usable)."""
     import ctypes as C
-    import socket
 
     import numpy as np
     import torch.distributed as dist
@@ -218,10 +214,7 @@ def test_p2p_exchange_single_rank_and_timeout(cuda):
     from freemoe_b200._lib import load
     from freemoe_b200.ep import DeviceOps, EPLayer
 
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    dist.init_process_group("gloo", init_method=_file_store(tmp_path), rank=0, world_size=1)
     try:
         E, k, d, ffn, T, t = 16, 4, 256, 256, 64, 12
         rb = hotpath.row_bytes
