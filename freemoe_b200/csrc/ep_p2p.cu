@@ -112,8 +112,8 @@ __global__ void p2p_counts_kernel(uint8_t *const *peers, uint32_t world, uint32_
 }
 
 // One warp: wait for every source's matrix row, then derive this rank's plan.
-__global__ void p2p_plan_kernel(uint8_t *mine, Mailbox L, uint32_t world, uint32_t rank, uint32_t epoch,
-                                uint64_t timeout_ns, int *status) {
+__global__ void p2p_plan_kernel(uint8_t *mine, Mailbox L, uint32_t world, uint32_t rank, uint32_t cap,
+                                uint32_t epoch, uint64_t timeout_ns, int *status) {
     const uint32_t lane = threadIdx.x;
     epoch = call_epoch(epoch, at<uint32_t>(mine, L.ctr) + 2);
     for (uint32_t s = lane; s < world; s += 32) wait_flag(at<uint32_t>(mine, L.mflag) + s, epoch, timeout_ns, status);
@@ -131,7 +131,9 @@ __global__ void p2p_plan_kernel(uint8_t *mine, Mailbox L, uint32_t world, uint32
         src_pos[s] = before;
     }
     recv_off[world] = acc;
-    *at<uint32_t>(mine, L.n_recv) = acc;
+    // rows past the capacity were dropped by their senders: count only the kept ones
+    if (acc > cap) raise_device_status(status, FM_STATUS_INVALID_ARGUMENT);
+    *at<uint32_t>(mine, L.n_recv) = acc < cap ? acc : cap;
     for (uint32_t r = 0; r < world; ++r) {
         uint32_t before = 0; // rows of lower sources at destination r
         for (uint32_t s = 0; s < rank; ++s) before += m[static_cast<uint64_t>(s) * world + r];
@@ -268,7 +270,9 @@ __global__ void __launch_bounds__(128)
             src_pos[q] = before;
         }
         recv_off[world] = acc;
-        *at<uint32_t>(mine, L.n_recv) = acc;
+        // rows past the capacity were dropped by their senders: count only the kept ones
+        if (acc > cap) raise_device_status(status, FM_STATUS_INVALID_ARGUMENT);
+        *at<uint32_t>(mine, L.n_recv) = acc < cap ? acc : cap;
     }
     if (first)
         for (uint32_t r = tid; r < world; r += blockDim.x) at<uint32_t>(mine, L.my_pos)[r] = s_mypos[r];
@@ -531,7 +535,8 @@ extern "C" int fmcuda_ep_p2p_dispatch(const uint32_t *ids, const float *weights,
     p2p_counts_kernel<<<1, 64, 0, s>>>(pp, world, rank, counts, L.matrix, L.mflag, epoch,
                                        reinterpret_cast<const uint32_t *>(mine + L.ctr) + 2);
     if ((rc = check_launch("peer counts launch"))) return rc;
-    p2p_plan_kernel<<<1, 32, 0, s>>>(mine, L, world, rank, epoch, timeout_ns_of(timeout_ms), device_status_word());
+    p2p_plan_kernel<<<1, 32, 0, s>>>(mine, L, world, rank, capacity, epoch, timeout_ns_of(timeout_ms),
+                                     device_status_word());
     if ((rc = check_launch("peer plan launch"))) return rc;
     if (x_dtype == FM_X_F32)
         p2p_pack_send_kernel<float><<<grid, 128, 0, s>>>(static_cast<const float *>(x), ids, weights, items, offsets,
