@@ -26,10 +26,11 @@ int tg_sm_count() {
     return n;
 }
 
-template <int MODE> int tg_configure() {
+template <int MODE, bool WIDE> int tg_configure() {
     static int done = 0;
     if (!done) {
-        const cudaError_t err = cudaFuncSetAttribute(tgemv_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const cudaError_t err = cudaFuncSetAttribute(tgemv_kernel<MODE, WIDE>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      TgLayout<MODE>::smem_bytes(TG_MAX_EXPERTS));
         if (err != cudaSuccess) return cuda_status(err, "tgemv shared-memory attribute");
         done = 1;
@@ -76,6 +77,10 @@ uint32_t tg_max_tiles(uint32_t pairs_max, uint32_t experts) {
     return pairs_max / TG_NT + (pairs_max < experts ? pairs_max : experts);
 }
 
+// Wide mode (one weight conversion for two token tiles) pays when the experts
+// hold two or more tiles on average: at least 16 routed pairs per expert.
+bool tg_wide(uint32_t pairs_max, uint32_t experts) { return pairs_max >= 16ull * experts; }
+
 bool tg_shape(uint32_t d, uint32_t ffn) { return d % 256 == 0 && ffn % 256 == 0 && d > 0 && ffn > 0; }
 
 TgSections tg_sections(uint32_t pairs_max, uint32_t experts, uint32_t d, uint32_t ffn) {
@@ -85,7 +90,8 @@ TgSections tg_sections(uint32_t pairs_max, uint32_t experts, uint32_t d, uint32_
     t.img_gu = a256(tiles * (d / 256) * TG_IMG);
     t.img_dn = a256(tiles * (ffn / 256) * TG_IMG);
     t.partial = a256(2ull * TG_MAX_CTAS * 2 * 2 * TG_NT * TG_ROWS * 4);
-    t.cnt = a256(tiles * (ffn / TG_ROWS + d / TG_ROWS) * 4);
+    // stream-K arrivals per unit (wide mode: per unit and half, 2 x pairs <= tiles + experts)
+    t.cnt = a256((tiles + experts) * (ffn / TG_ROWS + d / TG_ROWS) * 4);
     t.maps = a256(static_cast<uint64_t>(experts) * 3 * sizeof(CUtensorMap) + 256);
     return t;
 }
@@ -101,8 +107,10 @@ namespace {
 // Stream-K counters and the raw-weight map templates of one expert stage.
 int tg_map_args(const TgStage &t, uint32_t *cnt, uint8_t *maps_area, TgMapArgs &ma) {
     int rc;
-    if ((rc = tg_configure<TG_GATE_UP>())) return rc;
-    if ((rc = tg_configure<TG_DOWN>())) return rc;
+    if ((rc = tg_configure<TG_GATE_UP, false>())) return rc;
+    if ((rc = tg_configure<TG_DOWN, false>())) return rc;
+    if ((rc = tg_configure<TG_GATE_UP, true>())) return rc;
+    if ((rc = tg_configure<TG_DOWN, true>())) return rc;
     const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
     ma = TgMapArgs{};
     ma.maps = reinterpret_cast<CUtensorMap *>(maps_area + 256);
@@ -110,7 +118,7 @@ int tg_map_args(const TgStage &t, uint32_t *cnt, uint8_t *maps_area, TgMapArgs &
     ma.up_off = t.up_offset;
     ma.down_off = t.down_offset;
     ma.cnt = cnt;
-    ma.n_cnt = tiles * (t.ffn / TG_ROWS + t.d / TG_ROWS);
+    ma.n_cnt = (tiles + t.experts) * (t.ffn / TG_ROWS + t.d / TG_ROWS);
     const uint32_t rb_gu = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, t.d));
     const uint32_t rb_dn = static_cast<uint32_t>(row_bytes(FM_TYPE_Q4_K, t.ffn));
     if ((rc = tg_template(&ma.tmpl_gu, ma.maps, rb_gu, t.ffn))) return rc;
@@ -123,6 +131,7 @@ int tg_gemvs(const TgStage &t, const TgMapArgs &ma, uint8_t *img_gu, uint8_t *im
     const uint32_t tiles = tg_max_tiles(t.pairs_max, t.experts);
     const uint32_t grid = static_cast<uint32_t>(tg_sm_count() < static_cast<int>(TG_MAX_CTAS) ? tg_sm_count()
                                                                                               : TG_MAX_CTAS);
+    const bool wide = tg_wide(t.pairs_max, t.experts);
     TgParams gu{};
     gu.slots = ma.slots;
     gu.w_off0 = 0;
@@ -140,7 +149,10 @@ int tg_gemvs(const TgStage &t, const TgMapArgs &ma, uint8_t *img_gu, uint8_t *im
     gu.unit_cnt = cnt;
     gu.status = device_status_word();
     int rc;
-    tgemv_kernel<TG_GATE_UP><<<grid, TG_THREADS, TgLayout<TG_GATE_UP>::smem_bytes(t.experts), s>>>(gu);
+    if (wide)
+        tgemv_kernel<TG_GATE_UP, true><<<grid, TG_THREADS, TgLayout<TG_GATE_UP>::smem_bytes(t.experts), s>>>(gu);
+    else
+        tgemv_kernel<TG_GATE_UP, false><<<grid, TG_THREADS, TgLayout<TG_GATE_UP>::smem_bytes(t.experts), s>>>(gu);
     if ((rc = check_launch("tgemv gate/up"))) return rc;
     mark(mark_ctx, 4);
     mark(mark_ctx, 5);
@@ -155,8 +167,11 @@ int tg_gemvs(const TgStage &t, const TgMapArgs &ma, uint8_t *img_gu, uint8_t *im
     dn.out_img = nullptr;
     dn.part = part;
     dn.out_rows = t.out_rows;
-    dn.unit_cnt = cnt + tiles * (t.ffn / TG_ROWS);
-    tgemv_kernel<TG_DOWN><<<grid, TG_THREADS, TgLayout<TG_DOWN>::smem_bytes(t.experts), s>>>(dn);
+    dn.unit_cnt = cnt + (tiles + t.experts) * (t.ffn / TG_ROWS);
+    if (wide)
+        tgemv_kernel<TG_DOWN, true><<<grid, TG_THREADS, TgLayout<TG_DOWN>::smem_bytes(t.experts), s>>>(dn);
+    else
+        tgemv_kernel<TG_DOWN, false><<<grid, TG_THREADS, TgLayout<TG_DOWN>::smem_bytes(t.experts), s>>>(dn);
     if ((rc = check_launch("tgemv down"))) return rc;
     mark(mark_ctx, 6);
     return FM_STATUS_OK;

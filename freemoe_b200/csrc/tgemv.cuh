@@ -125,15 +125,25 @@ template <int MODE> struct TgLayout {
     static constexpr uint32_t BARS_WG = 24;
     static constexpr uint32_t OFF_MISC = OFF_BAR + 2 * BARS_WG * 8;
     static constexpr uint32_t OFF_TILES = OFF_MISC + 64;
-    static constexpr uint32_t smem_bytes(uint32_t experts) { return 1024 + OFF_TILES + 4 * (experts + 1); }
+    // token-tile prefix, then (wide mode) tile-pair prefix, experts + 1 words each
+    static constexpr uint32_t smem_bytes(uint32_t experts) { return 1024 + OFF_TILES + 8 * (experts + 1); }
     // TMEM columns inside a pipeline's 256
     static constexpr uint32_t ACC_COLS = MODE == TG_GATE_UP ? 32 : 48;  // one buffer's accumulators
     static constexpr uint32_t ACC = 0;                         // [2 buffers][ACC_COLS]
     static constexpr uint32_t ASTG = 2 * ACC_COLS;             // [2 stages][NMAT * 32]
     static constexpr uint32_t MINS = ASTG + 2 * NMAT * 32;     // [2 buffers][NMAT * 8]
     static_assert(MINS + 2 * NMAT * 8 <= 256, "TMEM columns of one pipeline");
+    // wide mode (one step stream per CTA, two token tiles per step): half h
+    // converts chunks 2h, 2h + 1 into its own two A stages (each stage then takes
+    // one chunk per step, so every wait sees every phase); mins shared, one
+    // accumulator pair per half; raw ring of both pipelines' space
+    static constexpr uint32_t W_ASTG = 0;                  // [half][2 stages][NMAT * 32]
+    static constexpr uint32_t W_MINS = 4 * NMAT * 32;
+    static constexpr uint32_t W_ACC = W_MINS + 2 * NMAT * 8;
+    static_assert(W_ACC + 2 * 2 * ACC_COLS <= 512, "TMEM columns of a wide CTA");
+    static constexpr uint32_t PW = 2 * TG_RAW / STAGE;
     static_assert(P == 2 && P * STAGE == TG_RAW, "raw ring");
-    static_assert(1024 + OFF_TILES + 4 * (TG_MAX_EXPERTS + 1) <= 227u * 1024u, "shared memory per CTA");
+    static_assert(1024 + OFF_TILES + 8 * (TG_MAX_EXPERTS + 1) <= 227u * 1024u, "shared memory per CTA");
 };
 
 // Barriers of one pipeline, in its 24-slot block.
@@ -199,6 +209,53 @@ __device__ __forceinline__ void tg_tile_prefix(uint32_t *s_tile, const uint32_t 
         carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
     }
     if (lane == 0) s_tile[experts] = carry;
+}
+
+// Wide mode: units are (expert, row tile, pair of token tiles), the pairs of
+// expert e numbered from s_pair[e] (exclusive prefix of ceil(tiles / 2)); half
+// h of the CTA takes tile 2 tp + h of the pair.  A pair's missing second tile
+// reads the first one's image and has no tokens (ntok 0).
+__device__ __forceinline__ TgUnit tg_unit_wide(const uint32_t *s_tile, const uint32_t *s_pair, uint32_t experts,
+                                               uint32_t row_tiles, uint32_t u, uint32_t half,
+                                               const uint32_t *counts, const uint32_t *offsets) {
+    uint32_t lo = 0, hi = experts;
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (s_pair[mid] * row_tiles <= u) lo = mid;
+        else hi = mid;
+    }
+    TgUnit g;
+    g.e = lo;
+    const uint32_t npairs = s_pair[lo + 1] - s_pair[lo];
+    const uint32_t local = u - s_pair[lo] * row_tiles;
+    g.rho = local / npairs;
+    const uint32_t tp = local - g.rho * npairs;
+    const uint32_t tau = 2 * tp + half, ntiles = s_tile[lo + 1] - s_tile[lo];
+    const bool exists = tau < ntiles;
+    g.tile = s_tile[lo] + (exists ? tau : 2 * tp);
+    g.pair0 = __ldg(offsets + lo) + TG_NT * tau;
+    g.ntok = exists ? min(TG_NT, __ldg(counts + lo) - TG_NT * tau) : 0u;
+    return g;
+}
+
+// Exclusive prefix of ceil(tiles / 2) over the experts (one warp, after
+// tg_tile_prefix); s_pair[E] = total.
+__device__ __forceinline__ void tg_pair_prefix(uint32_t *s_pair, const uint32_t *s_tile, uint32_t experts,
+                                               uint32_t lane) {
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < experts; base += 32) {
+        const uint32_t e = base + lane;
+        const uint32_t v = e < experts ? (s_tile[e + 1] - s_tile[e] + 1) / 2 : 0u;
+        uint32_t incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= static_cast<uint32_t>(o)) incl += t;
+        }
+        if (e < experts) s_pair[e] = carry + incl - v;
+        carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    if (lane == 0) s_pair[experts] = carry;
 }
 
 // Pipeline p's steps are [tg_start(p), tg_start(p + 1)); the pipeline holding step s.
@@ -285,7 +342,7 @@ __host__ __device__ __forceinline__ uint32_t tg_sw_off(uint32_t n, uint32_t k) {
 }
 
 
-template <int MODE>
+template <int MODE, bool WIDE>
 __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) {
     using L = TgLayout<MODE>;
     constexpr int NMAT = 2;
@@ -295,6 +352,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
     uint32_t *misc = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC); // [0] TMEM base [1] abort [2] bad slot [3,4] last
     uint32_t *s_tile = reinterpret_cast<uint32_t *>(smem + L::OFF_TILES);
+    uint32_t *s_pair = s_tile + p.experts + 1;
     volatile uint32_t *abort_flag = misc + 1;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t E = p.experts;
@@ -306,6 +364,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
     __syncthreads();
     if (warp == 1) {
         tg_tile_prefix(s_tile, p.counts, E, lane);
+        if (WIDE) {
+            __syncwarp();
+            tg_pair_prefix(s_pair, s_tile, E, lane);
+        }
     } else if (warp == 3) {
         // every expert with tokens needs a resident slot with 16-byte aligned matrices
         for (uint32_t e = lane; e < E; e += 32) {
@@ -322,13 +384,15 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 mbar_init(&b.x_full[q], 1);
                 mbar_init(&b.x_free[q], 2); // both issuers
             }
-            for (uint32_t q = 0; q < L::P; ++q) {
+            // wide: the raw ring and the A stages of block 0 serve both halves
+            for (uint32_t q = 0; q < 4; ++q) {
                 mbar_init(&b.raw_full[q], 1);
-                mbar_init(&b.raw_free[q], 4); // the pipeline's converter warps
+                mbar_init(&b.raw_free[q], WIDE ? 8 : 4); // the converter warps reading the stage
             }
             for (uint32_t q = 0; q < 2; ++q) {
-                mbar_init(&b.a_full[q], 4);
-                mbar_init(&b.a_free[q], 2); // both issuers read every chunk
+                mbar_init(&b.a_full[q], 4);                // the warps converting the chunk
+                mbar_init(&b.a_free[q], WIDE ? 4 : 2);     // every issuer reads every chunk
+                // (wide: block h's two A stages are half h's)
                 mbar_init(&b.acc_full[q], 2);
                 mbar_init(&b.acc_free[q], 4);
                 mbar_init(&b.drain[q], 1);
@@ -342,7 +406,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         return;
     }
     const uint32_t row_tiles = p.out_dim / (DN ? 2 * TG_ROWS : TG_ROWS), nb = p.in_dim / 256;
-    const uint64_t W = static_cast<uint64_t>(s_tile[E]) * row_tiles * nb;
+    const uint64_t W = static_cast<uint64_t>(WIDE ? s_pair[E] : s_tile[E]) * row_tiles * nb;
     if (W == 0) return;
 
     if (warp == 0) {
@@ -353,9 +417,66 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = misc[0];
-    const uint64_t NP = 2ull * gridDim.x;
+    const uint64_t NP = WIDE ? gridDim.x : 2ull * gridDim.x;
 
-    if (warp == 0) {
+    if (WIDE && warp == 0) {
+        // ---- wide producer: one step stream, both halves' images, one raw box set
+        if (lane == 0) {
+            const uint64_t s0 = tg_start(blockIdx.x, W, NP), s1 = tg_start(blockIdx.x + 1ull, W, NP);
+            const TgBars b0 = tg_bars(bars), b1 = tg_bars(bars + L::BARS_WG);
+            uint32_t j = 0, cur_u = 0xFFFFFFFFu;
+            TgUnit g0{}, g1{};
+            long long last_progress = clock64();
+            while (s0 + j < s1 && !*abort_flag) {
+                const uint32_t xs = j % TG_XS, rs = j % L::PW;
+                if (!mbar_test_wait(&b0.x_free[xs], ((j / TG_XS) & 1u) ^ 1u) ||
+                    !mbar_test_wait(&b1.x_free[xs], ((j / TG_XS) & 1u) ^ 1u) ||
+                    !mbar_test_wait(&b0.raw_free[rs], ((j / L::PW) & 1u) ^ 1u)) {
+                    __nanosleep(64);
+                    if (clock64() - last_progress > (1ll << 31)) {
+                        *abort_flag = 1;
+                        raise_device_status(p.status, FM_STATUS_INTERNAL_ERROR);
+                    }
+                    continue;
+                }
+                const uint64_t s = s0 + j;
+                const uint32_t u = static_cast<uint32_t>(s / nb), b = static_cast<uint32_t>(s - static_cast<uint64_t>(u) * nb);
+                if (u != cur_u) {
+                    const uint32_t old_e = cur_u == 0xFFFFFFFFu ? 0xFFFFFFFFu : g0.e;
+                    g0 = tg_unit_wide(s_tile, s_pair, E, row_tiles, u, 0, p.counts, p.offsets);
+                    g1 = tg_unit_wide(s_tile, s_pair, E, row_tiles, u, 1, p.counts, p.offsets);
+                    if (g0.e != old_e)
+#pragma unroll
+                        for (int m = 0; m < (DN ? 1 : NMAT); ++m) tma_fence_acquire(p.maps + 3 * g0.e + p.map0 + m);
+                    cur_u = u;
+                }
+#pragma unroll
+                for (uint32_t w = 0; w < 2; ++w) {
+                    const TgBars &bw = w ? b1 : b0;
+                    const uint32_t tile = w ? g1.tile : g0.tile;
+                    mbar_expect_tx(&bw.x_full[xs], TG_IMG);
+                    bulk_g2s(smem + (w * TG_XS + xs) * TG_IMG, p.img + (static_cast<uint64_t>(tile) * nb + b) * TG_IMG,
+                             TG_IMG, &bw.x_full[xs]);
+                }
+                uint8_t *rdst = smem + L::OFF_RAW + rs * L::STAGE;
+                mbar_expect_tx(&b0.raw_full[rs], L::STAGE);
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+                    tma_load_2d(rdst + m * TG_BOX, p.maps + 3 * g0.e + p.map0 + (DN ? 0 : m),
+                                static_cast<int32_t>(b * TG_RB),
+                                static_cast<int32_t>((DN ? 2 * g0.rho + m : g0.rho) * TG_ROWS), &b0.raw_full[rs]);
+                ++j;
+                last_progress = clock64();
+            }
+            // copies still in flight must land before the CTA's shared memory goes away
+            for (uint32_t q = j > TG_XS ? j - TG_XS : 0; q < j; ++q) {
+                (void)mbar_wait(&b0.x_full[q % TG_XS], (q / TG_XS) & 1u);
+                (void)mbar_wait(&b1.x_full[q % TG_XS], (q / TG_XS) & 1u);
+            }
+            for (uint32_t q = j > L::PW ? j - L::PW : 0; q < j; ++q)
+                (void)mbar_wait(&b0.raw_full[q % L::PW], (q / L::PW) & 1u);
+        }
+    } else if (warp == 0) {
         // ---- producer of both pipelines ----------------------------------------
         if (lane == 0) {
             uint64_t s0[2], s1[2];
@@ -423,13 +544,17 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         }
     } else if (warp < TG_CONV0) {
         // ---- MMA issuers: warp 1 + 2w + i = issuer i of pipeline w --------------
+        // (wide: warp 1 + 2w + i = issuer i of half w, both halves on the shared A)
         const uint32_t wg = (warp - 1) >> 1, iss = (warp - 1) & 1u;
         if (lane == 0) {
-            const uint64_t pipe = 2ull * blockIdx.x + wg;
+            const uint64_t pipe = WIDE ? blockIdx.x : 2ull * blockIdx.x + wg;
             const uint64_t s0 = tg_start(pipe, W, NP), s1 = tg_start(pipe + 1, W, NP);
-            const TgBars bw = tg_bars(bars + wg * L::BARS_WG);
+            const TgBars bw = tg_bars(bars + wg * L::BARS_WG);       // x images, accumulators
+            const TgBars ba = WIDE ? tg_bars(bars) : bw;              // A stages
             const uint32_t idesc = idesc_f16_m128(16);
-            const uint32_t tw = tmem + wg * 256u;
+            const uint32_t t_acc = WIDE ? tmem + L::W_ACC + wg * (2 * L::ACC_COLS) : tmem + wg * 256u + L::ACC;
+            const uint32_t t_a = WIDE ? tmem + L::W_ASTG : tmem + wg * 256u + L::ASTG;
+            const uint32_t t_m = WIDE ? tmem + L::W_MINS : tmem + wg * 256u + L::MINS;
             uint32_t j = 0;
             bool issued = false;
             for (uint64_t s = s0; s < s1; ++s, ++j) {
@@ -438,37 +563,41 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 if (!tg_wait(&bw.acc_free[ab], ((j >> 1) & 1u) ^ 1u, abort_flag, p.status)) break;
                 tc_fence_after();
                 const uint64_t bd0 = smem_desc_sw128(smem_u32(smem + (wg * TG_XS + st) * TG_IMG));
-                const uint32_t acc = tw + L::ACC + ab * L::ACC_COLS + iss * 16u; // matrix / row tile iss
+                const uint32_t acc = t_acc + ab * L::ACC_COLS + iss * 16u; // matrix / row tile iss
                 bool ok = true;
 #pragma unroll
                 for (uint32_t c = 0; c < 4; ++c) {
-                    const uint32_t cc = 4 * j + c, as = cc & 1u;
-                    if (!tg_wait(&bw.a_full[as], (cc >> 1) & 1u, abort_flag, p.status)) {
+                    // the chunk's A stage: narrow, stage cc % 2 of the pipeline's ring;
+                    // wide, stage c % 2 of the converting half c / 2 (one use per step)
+                    const uint32_t cc = 4 * j + c, as = WIDE ? (c & 1u) : (cc & 1u);
+                    const uint32_t aph = WIDE ? (j & 1u) : ((cc >> 1) & 1u);
+                    const TgBars bh = WIDE ? tg_bars(bars + (c >> 1) * L::BARS_WG) : ba;
+                    if (!tg_wait(&bh.a_full[as], aph, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t astg = tw + L::ASTG + as * (NMAT * 32u) + iss * 32u;
+                    const uint32_t astg = t_a + (WIDE ? 2 * (c >> 1) + as : as) * (NMAT * 32u) + iss * 32u;
 #pragma unroll
                     for (uint32_t kk = 0; kk < 4; ++kk)
                         mma_f16_ts(acc, astg + kk * 8u, bd0 + ((c * 2048u + kk * 32u) >> 4), idesc, (c | kk) != 0u);
                     if (c == 0) {
                         // the block's mins (their A was stored before chunk 0's arrival)
                         const uint64_t bm = bd0 + (TG_MINS_OFF >> 4);
-                        const uint32_t ma = tw + L::MINS + ab * (NMAT * 8u);
+                        const uint32_t ma = t_m + ab * (NMAT * 8u);
                         if (!DN) {
                             mma_f16_ts(acc, ma + iss * 8u, bm, idesc, 1u);
                         } else if (iss == 0) {
                             // both row tiles into one accumulator, in order: tile 0 from
                             // K 0-15 of the sums image (columns 0-7), tile 1 from K 16-31
                             // (columns 8-15)
-                            const uint32_t am = tw + L::ACC + ab * L::ACC_COLS + 32u;
+                            const uint32_t am = t_acc + ab * L::ACC_COLS + 32u;
                             mma_f16_ts(am, ma, bm, idesc, 0u);
                             mma_f16_ts(am, ma + 8u, bm + (32u >> 4), idesc, 1u);
                         }
                     }
                     issued = true;
-                    tc_commit(&bw.a_free[as]);
+                    tc_commit(&bh.a_free[as]);
                 }
                 if (!ok) break;
                 tc_commit(&bw.acc_full[ab]);
@@ -482,14 +611,23 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         }
     } else {
         // ---- converters, read-back and epilogue ---------------------------------
+        // (wide: warps of half w convert chunks 2w, 2w + 1 of the shared step and
+        // read back half w's accumulators)
         const uint32_t wg = (warp - TG_CONV0) >> 2, wq = warp & 3u;
         const uint32_t r = wq * 32u + lane; // weight row inside the unit = TMEM lane
-        const uint64_t pipe = 2ull * blockIdx.x + wg;
+        const uint64_t pipe = WIDE ? blockIdx.x : 2ull * blockIdx.x + wg; // stream-K range
         const uint64_t s0 = tg_start(pipe, W, NP), s1 = tg_start(pipe + 1, W, NP);
         const uint32_t my = static_cast<uint32_t>(s1 - s0);
-        const TgBars bw = tg_bars(bars + wg * L::BARS_WG);
-        const uint32_t tw = tmem + wg * 256u + ((wq * 32u) << 16);
-        const uint8_t *raw = smem + L::OFF_RAW + wg * TG_RAW + r * TG_RB;
+        const TgBars bw = tg_bars(bars + wg * L::BARS_WG);            // accumulators
+        const TgBars ba = WIDE ? tg_bars(bars) : bw;                   // raw ring, A stages
+        const uint32_t lq = (wq * 32u) << 16;                          // this warp's TMEM lanes
+        const uint32_t t_acc = (WIDE ? tmem + L::W_ACC + wg * (2 * L::ACC_COLS) : tmem + wg * 256u + L::ACC) + lq;
+        const uint32_t t_a = (WIDE ? tmem + L::W_ASTG : tmem + wg * 256u + L::ASTG) + lq;
+        const uint32_t t_m = (WIDE ? tmem + L::W_MINS : tmem + wg * 256u + L::MINS) + lq;
+        const uint8_t *raw = smem + L::OFF_RAW + (WIDE ? 0u : wg * TG_RAW) + r * TG_RB;
+        constexpr uint32_t NRAW = WIDE ? L::PW : L::P;                 // raw stages
+        // stream-K parts of this warp's accumulators: pipeline q's at q (wide: 2 q + half)
+        auto part_of = [&](uint64_t q) -> uint64_t { return WIDE ? 2 * q + wg : q; };
         const uint32_t first_u = static_cast<uint32_t>(s0 / nb);
         const int bar_sk = 1 + wg;
         // (unit, block) of the next step to read back, advanced by one per read-back
@@ -509,7 +647,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             if (!tg_wait(&bw.acc_full[ab], (j >> 1) & 1u, abort_flag, p.status)) return false;
             tc_fence_after();
             uint32_t a[32];
-            tmem_ld32(tw + L::ACC + ab * L::ACC_COLS, a);
+            tmem_ld32(t_acc + ab * L::ACC_COLS, a);
             if (!DN) {
                 tmem_wait_ld();
 #pragma unroll
@@ -520,8 +658,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                                          fmaf(-pdm[m], __uint_as_float(a[16 * m + 8 + n]), tot[m][n]));
             } else {
                 uint32_t mn[8], mn1[8];
-                tmem_ld8(tw + L::ACC + ab * L::ACC_COLS + 32u, mn);
-                tmem_ld8(tw + L::ACC + ab * L::ACC_COLS + 40u, mn1);
+                tmem_ld8(t_acc + ab * L::ACC_COLS + 32u, mn);
+                tmem_ld8(t_acc + ab * L::ACC_COLS + 40u, mn1);
                 tmem_wait_ld();
 #pragma unroll
                 for (uint32_t n = 0; n < TG_NT; ++n) {
@@ -542,7 +680,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             }
             if (b != nb - 1 && j != my - 1) return true;
             // ---- the unit's epilogue --------------------------------------------
-            const TgUnit g = tg_unit(s_tile, E, row_tiles, u, p.counts, p.offsets);
+            const TgUnit g = WIDE ? tg_unit_wide(s_tile, s_pair, E, row_tiles, u, wg, p.counts, p.offsets)
+                                  : tg_unit(s_tile, E, row_tiles, u, p.counts, p.offsets);
             const uint64_t us = static_cast<uint64_t>(u) * nb;
             const bool whole = (s0 <= us) && (us + nb <= s1);
             float val[NMAT][TG_NT];
@@ -553,6 +692,9 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                     val[m][n] = tot[m][n];
                     tot[m][n] = 0.0f;
                 }
+            // wide: the missing second tile of a pair (every pipeline holding the
+            // unit skips it alike: no parts, no counter, no output)
+            if (WIDE && g.ntok == 0) return true;
             if (!whole) {
                 // the pipelines holding the unit's steps, in order (pipelines with
                 // empty ranges are skipped): pf, then the holder of the next step
@@ -571,7 +713,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                     }
                 }
                 const uint32_t slot = (u == first_u) ? 0u : 1u;
-                float *mine = p.partial + (pipe * 2 + slot) * (NMAT * TG_NT * TG_ROWS);
+                float *mine = p.partial + (part_of(pipe) * 2 + slot) * (NMAT * TG_NT * TG_ROWS);
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -580,9 +722,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 __threadfence();
                 named_bar_sync(bar_sk, 128);
                 if (wq == 1 && lane == 0) {
-                    const uint32_t old = atomicAdd(p.unit_cnt + u, 1u);
+                    const uint32_t ci = WIDE ? 2 * u + wg : u;
+                    const uint32_t old = atomicAdd(p.unit_cnt + ci, 1u);
                     const uint32_t last = old == nparts - 1 ? 1u : 0u;
-                    if (last) p.unit_cnt[u] = 0; // every part has arrived: ready for the next call
+                    if (last) p.unit_cnt[ci] = 0; // every part has arrived: ready for the next call
                     misc[3 + wg] = last;
                 }
                 named_bar_sync(bar_sk, 128);
@@ -599,7 +742,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 for (uint32_t q = pf, i = 0; i < nparts;
                      ++i, q = dense ? q + 1 : tg_pipe_of(tg_start(q + 1ull, W, NP), W, NP)) {
                     const uint32_t qslot = i == 0 ? slot_pf : 0u;
-                    const float *src = p.partial + (static_cast<uint64_t>(q) * 2 + qslot) * (NMAT * TG_NT * TG_ROWS);
+                    const float *src = p.partial + (part_of(q) * 2 + qslot) * (NMAT * TG_NT * TG_ROWS);
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -666,8 +809,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 if (my > 0) (void)readback(j - 1);
                 break;
             }
-            const uint32_t rs = j % L::P;
-            if (!tg_wait(&bw.raw_full[rs], (j / L::P) & 1u, abort_flag, p.status)) break;
+            const uint32_t rs = j % NRAW;
+            if (!tg_wait(&ba.raw_full[rs], (j / NRAW) & 1u, abort_flag, p.status)) break;
             const uint8_t *rows[2];
             TgHdr hd[2];
 #pragma unroll
@@ -675,24 +818,40 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 rows[m] = raw + rs * L::STAGE + m * TG_BOX;
                 hd[m] = tg_hdr(*reinterpret_cast<const uint4 *>(rows[m]));
             }
-            // mins A of this step (its buffer was last read by step j - 2's MMAs,
-            // whose accumulators have been read back)
+            if (!WIDE) {
+                // mins A of this step (its buffer was last read by step j - 2's MMAs,
+                // whose accumulators have been read back)
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                uint32_t mv[8];
-                tg_mins_a(hd[m], mv);
-                tmem_st8(tw + L::MINS + (j & 1u) * (NMAT * 8u) + m * 8u, mv);
+                for (int m = 0; m < NMAT; ++m) {
+                    uint32_t mv[8];
+                    tg_mins_a(hd[m], mv);
+                    tmem_st8(t_m + (j & 1u) * (NMAT * 8u) + m * 8u, mv);
+                }
             }
             bool ok = true;
 #pragma unroll
             for (uint32_t c = 0; c < 4; ++c) {
-                const uint32_t cc = 4 * j + c, as = cc & 1u;
-                if (!tg_wait(&bw.a_free[as], ((cc >> 1) & 1u) ^ 1u, abort_flag, p.status)) {
+                if (WIDE && (c >> 1) != wg) continue; // the other half's chunk
+                // A stage (as the issuers): wide, this half's own pair of stages
+                const uint32_t cc = 4 * j + c, as = WIDE ? (c & 1u) : (cc & 1u);
+                const uint32_t aph = WIDE ? (j & 1u) : ((cc >> 1) & 1u);
+                const TgBars &bh = WIDE ? bw : ba;
+                if (!tg_wait(&bh.a_free[as], aph ^ 1u, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t astg = tw + L::ASTG + as * (NMAT * 32u);
+                if (WIDE && c == 0) {
+                    // mins A of this step: its buffer was last read by step j - 2's mins
+                    // MMAs, issued before chunk 0 of step j - 1, whose stage this wait freed
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        uint32_t mv[8];
+                        tg_mins_a(hd[m], mv);
+                        tmem_st8(t_m + (j & 1u) * (NMAT * 8u) + m * 8u, mv);
+                    }
+                }
+                const uint32_t astg = t_a + (WIDE ? 2 * wg + as : as) * (NMAT * 32u);
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m) {
                     uint32_t v[32];
@@ -705,11 +864,11 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bw.a_full[as]);
+                if (lane == 0) mbar_arrive(&bh.a_full[as]);
             }
             if (!ok) break;
             __syncwarp(); // every lane has read the raw stage
-            if (lane == 0) mbar_arrive(&bw.raw_free[rs]);
+            if (lane == 0) mbar_arrive(&ba.raw_free[rs]);
             if (j > 0 && !readback(j - 1)) break;
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) {

@@ -32,6 +32,8 @@ struct TgStage {
 // pairs_max = routed pairs of one call, at most
 TgSections tg_sections(uint32_t pairs_max, uint32_t experts, uint32_t d, uint32_t ffn);
 bool tg_shape(uint32_t d, uint32_t ffn);
+// Whether the GEMVs take the wide mode (two token tiles per weight conversion).
+bool tg_wide(uint32_t pairs_max, uint32_t experts);
 // Q4_K gate/up/down, bf16 activations, d and ffn multiples of 256, <= 1024 experts.
 bool tg_eligible(const fmcuda_moe_args *a);
 // B images, gate/up + SwiGLU, down; `mark(ctx, i)` records stage event i (3 after

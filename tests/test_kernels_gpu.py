@@ -292,6 +292,31 @@ def test_moe_block_vs_oracle(cuda, oracle, t, T, xdt):
 
 
 @pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
+def test_moe_block_non_finite_logit_token(cuda, oracle, t):
+    """A token whose router logits hold a NaN gets no experts: INTERNAL_ERROR in
+    the status word, its ids absent, its output row exactly zero (the combine
+    of no terms), and every other token as the oracle computes it alone.  With
+    bf16 activations and Q4_K this runs the fused router + grouping + image
+    launch of the tcgen05 stage."""
+    rng = np.random.default_rng(900 + t)
+    E, k, d, ffn, T = 8, 2, 512, 768, 6
+    slots = make_experts(oracle, rng, E, d, ffn, t)
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    logits[2, 5] = np.nan
+    y, ids, _ = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                               gate_type=t, return_routing=True)
+    assert cuda.device_status(clear=True) == 28  # INTERNAL_ERROR
+    y = y.cpu().numpy()
+    assert np.all(ids.cpu().numpy().astype(np.uint32)[2] == 0xFFFFFFFF)
+    assert np.all(bits(y[2]) == 0)
+    valid = [0, 1, 3, 4, 5]
+    rc, ids_o, w_o, _ = oracle.route(logits[valid], k)
+    y_o = oracle.moe_block(x[valid], ids_o, w_o, slots, d, ffn, t)
+    assert rel_err(y[valid], y_o) < TOL
+
+
+@pytest.mark.parametrize("t", [TYPE_Q8_0, TYPE_Q4_K])
 def test_moe_block_skewed_routing(cuda, oracle, t):
     # one expert takes every token (5 token tiles of the same rows), two take
     # none, the rest share the second choices
@@ -310,6 +335,37 @@ def test_moe_block_skewed_routing(cuda, oracle, t):
     assert cuda.device_status() == 0
     assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
     assert rel_err(y.cpu().numpy(), y_o) < TOL
+
+
+@pytest.mark.parametrize("T", [64, 100])
+def test_moe_block_tile_pairs(cuda, oracle, T):
+    """At 16 or more routed pairs per expert the tcgen05 GEMVs convert each weight
+    block once for two 8-token tiles: one expert with many tiles (an odd count
+    among them), experts with a single tile (a pair without its second tile),
+    an expert with none; checked norm-wise and element-wise."""
+    rng = np.random.default_rng(1500 + T)
+    E, k, d, ffn = 8, 2, 512, 768
+    slots = make_experts(oracle, rng, E, d, ffn, TYPE_Q4_K)
+    x = bf16_round(rng.normal(0, 1, size=(T, d)).astype(np.float32))
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    logits[:, 2] += 3.0
+    logits[:, 5] -= 9.0
+    logits[:, 6] -= 1.5
+    rc, ids_o, w_o, _ = oracle.route(logits, k)
+    counts = np.bincount(ids_o.ravel(), minlength=E)
+    assert counts[5] == 0 and ((counts + 7) // 8 % 2 == 1).any()
+    y_o = oracle.moe_block(x, ids_o, w_o, slots, d, ffn, TYPE_Q4_K)
+    y, ids, w = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                               gate_type=TYPE_Q4_K, return_routing=True)
+    assert cuda.device_status() == 0
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_o)
+    got = y.cpu().numpy()
+    assert rel_err(got, y_o) < TOL
+    big = np.abs(y_o) > 1e-2 * np.abs(y_o).max()
+    assert float((np.abs(got - y_o)[big] / np.abs(y_o[big])).max()) < TOL
+    y2 = cuda.moe_block(dev(x, torch.bfloat16), dev(logits), [dev(s) for s in slots], top_k=k, ffn=ffn,
+                        gate_type=TYPE_Q4_K)
+    assert torch.equal(y2.cpu(), y.cpu())  # the stream-K counters were left at zero
 
 
 @pytest.mark.parametrize("T", [3, 20])
