@@ -135,12 +135,20 @@ template <int MODE> struct TgLayout {
     static_assert(MINS + 2 * NMAT * 8 <= 256, "TMEM columns of one pipeline");
     // wide mode (one step stream per CTA, two token tiles per step): half h
     // converts chunks 2h, 2h + 1 into its own two A stages (each stage then takes
-    // one chunk per step, so every wait sees every phase); mins shared, one
-    // accumulator pair per half; raw ring of both pipelines' space
+    // one chunk per step, so every wait sees every phase); mins shared; one
+    // N = 32 MMA covers both tiles (B rows 0-15 tile 0, 16-31 tile 1), so the
+    // accumulators hold per matrix (row tile) 32 columns, tile h's at 16 h
+    // (gate/up: codes 0-7, mins 8-15; down: hi 0-7, lo 8-15, then the mins
+    // accumulator at 64: tile h's row-tile-0 mins at 16 h, row tile 1's at 16 h + 8);
+    // x stages of 20 KB (chunk c of tile h at 4096 c + 2048 h, sums of tile h at
+    // 16384 + 2048 h); raw ring of both pipelines' space
     static constexpr uint32_t W_ASTG = 0;                  // [half][2 stages][NMAT * 32]
     static constexpr uint32_t W_MINS = 4 * NMAT * 32;
-    static constexpr uint32_t W_ACC = W_MINS + 2 * NMAT * 8;
-    static_assert(W_ACC + 2 * 2 * ACC_COLS <= 512, "TMEM columns of a wide CTA");
+    static constexpr uint32_t W_ACC_COLS = MODE == TG_GATE_UP ? 64 : 96;
+    static constexpr uint32_t W_ACC = W_MINS + 2 * NMAT * 8;  // [2 buffers][W_ACC_COLS]
+    static_assert(W_ACC + 2 * W_ACC_COLS <= 512, "TMEM columns of a wide CTA");
+    static constexpr uint32_t W_XIMG = 2 * TG_IMG;         // one wide x stage
+    static_assert(TG_XS * W_XIMG <= OFF_RAW, "wide x stages");
     static constexpr uint32_t PW = 2 * TG_RAW / STAGE;
     static_assert(P == 2 && P * STAGE == TG_RAW, "raw ring");
     static_assert(1024 + OFF_TILES + 8 * (TG_MAX_EXPERTS + 1) <= 227u * 1024u, "shared memory per CTA");
@@ -384,17 +392,17 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 mbar_init(&b.x_full[q], 1);
                 mbar_init(&b.x_free[q], 2); // both issuers
             }
-            // wide: the raw ring and the A stages of block 0 serve both halves
+            // wide: the raw ring, x stages and accumulators of block 0 serve both
+            // halves; block h's two A stages are half h's
             for (uint32_t q = 0; q < 4; ++q) {
                 mbar_init(&b.raw_full[q], 1);
                 mbar_init(&b.raw_free[q], WIDE ? 8 : 4); // the converter warps reading the stage
             }
             for (uint32_t q = 0; q < 2; ++q) {
                 mbar_init(&b.a_full[q], 4);                // the warps converting the chunk
-                mbar_init(&b.a_free[q], WIDE ? 4 : 2);     // every issuer reads every chunk
-                // (wide: block h's two A stages are half h's)
+                mbar_init(&b.a_free[q], 2);                // both issuers read every chunk
                 mbar_init(&b.acc_full[q], 2);
-                mbar_init(&b.acc_free[q], 4);
+                mbar_init(&b.acc_free[q], WIDE ? 8 : 4);   // the warps reading the accumulators back
                 mbar_init(&b.drain[q], 1);
             }
         }
@@ -423,14 +431,13 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         // ---- wide producer: one step stream, both halves' images, one raw box set
         if (lane == 0) {
             const uint64_t s0 = tg_start(blockIdx.x, W, NP), s1 = tg_start(blockIdx.x + 1ull, W, NP);
-            const TgBars b0 = tg_bars(bars), b1 = tg_bars(bars + L::BARS_WG);
+            const TgBars b0 = tg_bars(bars);
             uint32_t j = 0, cur_u = 0xFFFFFFFFu;
             TgUnit g0{}, g1{};
             long long last_progress = clock64();
             while (s0 + j < s1 && !*abort_flag) {
                 const uint32_t xs = j % TG_XS, rs = j % L::PW;
                 if (!mbar_test_wait(&b0.x_free[xs], ((j / TG_XS) & 1u) ^ 1u) ||
-                    !mbar_test_wait(&b1.x_free[xs], ((j / TG_XS) & 1u) ^ 1u) ||
                     !mbar_test_wait(&b0.raw_free[rs], ((j / L::PW) & 1u) ^ 1u)) {
                     __nanosleep(64);
                     if (clock64() - last_progress > (1ll << 31)) {
@@ -450,13 +457,15 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                         for (int m = 0; m < (DN ? 1 : NMAT); ++m) tma_fence_acquire(p.maps + 3 * g0.e + p.map0 + m);
                     cur_u = u;
                 }
+                // both tiles' images interleaved chunk by chunk (one N = 32 B operand)
+                uint8_t *xdst = smem + xs * L::W_XIMG;
+                mbar_expect_tx(&b0.x_full[xs], L::W_XIMG);
 #pragma unroll
                 for (uint32_t w = 0; w < 2; ++w) {
-                    const TgBars &bw = w ? b1 : b0;
-                    const uint32_t tile = w ? g1.tile : g0.tile;
-                    mbar_expect_tx(&bw.x_full[xs], TG_IMG);
-                    bulk_g2s(smem + (w * TG_XS + xs) * TG_IMG, p.img + (static_cast<uint64_t>(tile) * nb + b) * TG_IMG,
-                             TG_IMG, &bw.x_full[xs]);
+                    const uint8_t *src = p.img + (static_cast<uint64_t>(w ? g1.tile : g0.tile) * nb + b) * TG_IMG;
+#pragma unroll
+                    for (uint32_t c = 0; c < 5; ++c)
+                        bulk_g2s(xdst + c * 4096u + w * 2048u, src + c * 2048u, 2048u, &b0.x_full[xs]);
                 }
                 uint8_t *rdst = smem + L::OFF_RAW + rs * L::STAGE;
                 mbar_expect_tx(&b0.raw_full[rs], L::STAGE);
@@ -469,10 +478,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 last_progress = clock64();
             }
             // copies still in flight must land before the CTA's shared memory goes away
-            for (uint32_t q = j > TG_XS ? j - TG_XS : 0; q < j; ++q) {
+            for (uint32_t q = j > TG_XS ? j - TG_XS : 0; q < j; ++q)
                 (void)mbar_wait(&b0.x_full[q % TG_XS], (q / TG_XS) & 1u);
-                (void)mbar_wait(&b1.x_full[q % TG_XS], (q / TG_XS) & 1u);
-            }
             for (uint32_t q = j > L::PW ? j - L::PW : 0; q < j; ++q)
                 (void)mbar_wait(&b0.raw_full[q % L::PW], (q / L::PW) & 1u);
         }
@@ -545,14 +552,17 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
     } else if (warp < TG_CONV0) {
         // ---- MMA issuers: warp 1 + 2w + i = issuer i of pipeline w --------------
         // (wide: warp 1 + 2w + i = issuer i of half w, both halves on the shared A)
-        const uint32_t wg = (warp - 1) >> 1, iss = (warp - 1) & 1u;
-        if (lane == 0) {
+        // (wide: warps 1 + i, one per matrix or row tile, N = 32 over both tiles)
+        const uint32_t wg = WIDE ? 0u : (warp - 1) >> 1, iss = WIDE ? warp - 1 : (warp - 1) & 1u;
+        if (lane == 0 && (!WIDE || warp < 3)) {
             const uint64_t pipe = WIDE ? blockIdx.x : 2ull * blockIdx.x + wg;
             const uint64_t s0 = tg_start(pipe, W, NP), s1 = tg_start(pipe + 1, W, NP);
             const TgBars bw = tg_bars(bars + wg * L::BARS_WG);       // x images, accumulators
-            const TgBars ba = WIDE ? tg_bars(bars) : bw;              // A stages
-            const uint32_t idesc = idesc_f16_m128(16);
-            const uint32_t t_acc = WIDE ? tmem + L::W_ACC + wg * (2 * L::ACC_COLS) : tmem + wg * 256u + L::ACC;
+            const TgBars ba = bw;                                      // A stages (narrow)
+            const uint32_t idesc = idesc_f16_m128(WIDE ? 32 : 16);
+            constexpr uint32_t ACW = WIDE ? L::W_ACC_COLS : L::ACC_COLS;  // one accumulator buffer
+            constexpr uint32_t MW = WIDE ? 32u : 16u;                     // columns per matrix / row tile
+            const uint32_t t_acc = WIDE ? tmem + L::W_ACC : tmem + wg * 256u + L::ACC;
             const uint32_t t_a = WIDE ? tmem + L::W_ASTG : tmem + wg * 256u + L::ASTG;
             const uint32_t t_m = WIDE ? tmem + L::W_MINS : tmem + wg * 256u + L::MINS;
             uint32_t j = 0;
@@ -562,8 +572,9 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                 if (!tg_wait(&bw.x_full[st], (j / TG_XS) & 1u, abort_flag, p.status)) break;
                 if (!tg_wait(&bw.acc_free[ab], ((j >> 1) & 1u) ^ 1u, abort_flag, p.status)) break;
                 tc_fence_after();
-                const uint64_t bd0 = smem_desc_sw128(smem_u32(smem + (wg * TG_XS + st) * TG_IMG));
-                const uint32_t acc = t_acc + ab * L::ACC_COLS + iss * 16u; // matrix / row tile iss
+                const uint32_t xbase = smem_u32(smem + (WIDE ? st * L::W_XIMG : (wg * TG_XS + st) * TG_IMG));
+                const uint64_t bd0 = smem_desc_sw128(xbase);
+                const uint32_t acc = t_acc + ab * ACW + iss * MW; // matrix / row tile iss
                 bool ok = true;
 #pragma unroll
                 for (uint32_t c = 0; c < 4; ++c) {
@@ -578,12 +589,13 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                     }
                     tc_fence_after();
                     const uint32_t astg = t_a + (WIDE ? 2 * (c >> 1) + as : as) * (NMAT * 32u) + iss * 32u;
+                    constexpr uint32_t CHUNK_B = WIDE ? 4096u : 2048u; // bytes of one chunk's B rows
 #pragma unroll
                     for (uint32_t kk = 0; kk < 4; ++kk)
-                        mma_f16_ts(acc, astg + kk * 8u, bd0 + ((c * 2048u + kk * 32u) >> 4), idesc, (c | kk) != 0u);
+                        mma_f16_ts(acc, astg + kk * 8u, bd0 + ((c * CHUNK_B + kk * 32u) >> 4), idesc, (c | kk) != 0u);
                     if (c == 0) {
                         // the block's mins (their A was stored before chunk 0's arrival)
-                        const uint64_t bm = bd0 + (TG_MINS_OFF >> 4);
+                        const uint64_t bm = bd0 + ((4 * CHUNK_B) >> 4);
                         const uint32_t ma = t_m + ab * (NMAT * 8u);
                         if (!DN) {
                             mma_f16_ts(acc, ma + iss * 8u, bm, idesc, 1u);
@@ -591,7 +603,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                             // both row tiles into one accumulator, in order: tile 0 from
                             // K 0-15 of the sums image (columns 0-7), tile 1 from K 16-31
                             // (columns 8-15)
-                            const uint32_t am = t_acc + ab * L::ACC_COLS + 32u;
+                            const uint32_t am = t_acc + ab * ACW + 2 * MW;
                             mma_f16_ts(am, ma, bm, idesc, 0u);
                             mma_f16_ts(am, ma + 8u, bm + (32u >> 4), idesc, 1u);
                         }
@@ -618,10 +630,11 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         const uint64_t pipe = WIDE ? blockIdx.x : 2ull * blockIdx.x + wg; // stream-K range
         const uint64_t s0 = tg_start(pipe, W, NP), s1 = tg_start(pipe + 1, W, NP);
         const uint32_t my = static_cast<uint32_t>(s1 - s0);
-        const TgBars bw = tg_bars(bars + wg * L::BARS_WG);            // accumulators
-        const TgBars ba = WIDE ? tg_bars(bars) : bw;                   // raw ring, A stages
+        const TgBars bw = tg_bars(bars + wg * L::BARS_WG);            // A stages (wide: this half's)
+        const TgBars ba = WIDE ? tg_bars(bars) : bw;                   // raw ring, accumulators
         const uint32_t lq = (wq * 32u) << 16;                          // this warp's TMEM lanes
-        const uint32_t t_acc = (WIDE ? tmem + L::W_ACC + wg * (2 * L::ACC_COLS) : tmem + wg * 256u + L::ACC) + lq;
+        const uint32_t t_acc = (WIDE ? tmem + L::W_ACC : tmem + wg * 256u + L::ACC) + lq;
+        constexpr uint32_t ACW = WIDE ? L::W_ACC_COLS : L::ACC_COLS;  // one accumulator buffer
         const uint32_t t_a = (WIDE ? tmem + L::W_ASTG : tmem + wg * 256u + L::ASTG) + lq;
         const uint32_t t_m = (WIDE ? tmem + L::W_MINS : tmem + wg * 256u + L::MINS) + lq;
         const uint8_t *raw = smem + L::OFF_RAW + (WIDE ? 0u : wg * TG_RAW) + r * TG_RB;
@@ -644,10 +657,22 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
         // epilogue when j is the unit's last step in this pipeline.
         auto readback = [&](uint32_t j) -> bool {
             const uint32_t ab = j & 1u;
-            if (!tg_wait(&bw.acc_full[ab], (j >> 1) & 1u, abort_flag, p.status)) return false;
+            if (!tg_wait(&ba.acc_full[ab], (j >> 1) & 1u, abort_flag, p.status)) return false;
             tc_fence_after();
             uint32_t a[32];
-            tmem_ld32(t_acc + ab * L::ACC_COLS, a);
+            if (WIDE) {
+                // this tile's 16 columns of each matrix (row tile)
+                uint32_t a0[16], a1[16];
+                tmem_ld16(t_acc + ab * ACW + wg * 16u, a0);
+                tmem_ld16(t_acc + ab * ACW + 32u + wg * 16u, a1);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    a[i] = a0[i];
+                    a[16 + i] = a1[i];
+                }
+            } else {
+                tmem_ld32(t_acc + ab * ACW, a);
+            }
             if (!DN) {
                 tmem_wait_ld();
 #pragma unroll
@@ -658,8 +683,9 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
                                          fmaf(-pdm[m], __uint_as_float(a[16 * m + 8 + n]), tot[m][n]));
             } else {
                 uint32_t mn[8], mn1[8];
-                tmem_ld8(t_acc + ab * L::ACC_COLS + 32u, mn);
-                tmem_ld8(t_acc + ab * L::ACC_COLS + 40u, mn1);
+                const uint32_t mcol = WIDE ? 64u + wg * 16u : 32u;
+                tmem_ld8(t_acc + ab * ACW + mcol, mn);
+                tmem_ld8(t_acc + ab * ACW + mcol + 8u, mn1);
                 tmem_wait_ld();
 #pragma unroll
                 for (uint32_t n = 0; n < TG_NT; ++n) {
@@ -671,7 +697,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tgemv_kernel(const TgParams p) 
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bw.acc_free[ab]);
+            if (lane == 0) mbar_arrive(&ba.acc_free[ab]);
 
             const uint32_t u = rb_u, b = rb_b;
             if (++rb_b == nb) {
